@@ -1,0 +1,150 @@
+"""ctypes binding of ``libavey_b200.so`` (C ABI: ``include/avey_b200.h``).
+
+Loading fails loudly: there is no fallback when the library is missing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / 'lib' / 'libavey_b200.so'
+
+AVEY_F32, AVEY_F16, AVEY_BF16, AVEY_F64 = 0, 1, 2, 3
+KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
+ACTIVATION_IDS = {'identity': 0, 'relu': 1, 'relu2': 2, 'silu': 3, 'gelu': 4}
+
+STATUS_NAMES = {
+    0: 'AVEY_OK', -1: 'AVEY_ERR_ARGUMENT', -2: 'AVEY_ERR_ARCH', -3: 'AVEY_ERR_UNSUPPORTED',
+    -4: 'AVEY_ERR_LAUNCH', -5: 'AVEY_ERR_DEVICE', -6: 'AVEY_ERR_CUDA',
+}
+
+# Exported symbols, mirrored from include/avey_b200.h (tests check the header).
+EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_last_error', 'avey_device_status',
+           'avey_launch_count', 'avey_abi_version')
+ABI_VERSION = 1
+
+
+class AveyFwdParams(ctypes.Structure):
+    _fields_ = [
+        ('struct_size', ctypes.c_uint32),
+        ('dtype', ctypes.c_int32),
+        ('batch', ctypes.c_int64),
+        ('context', ctypes.c_int64),
+        ('features', ctypes.c_int64),
+        ('z_tr', ctypes.c_void_p),
+        ('z_tr_batch_stride', ctypes.c_int64),
+        ('z_tr_row_stride', ctypes.c_int64),
+        ('v', ctypes.c_void_p),
+        ('v_row_stride', ctypes.c_int64),
+        ('z_tl', ctypes.c_void_p),
+        ('z_tl_batch_stride', ctypes.c_int64),
+        ('z_tl_row_stride', ctypes.c_int64),
+        ('bias', ctypes.c_void_p),
+        ('valid', ctypes.c_void_p),
+        ('valid_batch_stride', ctypes.c_int64),
+        ('valid_row_stride', ctypes.c_int64),
+        ('out', ctypes.c_void_p),
+        ('out_batch_stride', ctypes.c_int64),
+        ('out_row_stride', ctypes.c_int64),
+        ('eps', ctypes.c_double),
+        ('norm_eps', ctypes.c_double),
+        ('causal', ctypes.c_int32),
+        ('normalize', ctypes.c_int32),
+        ('activation', ctypes.c_int32),
+        ('kernel', ctypes.c_int32),
+    ]
+
+
+class AveyPlan(ctypes.Structure):
+    _fields_ = [
+        ('kernel', ctypes.c_int32),
+        ('launches', ctypes.c_int32),
+        ('grid', ctypes.c_int32),
+        ('block', ctypes.c_int32),
+        ('smem_bytes', ctypes.c_int32),
+        ('reason', ctypes.c_int32),
+    ]
+
+
+class NativeError(RuntimeError):
+    """A non-OK AveyStatus from the library."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f'{STATUS_NAMES.get(status, status)}: {message}')
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def library_path() -> Path:
+    override = os.environ.get('AVEY_B200_LIB')
+    return Path(override) if override else LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if not path.exists():
+            raise RuntimeError(
+                f'avey_kernel_b200: CUDA library not found at {path}. Build it with '
+                '`python -m avey_kernel_b200.csrc.build` (there is no CPU fallback).')
+        dll = ctypes.CDLL(str(path))
+        dll.avey_fwd_v1.argtypes = [ctypes.POINTER(AveyFwdParams), ctypes.c_void_p]
+        dll.avey_fwd_v1.restype = ctypes.c_int
+        dll.avey_fwd_plan.argtypes = [ctypes.POINTER(AveyFwdParams), ctypes.POINTER(AveyPlan)]
+        dll.avey_fwd_plan.restype = ctypes.c_int
+        dll.avey_last_error.argtypes = []
+        dll.avey_last_error.restype = ctypes.c_char_p
+        dll.avey_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
+        dll.avey_device_status.restype = ctypes.c_int
+        dll.avey_launch_count.argtypes = []
+        dll.avey_launch_count.restype = ctypes.c_uint64
+        dll.avey_abi_version.argtypes = []
+        dll.avey_abi_version.restype = ctypes.c_int
+        if dll.avey_abi_version() != ABI_VERSION:
+            raise RuntimeError(f'{path}: ABI version {dll.avey_abi_version()} != {ABI_VERSION}')
+        _lib = dll
+        return _lib
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = lib().avey_last_error().decode(errors='replace')
+        raise NativeError(status, msg)
+
+
+def forward(params: AveyFwdParams, stream: int) -> None:
+    _check(lib().avey_fwd_v1(ctypes.byref(params), ctypes.c_void_p(stream)))
+
+
+def plan(params: AveyFwdParams) -> AveyPlan:
+    out = AveyPlan()
+    _check(lib().avey_fwd_plan(ctypes.byref(params), ctypes.byref(out)))
+    return out
+
+
+def device_status(clear: bool = False) -> int:
+    flags = ctypes.c_uint32(0)
+    _check(lib().avey_device_status(ctypes.byref(flags), int(clear)))
+    return flags.value
+
+
+def launch_count() -> int:
+    return int(lib().avey_launch_count())
+
+
+def new_params() -> AveyFwdParams:
+    p = AveyFwdParams()
+    p.struct_size = ctypes.sizeof(AveyFwdParams)
+    return p

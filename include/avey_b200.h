@@ -1,0 +1,148 @@
+/*
+ * avey_b200.h -- C ABI of the B200 (sm_100a) contextualizer forward library.
+ *
+ * One call computes, for every batch row b,
+ *
+ *   out[b] = z_tl[b] * act( (S_b (.) V (.) M_b) z_tr[b] / den_b + bias )
+ *
+ * with S_b the cosine similarity of the rows of z_tr[b], M_b the causal and
+ * padding mask and den_b the signed row sum (Avey-B) or 1 (Avey): the math of
+ * the reference's avey_kernels/ops.py:66-96 (_reference).
+ *
+ * The library is plain C at this boundary: raw device pointers, element
+ * strides and sizes, no framework types. It never throws; every entry point
+ * returns an AveyStatus and avey_last_error() describes the last failure on
+ * the calling thread. Calls only enqueue work on the given stream: they do not
+ * synchronise and do not allocate, so they can be captured in a CUDA graph.
+ */
+#ifndef AVEY_B200_H
+#define AVEY_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AVEY_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define AVEY_API __attribute__((visibility("default")))
+#else
+#define AVEY_API
+#endif
+
+/* Element types of z_tr, v, z_tl, bias and out (all share one type). */
+typedef enum AveyDtype {
+  AVEY_F32 = 0,
+  AVEY_F16 = 1,
+  AVEY_BF16 = 2,
+  AVEY_F64 = 3,
+} AveyDtype;
+
+/* Activation ids; the numbering is that of the reference, _triton.py:169. */
+typedef enum AveyActivation {
+  AVEY_ACT_IDENTITY = 0,
+  AVEY_ACT_RELU = 1,
+  AVEY_ACT_RELU2 = 2,
+  AVEY_ACT_SILU = 3,
+  AVEY_ACT_GELU = 4, /* tanh approximation */
+} AveyActivation;
+
+/* Kernel selection. AUTO picks the tcgen05 kernel whenever the shape, dtype
+ * and alignment allow it, else the general CUDA-core kernel. */
+typedef enum AveyKernel {
+  AVEY_KERNEL_AUTO = 0,
+  AVEY_KERNEL_SIMT = 1,   /* general CUDA-core kernel: any dtype/stride/shape */
+  AVEY_KERNEL_TCGEN05 = 2 /* fused TMA + tcgen05 + TMEM kernel (bf16 / f16) */
+} AveyKernel;
+
+typedef enum AveyStatus {
+  AVEY_OK = 0,
+  AVEY_ERR_ARGUMENT = -1,    /* bad size, pointer, stride, flag or struct */
+  AVEY_ERR_ARCH = -2,        /* current device is not sm_100 */
+  AVEY_ERR_UNSUPPORTED = -3, /* a forced kernel cannot run these inputs */
+  AVEY_ERR_LAUNCH = -4,      /* the CUDA launch itself failed */
+  AVEY_ERR_DEVICE = -5,      /* a kernel reported a timeout or fault flag */
+  AVEY_ERR_CUDA = -6,        /* another CUDA runtime / driver call failed */
+} AveyStatus;
+
+/*
+ * Forward parameters. Strides are in ELEMENTS. The feature (last) dimension
+ * of z_tr, z_tl and out must have stride 1; the other strides are free, so the
+ * head and tail halves of one [B, C, 2d'] tensor are passed as two views
+ * (row stride 2d') without a copy. Optional tensors are NULL when absent.
+ * valid holds one byte per (batch, position): nonzero = valid.
+ */
+typedef struct AveyFwdParams {
+  uint32_t struct_size; /* sizeof(AveyFwdParams); guards ABI drift */
+  int32_t dtype;        /* AveyDtype */
+  int64_t batch;        /* B  >= 1 */
+  int64_t context;      /* C  >= 1 (tokens per batch row) */
+  int64_t features;     /* d' >= 1 */
+
+  const void* z_tr;     /* [B, C, d'] tail half (required) */
+  int64_t z_tr_batch_stride, z_tr_row_stride;
+  const void* v;        /* [C, C] indexed [query, key] (Avey) or NULL */
+  int64_t v_row_stride;
+  const void* z_tl;     /* [B, C, d'] head half, the gate, or NULL */
+  int64_t z_tl_batch_stride, z_tl_row_stride;
+  const void* bias;     /* [d'] contiguous, or NULL */
+  const uint8_t* valid; /* [B, C] bytes, or NULL */
+  int64_t valid_batch_stride, valid_row_stride;
+  void* out;            /* [B, C, d'] output, same dtype as z_tr */
+  int64_t out_batch_stride, out_row_stride;
+
+  double eps;      /* Avey-B denominator epsilon (used when normalize != 0) */
+  double norm_eps; /* L2-normalisation epsilon: x / max(||x||, norm_eps) */
+  int32_t causal;     /* keep key j <= query i (diagonal kept) */
+  int32_t normalize;  /* divide by the signed row sum + eps (Avey-B) */
+  int32_t activation; /* AveyActivation */
+  int32_t kernel;     /* AveyKernel */
+} AveyFwdParams;
+
+/* What avey_fwd_v1 would launch for these parameters. */
+typedef struct AveyPlan {
+  int32_t kernel;        /* AVEY_KERNEL_SIMT or AVEY_KERNEL_TCGEN05 */
+  int32_t launches;      /* kernel launches per call */
+  int32_t grid;          /* CTAs of the main launch */
+  int32_t block;         /* threads per CTA of the main launch */
+  int32_t smem_bytes;    /* dynamic shared memory per CTA */
+  int32_t reason;        /* 0, or why the tcgen05 kernel was not chosen */
+} AveyPlan;
+
+/*
+ * Run the contextualizer forward on `stream` (a cudaStream_t; NULL is the
+ * legacy default stream). Replaces, in the reference, the normalisation
+ * pre-pass plus the fused mixing launch: avey_kernels/ops.py:112-119
+ * (F.normalize into a temporary fp32 buffer, then mix) and
+ * avey_kernels/_triton.py:153-188 (the avey_kernels::mix custom op that
+ * launches _mix_kernel). Normalisation is fused into the kernel here.
+ * Returns AVEY_OK or a negative AveyStatus.
+ */
+AVEY_API int avey_fwd_v1(const AveyFwdParams* params, void* stream);
+
+/* Fill *plan with the launch avey_fwd_v1 would make; launches nothing.
+ * Has no reference counterpart (introspection for tests and benchmarks). */
+AVEY_API int avey_fwd_plan(const AveyFwdParams* params, AveyPlan* plan);
+
+/* Message for the last non-OK status returned on this thread ("" if none). */
+AVEY_API const char* avey_last_error(void);
+
+/* Device-side status word of the current device: 0, or the OR of the
+ * AVEY_DEVFLAG_* bits raised by kernels since the last clear. Synchronises
+ * the device. clear != 0 resets it. */
+#define AVEY_DEVFLAG_TIMEOUT 1u /* a bounded wait on an mbarrier gave up */
+AVEY_API int avey_device_status(uint32_t* flags, int clear);
+
+/* Number of kernels this library has launched in this process. */
+AVEY_API uint64_t avey_launch_count(void);
+
+/* AVEY_ABI_VERSION of the loaded library. */
+AVEY_API int avey_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AVEY_B200_H */

