@@ -22,9 +22,9 @@ STATUS_NAMES = {
 }
 
 # Exported symbols, mirrored from include/avey_b200.h (tests check the header).
-EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_last_error', 'avey_device_status',
-           'avey_launch_count', 'avey_abi_version')
-ABI_VERSION = 1
+EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_fwd_workspace_size', 'avey_last_error',
+           'avey_device_status', 'avey_launch_count', 'avey_abi_version')
+ABI_VERSION = 2
 
 
 class AveyFwdParams(ctypes.Structure):
@@ -55,6 +55,8 @@ class AveyFwdParams(ctypes.Structure):
         ('normalize', ctypes.c_int32),
         ('activation', ctypes.c_int32),
         ('kernel', ctypes.c_int32),
+        ('workspace', ctypes.c_void_p),
+        ('workspace_bytes', ctypes.c_uint64),
     ]
 
 
@@ -104,6 +106,9 @@ def lib() -> ctypes.CDLL:
         dll.avey_fwd_v1.restype = ctypes.c_int
         dll.avey_fwd_plan.argtypes = [ctypes.POINTER(AveyFwdParams), ctypes.POINTER(AveyPlan)]
         dll.avey_fwd_plan.restype = ctypes.c_int
+        dll.avey_fwd_workspace_size.argtypes = [ctypes.POINTER(AveyFwdParams),
+                                                ctypes.POINTER(ctypes.c_uint64)]
+        dll.avey_fwd_workspace_size.restype = ctypes.c_int
         dll.avey_last_error.argtypes = []
         dll.avey_last_error.restype = ctypes.c_char_p
         dll.avey_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
@@ -132,6 +137,12 @@ def plan(params: AveyFwdParams) -> AveyPlan:
     out = AveyPlan()
     _check(lib().avey_fwd_plan(ctypes.byref(params), ctypes.byref(out)))
     return out
+
+
+def workspace_size(params: AveyFwdParams) -> int:
+    out = ctypes.c_uint64(0)
+    _check(lib().avey_fwd_workspace_size(ctypes.byref(params), ctypes.byref(out)))
+    return int(out.value)
 
 
 def device_status(clear: bool = False) -> int:

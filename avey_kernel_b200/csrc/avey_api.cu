@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -15,6 +16,7 @@
 #include "avey_b200.h"
 #include "common.cuh"
 #include "ptx.cuh"
+#include "norm_prepass.cuh"
 #include "simt_kernel.cuh"
 #include "tc_kernel.cuh"
 
@@ -44,6 +46,7 @@ enum Reason {
   kReasonContext = 2,    // more than 512 tokens per row
   kReasonAlignment = 3,  // base / strides not 16-byte aligned (TMA, vector I/O)
   kReasonForced = 4,     // caller asked for the CUDA-core kernel
+  kReasonFeatures = 5,   // more than 2048 features (bias is staged in shared memory)
 };
 
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
@@ -102,6 +105,7 @@ int tc_reason(const AveyFwdParams* p) {
   if (p->kernel == AVEY_KERNEL_SIMT) return kReasonForced;
   if (p->dtype != AVEY_BF16 && p->dtype != AVEY_F16) return kReasonDtype;
   if (p->context > avey::kTcMaxKeys) return kReasonContext;
+  if (p->features > avey::kTcMaxFeatures) return kReasonFeatures;
   const bool a = aligned16(p->z_tr) && aligned16(p->out) && (!p->z_tl || aligned16(p->z_tl)) &&
                  (p->z_tr_row_stride % 8 == 0) && (p->out_row_stride % 8 == 0) &&
                  (p->z_tr_batch_stride % 8 == 0 || p->batch == 1) &&
@@ -117,17 +121,27 @@ struct TcLayout {
   int smem;
 };
 
+// Shared memory: [P region | phase-C ring | control block]. The phase-A
+// stages (query chunk + every key tile's chunk, 16 KB each) live in the P
+// region and the ring; phase B writes P (16 KB per 64 keys) into the P region.
 TcLayout tc_layout(const AveyFwdParams* p) {
   TcLayout l{};
   const int ctx = static_cast<int>(p->context);
   const int nk_max = (ctx + 127) / 128;
-  l.geom.p_bytes = nk_max * 2 * avey::kTcUnitBytes;
-  const int room = kMaxDynSmem - 1024 - avey::kTcCtrlBytes - l.geom.p_bytes;
+  l.geom.p_bytes = nk_max * 2 * avey::kTcPChunkBytes;
+  const int room =
+      kMaxDynSmem - 1024 - avey::kTcCtrlBytes - avey::kTcOutStageBytes - l.geom.p_bytes;
   int nslot = room / avey::kTcUnitBytes;
   if (nslot > avey::kTcMaxSlots) nslot = avey::kTcMaxSlots;
   l.geom.nslot = nslot;
+  // Phase-A stages use the P region and the phase-C ring together.
+  l.geom.a_stage_bytes = (1 + nk_max) * avey::kTcTileBytesA;
+  int nst = (l.geom.p_bytes + nslot * avey::kTcUnitBytes) / l.geom.a_stage_bytes;
+  if (nst > avey::kTcMaxStages) nst = avey::kTcMaxStages;
+  l.geom.a_nstage = nst;
   l.geom.n_qtiles = nk_max;
-  l.smem = 1024 + l.geom.p_bytes + nslot * avey::kTcUnitBytes + avey::kTcCtrlBytes;
+  l.smem = 1024 + l.geom.p_bytes + nslot * avey::kTcUnitBytes + avey::kTcOutStageBytes +
+           avey::kTcCtrlBytes;
   return l;
 }
 
@@ -162,6 +176,7 @@ avey::FwdArgs make_args(const AveyFwdParams* p) {
   a.has_zl = p->z_tl != nullptr;
   a.has_bias = p->bias != nullptr;
   a.has_valid = p->valid != nullptr;
+  a.sumsq = static_cast<float*>(p->workspace);
   return a;
 }
 
@@ -180,53 +195,93 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 3-D map over z_tr viewed as [batch][context][features] with a box of
-// `box_rows` rows x 64 features, 128-byte swizzle, zero fill out of bounds.
-int encode_zmap(const AveyFwdParams* p, int box_rows, CUtensorMap* map) {
+// `box_rows` rows x `box_cols` features (64-byte swizzle for 32 columns,
+// 128-byte swizzle for 64), zero fill out of bounds.
+int encode_map(const AveyFwdParams* p, const void* base, int64_t batch_stride, int64_t row_stride,
+               int box_cols, int box_rows, CUtensorMap* map) {
   auto fn = encode_fn();
   if (!fn) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const int es = elem_size(p->dtype);
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(p->features), static_cast<cuuint64_t>(p->context),
                         static_cast<cuuint64_t>(p->batch)};
-  int64_t bs = p->z_tr_batch_stride;
-  if (p->batch == 1) bs = p->z_tr_row_stride * p->context;  // unused; any aligned value
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(p->z_tr_row_stride * es),
+  int64_t bs = batch_stride;
+  if (p->batch == 1) bs = row_stride * p->context;  // unused; any aligned value
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * es),
                            static_cast<cuuint64_t>(((bs * es) + 15) / 16 * 16)};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  const CUtensorMapSwizzle swz =
+      box_cols * es == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt =
       p->dtype == AVEY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUresult r = fn(map, dt, 3, const_cast<void*>(p->z_tr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return AVEY_OK;
 }
 
-template <typename T>
+template <typename T, int ACT>
 int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(avey::tc_contextualize<T>,
+    attr_err = cudaFuncSetAttribute(avey::tc_contextualize<T, ACT>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   });
   if (attr_err != cudaSuccess)
     return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
-  CUtensorMap map_k, map_z;
-  int rc = encode_zmap(p, 128, &map_k);
+  CUtensorMap map_q, map_z, map_o;
+  int rc = encode_map(p, p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride, avey::kTcChunk, 128,
+                      &map_q);
   if (rc != AVEY_OK) return rc;
-  rc = encode_zmap(p, 32, &map_z);
+  rc = encode_map(p, p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride, 64, avey::kTcUnitKeys,
+                  &map_z);
+  if (rc != AVEY_OK) return rc;
+  rc = encode_map(p, p->out, p->out_batch_stride, p->out_row_stride, 32, 32, &map_o);
   if (rc != AVEY_OK) return rc;
   const TcLayout l = tc_layout(p);
   const avey::FwdArgs args = make_args(p);
-  const unsigned grid = static_cast<unsigned>(p->batch * l.geom.n_qtiles);
-  avey::tc_contextualize<T><<<grid, avey::kTcThreads, l.smem, stream>>>(args, map_k, map_z, l.geom);
-  const cudaError_t e = cudaGetLastError();
+  const uint64_t need = static_cast<uint64_t>(p->batch) * p->context * sizeof(float);
+  if (!p->workspace || p->workspace_bytes < need || (reinterpret_cast<uintptr_t>(p->workspace) & 3u))
+    return fail(AVEY_ERR_ARGUMENT, "the tcgen05 path needs a 4-byte aligned workspace of %llu bytes",
+                (unsigned long long)need);
+  // 1. Row sums of squares (the first launch lets the second start at once).
+  const int rows = static_cast<int>(p->batch * p->context);
+  const int pre_blocks = std::min(148 * 8, (rows + 7) / 8);
+  avey::norm_prepass<T><<<pre_blocks, avey::kPrepassThreads, 0, stream>>>(args);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "norm pre-pass launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  // 2. The fused kernel, as a programmatic dependent of the pre-pass: it waits
+  //    for the sums only before its P phase.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p->batch * l.geom.n_qtiles));
+  cfg.blockDim = dim3(avey::kTcThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(l.smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, avey::tc_contextualize<T, ACT>, args, map_q, map_z, map_o, l.geom);
   if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tcgen05 kernel launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return ok();
+}
+
+template <typename T>
+int launch_tc_act(const AveyFwdParams* p, cudaStream_t stream) {
+  switch (p->activation) {
+    case AVEY_ACT_RELU: return launch_tc<T, AVEY_ACT_RELU>(p, stream);
+    case AVEY_ACT_RELU2: return launch_tc<T, AVEY_ACT_RELU2>(p, stream);
+    case AVEY_ACT_SILU: return launch_tc<T, AVEY_ACT_SILU>(p, stream);
+    case AVEY_ACT_GELU: return launch_tc<T, AVEY_ACT_GELU>(p, stream);
+    default: return launch_tc<T, AVEY_ACT_IDENTITY>(p, stream);
+  }
 }
 
 template <typename T, typename A>
@@ -259,6 +314,7 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
   if (reason == kReasonNone) {
     const TcLayout l = tc_layout(p);
     plan->kernel = AVEY_KERNEL_TCGEN05;
+    plan->launches = 2;
     plan->grid = static_cast<int32_t>(p->batch * l.geom.n_qtiles);
     plan->block = avey::kTcThreads;
     plan->smem_bytes = l.smem;
@@ -272,6 +328,17 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
   return ok();
 }
 
+int avey_fwd_workspace_size(const AveyFwdParams* p, uint64_t* bytes) {
+  AveyPlan plan;
+  const int rc = avey_fwd_plan(p, &plan);
+  if (rc != AVEY_OK) return rc;
+  if (!bytes) return fail(AVEY_ERR_ARGUMENT, "bytes is NULL");
+  *bytes = plan.kernel == AVEY_KERNEL_TCGEN05
+               ? static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context) * sizeof(float)
+               : 0u;
+  return ok();
+}
+
 int avey_fwd_v1(const AveyFwdParams* p, void* stream_ptr) {
   AveyPlan plan;
   int rc = avey_fwd_plan(p, &plan);
@@ -280,8 +347,8 @@ int avey_fwd_v1(const AveyFwdParams* p, void* stream_ptr) {
   if (rc != AVEY_OK) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (plan.kernel == AVEY_KERNEL_TCGEN05) {
-    return p->dtype == AVEY_BF16 ? launch_tc<__nv_bfloat16>(p, stream)
-                                 : launch_tc<__half>(p, stream);
+    return p->dtype == AVEY_BF16 ? launch_tc_act<__nv_bfloat16>(p, stream)
+                                 : launch_tc_act<__half>(p, stream);
   }
   switch (p->dtype) {
     case AVEY_F32: return launch_simt<float, float>(p, stream);
@@ -313,5 +380,17 @@ int avey_device_status(uint32_t* flags, int clear) {
 uint64_t avey_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int avey_abi_version(void) { return AVEY_ABI_VERSION; }
+
+#ifdef AVEY_TRACE
+// Trace builds only: copy the per-CTA phase timeline (kTraceCtas x 16 u64).
+AVEY_API int avey_trace_read(unsigned long long* dst) {
+  return cudaMemcpyFromSymbol(dst, avey::g_trace, sizeof(avey::g_trace)) == cudaSuccess ? 0 : -1;
+}
+AVEY_API int avey_trace_units_read(unsigned long long* dst) {
+  return cudaMemcpyFromSymbol(dst, avey::g_trace_units, sizeof(avey::g_trace_units)) == cudaSuccess
+             ? 0
+             : -1;
+}
+#endif
 
 }  // extern "C"

@@ -19,7 +19,7 @@ ROOT = PKG.parent
 LIB_DIR = PKG / 'lib'
 LIB = LIB_DIR / 'libavey_b200.so'
 SOURCES = ['avey_api.cu']
-HEADERS = ['ptx.cuh', 'common.cuh', 'simt_kernel.cuh', 'tc_kernel.cuh']
+HEADERS = ['ptx.cuh', 'common.cuh', 'norm_prepass.cuh', 'simt_kernel.cuh', 'tc_kernel.cuh']
 
 NVCC_FLAGS = [
     '-gencode', 'arch=compute_100a,code=sm_100a',
@@ -49,11 +49,19 @@ def needs_build() -> bool:
     return any(p.stat().st_mtime > mtime for p in deps)
 
 
-def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
-    if not force and not needs_build():
+TRACE_LIB = LIB_DIR / 'libavey_b200_trace.so'
+
+
+def build(force: bool = False, verbose: bool = False, extra=(), trace: bool = False) -> Path:
+    """Build the library (or, with trace=True, the phase-timeline build that
+    records %globaltimer stamps per CTA; see ptx.cuh)."""
+    target = TRACE_LIB if trace else LIB
+    if not force and not trace and not needs_build():
         return LIB
     LIB_DIR.mkdir(exist_ok=True)
-    tmp = LIB.with_suffix('.so.tmp')
+    tmp = target.with_suffix('.so.tmp')
+    if trace:
+        extra = (*extra, '-DAVEY_TRACE')
     cmd = [nvcc_path(), *NVCC_FLAGS, *extra, '-I', str(ROOT / 'include'), '-I', str(CSRC),
            *[str(CSRC / s) for s in SOURCES], '-o', str(tmp), '-lcudart']
     if verbose:
@@ -64,8 +72,8 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
         raise RuntimeError(f'nvcc failed with exit code {res.returncode}')
     if verbose and (res.stdout or res.stderr):
         print(res.stdout + res.stderr)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, target)
+    return target
 
 
 def main():
@@ -73,10 +81,11 @@ def main():
     ap.add_argument('--force', action='store_true')
     ap.add_argument('--verbose', action='store_true')
     ap.add_argument('--ptxas-info', action='store_true', help='print registers / spills / smem')
+    ap.add_argument('--trace', action='store_true', help='build lib/libavey_b200_trace.so')
     args = ap.parse_args()
     extra = ['-Xptxas', '-v'] if args.ptxas_info else []
     print(build(force=args.force or args.ptxas_info, verbose=args.verbose or args.ptxas_info,
-                extra=extra))
+                extra=extra, trace=args.trace))
 
 
 if __name__ == '__main__':

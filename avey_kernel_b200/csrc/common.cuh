@@ -26,6 +26,7 @@ struct FwdArgs {
   double eps_d, norm_eps_d;
   int causal, normalize, act;
   int has_v, has_zl, has_bias, has_valid;
+  float* sumsq;  // workspace: per-row sums of squares of z_tr [batch][ctx] (tcgen05 path)
 };
 
 template <typename T>
@@ -43,11 +44,13 @@ struct Elem<double> {
 template <>
 struct Elem<__half> {
   __device__ static float load(const __half* p) { return __half2float(__ldg(p)); }
+  __device__ static float to_f(__half x) { return __half2float(x); }
   __device__ static __half from_f(float x) { return __float2half_rn(x); }
 };
 template <>
 struct Elem<__nv_bfloat16> {
   __device__ static float load(const __nv_bfloat16* p) { return __bfloat162float(__ldg(p)); }
+  __device__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
   __device__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
 };
 
@@ -93,6 +96,24 @@ __device__ __forceinline__ A activate(A x, int act) {
     }
     default:
       return x;
+  }
+}
+
+// Activation with the id fixed at compile time (one case per kernel instance).
+template <int ACT>
+__device__ __forceinline__ float act_fn(float x) {
+  if constexpr (ACT == 1) {
+    return x < 0.f ? 0.f : x;
+  } else if constexpr (ACT == 2) {
+    const float r = x < 0.f ? 0.f : x;
+    return r * r;
+  } else if constexpr (ACT == 3) {
+    return x * sigmoid_stable(x);
+  } else if constexpr (ACT == 4) {
+    const float t = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+    return x * sigmoid_stable(2.f * t);
+  } else {
+    return x;
   }
 }
 

@@ -11,6 +11,34 @@ namespace avey {
 // The library is a single translation unit, so the definition lives here.
 __device__ unsigned int g_devflags = 0u;
 
+// Optional phase timeline (trace builds only, -DAVEY_TRACE): per CTA, the
+// %globaltimer value (ns) at numbered points of the kernel.
+#ifdef AVEY_TRACE
+constexpr int kTraceCtas = 2048;
+constexpr int kTraceSlots = 16;
+__device__ unsigned long long g_trace[kTraceCtas][kTraceSlots];
+__device__ __forceinline__ void trace_stamp(int slot) {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  if (blockIdx.x < kTraceCtas) g_trace[blockIdx.x][slot] = t;
+}
+#define AVEY_STAMP(slot) ::avey::trace_stamp(slot)
+// Per-unit events of the first kTraceUnitCtas CTAs: [cta][unit][event].
+constexpr int kTraceUnitCtas = 4;
+constexpr int kTraceUnits = 256;
+__device__ unsigned long long g_trace_units[kTraceUnitCtas][kTraceUnits][4];
+__device__ __forceinline__ void trace_unit(int unit, int event) {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  if (blockIdx.x < kTraceUnitCtas && unit >= 0 && unit < kTraceUnits)
+    g_trace_units[blockIdx.x][unit][event] = t;
+}
+#define AVEY_STAMP_UNIT(unit, event) ::avey::trace_unit(unit, event)
+#else
+#define AVEY_STAMP(slot) ((void)0)
+#define AVEY_STAMP_UNIT(unit, event) ((void)0)
+#endif
+
 // ~2^31 SM cycles (about one second at 1.9 GHz) before a wait gives up.
 constexpr long long kWaitLimitCycles = 1ll << 31;
 
@@ -78,6 +106,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: the primary grid lets dependents start early;
+// a dependent waits for the primary grid's completion (and its memory) only
+// where it consumes its results.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -93,6 +132,34 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
+}
+
+// Bring [src, src + bytes) into L2 without a destination (16-byte aligned
+// address, size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
+               : "memory");
+}
+
+// 3-D tiled store of one box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(x), "r"(y), "r"(z), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until the issuing thread's bulk groups have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until the issuing thread's bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05
@@ -156,18 +223,40 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// tcgen05.wait::ld that also "redefines" the destination registers of the
+// preceding tmem_ld32, so the compiler cannot move their uses above the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+        "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+        "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor for tcgen05.mma (sm_100 layout): start
-// address, leading / stride byte offsets (all >> 4), version 1, 128-byte swizzle.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// address, leading / stride byte offsets (all >> 4), version 1, swizzle mode
+// (2 = 128-byte, 4 = 64-byte, 6 = 32-byte swizzle).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint32_t swizzle) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;  // descriptor version for sm_100
-  d |= 2ull << 61;  // SWIZZLE_128B
+  d |= static_cast<uint64_t>(swizzle & 7u) << 61;
   return d;
+}
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  return smem_desc(saddr, lbo_bytes, sbo_bytes, 2u);
+}
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t sbo_bytes) {
+  return smem_desc(saddr, 16u, sbo_bytes, 4u);
 }
 
 // Instruction descriptor for kind::f16 with fp32 accumulation.

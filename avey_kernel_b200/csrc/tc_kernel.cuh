@@ -1,33 +1,37 @@
 // Fused tcgen05 contextualizer kernel for bf16 / f16 inputs (sm_100a).
 //
 // One CTA owns one work item: 128 query rows (a "query tile") of one batch
-// row, and computes the whole output row block [128, d'] in three phases that
-// keep the similarity matrix on chip:
+// row, and computes the output row block [128, d'] in three phases that keep
+// the similarity matrix on chip:
 //
-//  A. Gram phase. TMA streams the query tile and every needed key tile in
-//     64-feature chunks (128 x 64 bf16 = 16 KB units, 128-byte swizzle) through
-//     a ring of shared-memory slots. The MMA warp accumulates the raw Gram
-//     block G = Z_q Z_k^T (fp32) in TMEM, one 128-column tile per key tile
-//     (up to 512 keys = all 512 TMEM columns). Meanwhile eight compute warps
-//     read each key unit from shared memory and accumulate the row sums of
-//     squares: the L2 normalisation is fused here, no normalised copy exists.
+//  A. Gram phase. TMA streams 64-feature chunks of the query tile and of every
+//     needed key tile (128-byte swizzle) into chunk stages that live in the P
+//     region and the phase-C ring (both unused until later). The MMA warp
+//     accumulates the raw Gram block G = Z_q Z_k^T (fp32) in TMEM, two key
+//     tiles per MMA (N = 256), up to 512 keys = all 512 TMEM columns. The L2
+//     normalisation is applied to G in phase B from per-row sums of squares
+//     (4 bytes per row, written by norm_prepass into the workspace, which runs
+//     concurrently through programmatic dependent launch); no normalised copy
+//     of z_tr exists anywhere.
 //  B. P phase. The compute warps read G from TMEM (thread = query row), form
 //     P = G * rinv_i * rinv_j * V[i, j] under the causal / padding masks
 //     (select, so NaN padding cannot leak), accumulate the signed row sum for
-//     Avey-B in fp32, and write P as bf16 / f16 into shared memory in the
+//     Avey-B in fp32, and write P as bf16 / f16 into the P region in the
 //     K-major 128-byte-swizzle layout the tensor core reads. P never reaches
 //     global memory.
 //  C. Mix phase. TMA streams z_tr again as 32-key x 256-feature units (MN-major
-//     B operand) and the MMA warp computes O = P Z for 256-feature slices into
-//     two TMEM buffers (256 columns each, reusing the Gram columns). The
-//     compute warps drain each slice: divide by (den + eps), add the bias,
-//     apply the activation, multiply by the gate, zero padded rows, store.
+//     B operand, 128-byte swizzle) through a ring that is filled during phase
+//     A already. The MMA warp computes O = P Z for 256-feature slices into two
+//     TMEM buffers (256 columns each, reusing the Gram columns). The compute
+//     warps drain each slice: divide by (den + eps), add the bias, apply the
+//     activation, multiply by the gate, zero padded rows, store.
 //
-// Roles: warp 0 issues TMA, warp 1 owns TMEM and issues MMAs, warps 4-11 are
-// the compute warps (two warpgroups; warpgroup h drains slices s = h mod 2).
-// Every wait is bounded (ptx.cuh): a wait that gives up raises the device
-// flag, and all later waits in the grid return at once, so the kernel always
-// terminates and frees its TMEM.
+// Roles: warp 0 issues TMA (and L2 prefetches of the item's V rows and gate
+// rows), warp 1 owns TMEM and issues MMAs, warps 4-11 are the compute warps
+// (two warpgroups; warpgroup h drains slices s = h mod 2). Every wait is
+// bounded (ptx.cuh): a wait that gives up raises the device flag, and all
+// later waits in the grid return at once, so the kernel always terminates and
+// frees its TMEM.
 //
 // Reference: the fused loop of avey_kernels/_triton.py:53-128 (S tile 83-92,
 // V 93-96, masks 97-100, row sum 101-102, S.Z 103-105, divide 106-107, bias
@@ -46,22 +50,31 @@ namespace avey {
 
 constexpr int kTcThreads = 384;
 constexpr int kTcMaxKeys = 512;      // keys per work item (TMEM holds 512 fp32 columns)
-constexpr int kTcUnitBytes = 16384;  // one ring slot
+constexpr int kTcUnitBytes = 32768;  // one phase-C ring slot (64 keys x 256 features)
+constexpr int kTcUnitKeys = 64;      // keys per phase-C unit
+constexpr int kTcPChunkBytes = 16384; // P for 64 keys x 128 rows (bf16 / f16)
+constexpr int kTcOutTileBytes = 2048; // one warp's 32 x 32 output staging tile
+constexpr int kTcOutStageBytes = 8 * kTcOutTileBytes;
+constexpr int kTcZBoxBytes = 8192;   // one {64 features x 64 keys} box of a unit
 constexpr int kTcMaxSlots = 8;
-constexpr int kTcCtrlBytes = 4096;
+constexpr int kTcMaxStages = 8;
+constexpr int kTcChunk = 64;                      // phase-A feature chunk (128-byte rows)
+constexpr int kTcTileBytesA = 128 * kTcChunk * 2; // one 128-row tile of a chunk (16 KB)
+constexpr int kTcMaxFeatures = 2048;  // bias staged in shared memory
+constexpr int kTcCtrlBytes = 12288;
 
 struct TcGeom {
-  int nslot;    // ring slots
-  int p_bytes;  // bytes of the P region (16 KB per 64 keys)
-  int n_qtiles; // query tiles per batch row
+  int nslot;          // phase-C ring slots
+  int p_bytes;        // bytes of the P region (16 KB per 64 keys)
+  int n_qtiles;       // query tiles per batch row
+  int a_nstage;       // phase-A stages inside the P region + phase-C ring
+  int a_stage_bytes;  // (1 + key tiles) x 8 KB
 };
 
-// Shared-memory control block (offsets in bytes).
+// Shared-memory control block.
 struct TcCtrl {
-  uint64_t full[kTcMaxSlots];
-  uint64_t empty[kTcMaxSlots];
-  uint64_t aux[kTcMaxSlots];
-  uint64_t fixed[kTcMaxSlots];
+  uint64_t a_full[kTcMaxStages], a_empty[kTcMaxStages];
+  uint64_t full[kTcMaxSlots], empty[kTcMaxSlots], fixed[kTcMaxSlots];
   uint64_t s_full, p_ready;
   uint64_t o_full[2], o_empty[2];
   uint32_t tmem_base;
@@ -70,7 +83,9 @@ struct TcCtrl {
   int pad_[1];
   float rinv[kTcMaxKeys];  // sums of squares, then inverse norms
   float den[2][128];
+  uint32_t kbits[kTcMaxKeys / 32];
   uint8_t kvalid[kTcMaxKeys];
+  float bias[kTcMaxFeatures];
 };
 static_assert(sizeof(TcCtrl) <= kTcCtrlBytes, "control block too large");
 
@@ -98,12 +113,12 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Unpack 8 16-bit values held in a uint4 to fp32.
+// Element e (0..31) of 32 packed 16-bit values.
 template <typename T>
-__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
-  const T* h = reinterpret_cast<const T*>(&v);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = to_f32<T>(h[i]);
+__device__ __forceinline__ float raw_at(const uint32_t (&w)[16], int e) {
+  const uint32_t word = w[e >> 1];
+  const uint16_t h = static_cast<uint16_t>((e & 1) ? (word >> 16) : (word & 0xFFFFu));
+  return to_f32<T>(*reinterpret_cast<const T*>(&h));
 }
 
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
@@ -127,39 +142,52 @@ __device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
   return v;
 }
 
-// Load 32 consecutive elements starting at p (p 16-byte aligned when vec).
+// 32 consecutive 16-bit elements starting at p into w[16] (p 16-byte aligned
+// when vec); elements at or past n_ok read as zero.
 template <typename T>
-__device__ __forceinline__ void load32(const T* p, int n_ok, bool vec, float (&f)[32]) {
+__device__ __forceinline__ void load_raw32(const T* p, int n_ok, bool vec, uint32_t (&w)[16]) {
   if (vec && n_ok >= 32) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      float t[8];
-      unpack8<T>(ld_global_nc_v4(p + 8 * q), t);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[8 * q + e] = t[e];
+      const uint4 v = ld_global_nc_v4(p + 8 * q);
+      w[4 * q] = v.x;
+      w[4 * q + 1] = v.y;
+      w[4 * q + 2] = v.z;
+      w[4 * q + 3] = v.w;
     }
   } else {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) f[e] = e < n_ok ? to_f32<T>(p[e]) : 0.f;
+    for (int e = 0; e < 32; e += 2) {
+      const uint32_t lo = e < n_ok ? h[e] : 0u;
+      const uint32_t hi = e + 1 < n_ok ? h[e + 1] : 0u;
+      w[e >> 1] = lo | (hi << 16);
+    }
   }
 }
 
-template <typename T>
+template <typename T, int ACT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_contextualize(const FwdArgs args, const __grid_constant__ CUtensorMap map_k,
-                     const __grid_constant__ CUtensorMap map_z, const TcGeom geom) {
+    tc_contextualize(const FwdArgs args, const __grid_constant__ CUtensorMap map_q,
+                     const __grid_constant__ CUtensorMap map_z,
+                     const __grid_constant__ CUtensorMap map_o, const TcGeom geom) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the 128-byte-swizzle atoms.
+  // 1024-byte alignment for the swizzle atoms.
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw_addr);
-  const uint32_t p_addr = base;
+  const uint32_t p_addr = base;  // P region; phase-A stages before phase B
   const uint32_t ring_addr = base + static_cast<uint32_t>(geom.p_bytes);
-  TcCtrl* ctrl = reinterpret_cast<TcCtrl*>(base_ptr + geom.p_bytes + geom.nslot * kTcUnitBytes);
+  // [P region | phase-C ring | output staging | control block]
+  const uint32_t out_stage_addr = ring_addr + static_cast<uint32_t>(geom.nslot * kTcUnitBytes);
+  TcCtrl* ctrl = reinterpret_cast<TcCtrl*>(base_ptr + geom.p_bytes + geom.nslot * kTcUnitBytes +
+                                           kTcOutStageBytes);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) AVEY_STAMP(0);
   const int nslot = geom.nslot;
+  const int nst = geom.a_nstage;
   const int C = args.ctx, D = args.feat, B = args.batch;
 
   // Work item: causal items with more key tiles come first (longest first).
@@ -167,15 +195,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int qt = args.causal ? geom.n_qtiles - 1 - item / B : item / B;
   const int b = item % B;
   const int q_lo = qt * 128;
+#ifdef AVEY_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) g_trace[blockIdx.x][15] = qt * 100000ull + b;
+#endif
 
   const uint8_t* va = args.has_valid ? args.valid + static_cast<int64_t>(b) * args.va_bs : nullptr;
 
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
+    for (int s = 0; s < kTcMaxStages; ++s) {
+      mbar_init(smem_u32(&ctrl->a_full[s]), 1);
+      mbar_init(smem_u32(&ctrl->a_empty[s]), 1);
+    }
     for (int s = 0; s < kTcMaxSlots; ++s) {
       mbar_init(smem_u32(&ctrl->full[s]), 1);
       mbar_init(smem_u32(&ctrl->empty[s]), 1);
-      mbar_init(smem_u32(&ctrl->aux[s]), 8);
       mbar_init(smem_u32(&ctrl->fixed[s]), 4);
     }
     mbar_init(smem_u32(&ctrl->s_full), 1);
@@ -189,8 +223,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_z);
+    tma_prefetch_desc(&map_o);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctrl->tmem_base), 512);
@@ -211,99 +246,137 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctrl->tmem_base;
+  if (tid == 0) AVEY_STAMP(1);
 
   // ---------------------------------------------------------------- geometry
   const int kv_end = ctrl->last_valid + 1;  // == C without a mask
   const bool skip = q_lo >= kv_end;         // no valid query row in this tile
   const int nkeys = args.causal ? min(kv_end, q_lo + 128) : kv_end;
-  const int nk = skip ? 0 : (nkeys + 127) / 128;  // key tiles (phase A)
-  const int nchunk = (D + 63) / 64;                // feature chunks (phase A)
-  const int nslices = (D + 255) / 256;             // output slices (phase C)
-  const int nunits = skip ? 0 : (nkeys + 31) / 32; // 32-key units per slice
-  const int units_a = nchunk * (1 + nk);
+  const int nk = skip ? 0 : (nkeys + 127) / 128;       // key tiles
+  const int nchunk = (D + kTcChunk - 1) / kTcChunk;     // phase-A feature chunks
+  const int nslices = (D + 255) / 256;                  // output slices (phase C)
+  const int nunits = skip ? 0 : (nkeys + kTcUnitKeys - 1) / kTcUnitKeys;  // units per slice
+  const int units_c = nslices * nunits;
   const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
 
   if (warp == 0) {
     // ============================================================ TMA producer
-    if (lane == 0 && !skip) {
-      // acount[s]: phase-A units placed in slot s so far; prev_a[s]: the slot's
-      // last occupant was a phase-A unit (released by the MMA *and* the
-      // compute warps' `aux` arrival).
-      uint32_t acount[kTcMaxSlots];
-      bool prev_a[kTcMaxSlots];
-#pragma unroll
-      for (int s = 0; s < kTcMaxSlots; ++s) {
-        acount[s] = 0;
-        prev_a[s] = false;
-      }
-      int u = 0;
-      auto acquire = [&](int slot, int use) {
-        if (use > 0) {
-          mbar_wait(smem_u32(&ctrl->empty[slot]), (use - 1) & 1);
-          if (prev_a[slot]) mbar_wait(smem_u32(&ctrl->aux[slot]), (acount[slot] - 1) & 1);
+    // The whole warp walks the schedule; one lane issues. Slot indices and
+    // barrier parities advance incrementally (no divisions in the hot loop).
+    if (!skip) {
+      const bool leader = lane == 0;
+      // Phase-A stage state.
+      int a_st = 0, a_use = 0, c = 0;
+      // Phase-C ring state.
+      int c_slot = 0, c_use = 0, u = 0, sl = 0, uu = 0;
+      int nbox = (min(256, D) + 63) / 64;
+      auto load_stage = [&]() {
+        if (a_use > 0) mbar_wait(smem_u32(&ctrl->a_empty[a_st]), (a_use - 1) & 1);
+        if (leader) AVEY_STAMP_UNIT(c, 0);
+        if (leader) {
+          const uint32_t full = smem_u32(&ctrl->a_full[a_st]);
+          const uint32_t st = p_addr + a_st * geom.a_stage_bytes;
+          mbar_arrive_expect_tx(full, (1 + nk) * kTcTileBytesA);
+          tma_load_3d(st, &map_q, full, c * kTcChunk, q_lo, b);
+          for (int t = 0; t < nk; ++t)
+            tma_load_3d(st + (1 + t) * kTcTileBytesA, &map_q, full, c * kTcChunk, t * 128, b);
+        }
+        __syncwarp();
+        ++c;
+        if (++a_st == nst) {
+          a_st = 0;
+          ++a_use;
         }
       };
-      for (int c = 0; c < nchunk; ++c) {
-        for (int t = -1; t < nk; ++t) {
-          const int slot = u % nslot, use = u / nslot;
-          acquire(slot, use);
-          const uint32_t full = smem_u32(&ctrl->full[slot]);
-          mbar_arrive_expect_tx(full, kTcUnitBytes);
-          tma_load_3d(ring_addr + slot * kTcUnitBytes, &map_k, full, c * 64,
-                      (t < 0 ? qt : t) * 128, b);
-          prev_a[slot] = true;
-          ++acount[slot];
-          ++u;
-        }
-      }
-      for (int s = 0; s < nslices; ++s) {
-        const int width = min(256, D - s * 256);
-        const int nbox = (width + 63) / 64;
-        for (int uu = 0; uu < nunits; ++uu) {
-          const int slot = u % nslot, use = u / nslot;
-          acquire(slot, use);
-          prev_a[slot] = false;
-          const uint32_t full = smem_u32(&ctrl->full[slot]);
-          mbar_arrive_expect_tx(full, nbox * 4096);
+      auto load_unit = [&]() {
+        if (c_use > 0) mbar_wait(smem_u32(&ctrl->empty[c_slot]), (c_use - 1) & 1);
+        if (leader) AVEY_STAMP_UNIT(128 + u, 0);
+        if (leader) {
+          const uint32_t full = smem_u32(&ctrl->full[c_slot]);
+          const uint32_t dst = ring_addr + c_slot * kTcUnitBytes;
+          mbar_arrive_expect_tx(full, nbox * kTcZBoxBytes);
           for (int i = 0; i < nbox; ++i)
-            tma_load_3d(ring_addr + slot * kTcUnitBytes + i * 4096, &map_z, full,
-                        s * 256 + i * 64, uu * 32, b);
-          ++u;
+            tma_load_3d(dst + i * kTcZBoxBytes, &map_z, full, sl * 256 + i * 64, uu * kTcUnitKeys, b);
+        }
+        __syncwarp();
+        ++u;
+        if (++uu == nunits) {
+          uu = 0;
+          ++sl;
+          nbox = (min(256, D - sl * 256) + 63) / 64;
+        }
+        if (++c_slot == nslot) {
+          c_slot = 0;
+          ++c_use;
+        }
+      };
+      // Phase-A stages span the P region and the phase-C ring, so the ring is
+      // filled only once every stage has been released for the last time (the
+      // MMA warp is done with it); phase B, which writes P into the low part of
+      // the same space, overlaps the first ring loads.
+      while (c < nchunk) load_stage();
+      {
+        // Final release of every stage slot s: its last use is use index
+        // (uses[s] - 1), where uses[s] = number of chunks that went to slot s.
+        for (int st_i = 0; st_i < min(nst, nchunk); ++st_i) {
+          const int uses = (nchunk - st_i + nst - 1) / nst;
+          mbar_wait(smem_u32(&ctrl->a_empty[st_i]), (uses - 1) & 1);
         }
       }
+      while (u < units_c) load_unit();
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
-    if (lane == 0 && !skip) {
-      const uint32_t idesc_g = idesc_f16(fmt, 128, 128, 0, 0);
-      int u = 0;
+    if (!skip) {
+      const bool leader = lane == 0;
+      // Descriptors are advanced by adding (byte offset >> 4) to the start
+      // address field; every address stays below 2^18, so nothing carries out.
+      const uint64_t dq0 = smem_desc_sw128(p_addr, 16, 1024);
+      const uint32_t stage_adv = static_cast<uint32_t>(geom.a_stage_bytes) >> 4;
+      const uint32_t idesc_g256 = idesc_f16(fmt, 128, 256, 0, 0);
+      const uint32_t idesc_g128 = idesc_f16(fmt, 128, 128, 0, 0);
+      const uint32_t idesc_g1 = nk >= 2 ? idesc_g256 : idesc_g128;
+      const uint32_t idesc_g2 = nk >= 4 ? idesc_g256 : idesc_g128;
+      int st = 0;
+      uint32_t ph = 0;
       for (int c = 0; c < nchunk; ++c) {
-        const int qslot = u % nslot;
-        mbar_wait(smem_u32(&ctrl->full[qslot]), (u / nslot) & 1);
+        mbar_wait(smem_u32(&ctrl->a_full[st]), ph);
         tc_fence_after();
-        const uint32_t qa = ring_addr + qslot * kTcUnitBytes;
-        ++u;
-        for (int t = 0; t < nk; ++t) {
-          const int slot = u % nslot;
-          mbar_wait(smem_u32(&ctrl->full[slot]), (u / nslot) & 1);
-          tc_fence_after();
-          const uint32_t ka = ring_addr + slot * kTcUnitBytes;
+        if (leader) AVEY_STAMP_UNIT(c, 1);
+        if (leader) {
+          const uint64_t dq = dq0 + st * stage_adv;
+          // Four 16-feature K steps (32 bytes each inside the 128-byte swizzled
+          // rows); key tiles (0,1) and (2,3) are each one N = 256 MMA.
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc_mma_f16(tmem + t * 128, smem_desc_sw128(qa + k * 32, 16, 1024),
-                       smem_desc_sw128(ka + k * 32, 16, 1024), idesc_g, (c | k) != 0);
-          tc_commit(smem_u32(&ctrl->empty[slot]));
-          ++u;
+          for (int k = 0; k < kTcChunk / 16; ++k) {
+            const uint32_t acc = (c != 0 || k != 0) ? 1u : 0u;
+            tc_mma_f16(tmem, dq + 2 * k, dq + (kTcTileBytesA >> 4) + 2 * k, idesc_g1, acc);
+            if (nk > 2)
+              tc_mma_f16(tmem + 256, dq + 2 * k, dq + (3 * kTcTileBytesA >> 4) + 2 * k, idesc_g2,
+                         acc);
+          }
+          tc_commit(smem_u32(&ctrl->a_empty[st]));
+          AVEY_STAMP_UNIT(c, 2);
         }
-        tc_commit(smem_u32(&ctrl->empty[qslot]));
+        __syncwarp();
+        if (++st == nst) {
+          st = 0;
+          ph ^= 1u;
+        }
       }
-      tc_commit(smem_u32(&ctrl->s_full));
+      if (leader) {
+        tc_commit(smem_u32(&ctrl->s_full));
+        AVEY_STAMP(2);  // last Gram MMA issued
+      }
+      __syncwarp();
       mbar_wait(smem_u32(&ctrl->p_ready), 0);
       tc_fence_after();
+      if (leader) AVEY_STAMP(3);  // P observed by the MMA warp
       const bool fix = ctrl->fix != 0;
-      uint32_t fixcount[kTcMaxSlots];
-#pragma unroll
-      for (int s = 0; s < kTcMaxSlots; ++s) fixcount[s] = 0;
+      const uint64_t dp0 = smem_desc_sw128(p_addr, 16, 1024);
+      const uint64_t dz0 = smem_desc_sw128(ring_addr, kTcZBoxBytes, 1024);
+      int slot = 0;
+      ph = 0;
       for (int s = 0; s < nslices; ++s) {
         const int buf = s & 1;
         if (s >= 2) {
@@ -311,28 +384,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_after();
         }
         const int width = min(256, D - s * 256);
-        const uint32_t n_mma = static_cast<uint32_t>((width + 15) & ~15);
-        const uint32_t idesc_o = idesc_f16(fmt, 128, n_mma, 0, 1);
+        const uint32_t idesc_o = idesc_f16(fmt, 128, static_cast<uint32_t>((width + 15) & ~15), 0, 1);
+        const uint32_t d_tmem = tmem + buf * 256;
         for (int uu = 0; uu < nunits; ++uu) {
-          const int slot = u % nslot;
-          if (fix)
-            mbar_wait(smem_u32(&ctrl->fixed[slot]), (fixcount[slot]++) & 1);
-          else
-            mbar_wait(smem_u32(&ctrl->full[slot]), (u / nslot) & 1);
+          mbar_wait(smem_u32(fix ? &ctrl->fixed[slot] : &ctrl->full[slot]), ph);
           tc_fence_after();
-          const uint32_t za = ring_addr + slot * kTcUnitBytes;
+          if (leader) AVEY_STAMP_UNIT(128 + s * nunits + uu, 1);
+          if (leader) {
+            // P keys 64 uu .. +63 are P chunk uu (16 KB, K-major); K steps of 16
+            // keys advance 32 bytes in P and 16 rows (2 KB) in the Z unit.
+            const uint64_t dp = dp0 + uu * (kTcPChunkBytes >> 4);
+            const uint64_t dz = dz0 + slot * (kTcUnitBytes >> 4);
 #pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int j0 = uu * 32 + k * 16;
-            const uint32_t pa = p_addr + (j0 >> 6) * 16384 + ((j0 & 63) >> 4) * 32;
-            tc_mma_f16(tmem + buf * 256, smem_desc_sw128(pa, 16, 1024),
-                       smem_desc_sw128(za + k * 2048, 4096, 1024), idesc_o, (uu | k) != 0);
+            for (int k = 0; k < kTcUnitKeys / 16; ++k)
+              tc_mma_f16(d_tmem, dp + 2 * k, dz + k * (2048 >> 4), idesc_o,
+                         (uu != 0 || k != 0) ? 1u : 0u);
+            tc_commit(smem_u32(&ctrl->empty[slot]));
+            AVEY_STAMP_UNIT(128 + s * nunits + uu, 2);
           }
-          tc_commit(smem_u32(&ctrl->empty[slot]));
-          ++u;
+          __syncwarp();
+          if (++slot == nslot) {
+            slot = 0;
+            ph ^= 1u;
+          }
         }
-        tc_commit(smem_u32(&ctrl->o_full[buf]));
+        if (leader) tc_commit(smem_u32(&ctrl->o_full[buf]));
+        __syncwarp();
       }
+      if (leader) AVEY_STAMP(4);  // last mix MMA issued
     }
   } else if (warp >= 4) {
     // ============================================================ compute warps
@@ -349,67 +428,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (skip) {
       // Every query row of this tile is padding: the output rows are zero.
       const int rows = min(128, C - q_lo);
-      for (int e = (cw * 32 + lane) * 8; e < rows * D; e += 256 * 8) {
-        for (int k = 0; k < 8 && e + k < rows * D; ++k) {
-          const int r = (e + k) / D, f = (e + k) % D;
-          out[static_cast<int64_t>(q_lo + r) * args.o_rs + f] = store_cast<T, float>(0.f);
-        }
+      for (int e = cw * 32 + lane; e < rows * D; e += 256) {
+        const int r = e / D, f = e % D;
+        out[static_cast<int64_t>(q_lo + r) * args.o_rs + f] = store_cast<T, float>(0.f);
       }
     } else {
-      // ---------------- phase A: sums of squares of every key row, from smem
-      float ss[4][4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) ss[t][q] = 0.f;
-      {
-        // The compute warps step through every phase-A unit (query units too,
-        // without reading them) so that they observe each phase of each slot's
-        // barrier in order; the producer waits for their `aux` arrival before
-        // refilling a phase-A slot.
-        int u = 0;
-        for (int c = 0; c < nchunk; ++c) {
-          {
-            const int slot = u % nslot;
-            mbar_wait(smem_u32(&ctrl->full[slot]), (u / nslot) & 1);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&ctrl->aux[slot]));
-            ++u;
-          }
-          for (int t = 0; t < nk; ++t) {
-            const int slot = u % nslot;
-            mbar_wait(smem_u32(&ctrl->full[slot]), (u / nslot) & 1);
-            const uint32_t ua = ring_addr + slot * kTcUnitBytes;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int r = cw * 16 + q * 4 + (lane >> 3);
-              const int phys = (lane & 7) ^ (r & 7);
-              float f[8];
-              unpack8<T>(ld_shared_v4(ua + r * 128 + phys * 16), f);
-              float s = 0.f;
-#pragma unroll
-              for (int e = 0; e < 8; ++e) s = fmaf(f[e], f[e], s);
-              s += __shfl_xor_sync(0xffffffffu, s, 1);
-              s += __shfl_xor_sync(0xffffffffu, s, 2);
-              s += __shfl_xor_sync(0xffffffffu, s, 4);
-#pragma unroll
-              for (int tt = 0; tt < 4; ++tt)
-                if (tt == t) ss[tt][q] += s;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&ctrl->aux[slot]));
-            ++u;
-          }
-        }
+      // Warm L2 with this thread's half of its gate row (read in phase C).
+      if (args.has_zl && i < C) {
+        const char* grow = reinterpret_cast<const char*>(zl + static_cast<int64_t>(i) * args.zl_rs);
+        const int nlines = (D * 2 + 127) / 128;
+        const int half = (nlines + 1) / 2;
+        for (int l = h * half; l < min(nlines, (h + 1) * half); ++l)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(grow + l * 128));
       }
-      if ((lane & 7) == 0) {
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (t < nk) ctrl->rinv[t * 128 + cw * 16 + q * 4 + (lane >> 3)] = ss[t][q];
+      // ---------------- phase A (compute warps): sums of squares of the key rows
+      // from norm_prepass, which may still be running (programmatic dependent
+      // launch): wait for it only here.
+      griddep_wait();
+      {
+        const float* ssq = args.sumsq + static_cast<int64_t>(b) * C;
+        for (int j = cw * 32 + lane; j < nk * 128; j += 256) ctrl->rinv[j] = j < C ? ssq[j] : 0.f;
       }
       named_bar_sync(1, 256);
+      if (cw == 0 && lane == 0) AVEY_STAMP(5);  // norms read
       {
         const int tid_c = cw * 32 + lane;
         const float norm_eps = args.norm_eps_f;
@@ -421,50 +462,87 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ctrl->rinv[j] = 1.f / fmaxf(sqrtf(s2), norm_eps);
         }
         if (bad) ctrl->fix = 1;
+        // Key bitmask: bit e of word w <=> key 32 w + e is valid and < nkeys.
+        if (tid_c < kTcMaxKeys / 32) {
+          uint32_t m = 0u;
+          for (int e = 0; e < 32; ++e) {
+            const int j = tid_c * 32 + e;
+            if (j < nkeys && ctrl->kvalid[j]) m |= 1u << e;
+          }
+          ctrl->kbits[tid_c] = m;
+        }
+        if (args.has_bias)
+          for (int f = tid_c; f < D; f += 256)
+            ctrl->bias[f] = to_f32<T>(static_cast<const T*>(args.bias)[f]);
       }
       named_bar_sync(1, 256);
 
-      // ---------------- phase B: P = G * rinv_i * rinv_j * V, masked, to smem
+      // ---------------- phase B: P = G * rinv_i * rinv_j * V, masked, into smem
       mbar_wait(smem_u32(&ctrl->s_full), 0);
       tc_fence_after();
+      if (cw == 0 && lane == 0) AVEY_STAMP(6);  // Gram complete
       const bool row_ok = i < C && ctrl->kvalid[i];
       const float rqi = row_ok ? ctrl->rinv[i] : 0.f;
       const T* vrow = (args.has_v && i < C) ? static_cast<const T*>(args.v) + static_cast<int64_t>(i) * args.v_rs
                                             : nullptr;
       const bool v_vec = (reinterpret_cast<uintptr_t>(args.v) & 15u) == 0 && (args.v_rs & 7) == 0;
       float den = 0.f;
-      const int half_cols = nk * 64;
-      for (int ch = 0; ch < half_cols / 32; ++ch) {
-        const int c0 = h * half_cols + ch * 32;
-        uint32_t g[32];
-        tmem_ld32(tmem + lane_off + c0, g);
-        tmem_wait_ld();
-        float vv[32];
-        if (vrow)
-          load32<T>(vrow + c0, C - c0, v_vec, vv);
-        else
+      {
+        const int c_begin = h * nk * 64;
+        const int nch = nk * 2;
+        // V without a weight matrix is 1.0 everywhere (packed 16-bit ones).
+        const uint32_t one2 = pack2<T>(1.f, 1.f);
+        uint32_t vw[16], vn[16], vnn[16];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) vv[e] = 1.f;
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p2[2];
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int j = c0 + e + k;
-            const bool ok = row_ok && j < nkeys && ctrl->kvalid[j] && (!args.causal || j <= i);
-            const float p = __uint_as_float(g[e + k]) * rqi * ctrl->rinv[j] * vv[e + k];
-            p2[k] = ok ? p : 0.f;
-            den += p2[k];
-          }
-          pk[e >> 1] = pack2<T>(p2[0], p2[1]);
+        for (int q = 0; q < 16; ++q) vw[q] = vn[q] = vnn[q] = one2;
+        if (vrow) {
+          load_raw32<T>(vrow + c_begin, C - c_begin, v_vec, vw);
+          if (nch > 1) load_raw32<T>(vrow + c_begin + 32, C - c_begin - 32, v_vec, vn);
         }
-        const uint32_t chunk = p_addr + (c0 >> 6) * 16384 + row * 128;
-        const int ubase = (c0 & 63) >> 3;
+#pragma unroll 1
+        for (int ch = 0; ch < nch; ++ch) {
+          const int c0 = c_begin + ch * 32;
+          uint32_t g[32];
+          tmem_ld32(tmem + lane_off + c0, g);
+          if (vrow && ch + 2 < nch) load_raw32<T>(vrow + c0 + 64, C - c0 - 64, v_vec, vnn);
+          // Allowed keys of this chunk: valid, below nkeys, and j <= i if causal.
+          uint32_t okb = row_ok ? ctrl->kbits[c0 >> 5] : 0u;
+          if (args.causal) {
+            const int lim = i - c0 + 1;
+            okb &= lim >= 32 ? 0xFFFFFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+          }
+          tmem_wait_ld(g);
+          const float4* rk4 = reinterpret_cast<const float4*>(&ctrl->rinv[c0]);
+          uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int phys = (ubase + q) ^ (row & 7);
-          st_shared_v4(chunk + phys * 16, pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          for (int q = 0; q < 8; ++q) {
+            const float4 rk = rk4[q];
+            const float r[4] = {rk.x, rk.y, rk.z, rk.w};
+            float pv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int idx = 4 * q + e;
+              const float p = __uint_as_float(g[idx]) * rqi * r[e] * raw_at<T>(vw, idx);
+              pv[e] = ((okb >> idx) & 1u) ? p : 0.f;
+              den += pv[e];
+            }
+            pk[2 * q] = pack2<T>(pv[0], pv[1]);
+            pk[2 * q + 1] = pack2<T>(pv[2], pv[3]);
+          }
+          const uint32_t chunk = p_addr + (c0 >> 6) * kTcPChunkBytes + row * 128;
+          const int ubase = (c0 & 63) >> 3;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int phys = (ubase + q) ^ (row & 7);
+            st_shared_v4(chunk + phys * 16, pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+          if (vrow) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              vw[q] = vn[q];
+              vn[q] = vnn[q];
+            }
+          }
         }
       }
       ctrl->den[h][row] = den;
@@ -473,6 +551,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctrl->p_ready));
       named_bar_sync(1, 256);
+      if (cw == 0 && lane == 0) AVEY_STAMP(7);  // P written
       const float inv_den =
           args.normalize ? 1.f / (ctrl->den[0][row] + ctrl->den[1][row] + args.eps_f) : 1.f;
       const bool fix = ctrl->fix != 0;
@@ -480,78 +559,126 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // ---------------- phase C: drain O slices (and, in fix mode, clean units)
       const bool zl_vec = zl && (reinterpret_cast<uintptr_t>(args.z_tl) & 15u) == 0 &&
                           (args.zl_rs & 7) == 0 && (args.zl_bs & 7) == 0;
-      const bool o_vec = (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0 &&
-                         (args.o_rs & 7) == 0 && (args.o_bs & 7) == 0;
-      const bool b_vec = args.has_bias && (reinterpret_cast<uintptr_t>(args.bias) & 15u) == 0;
-      auto drain = [&](int s, int buf) {
+      const T* zrow = (zl && i < C) ? zl + static_cast<int64_t>(i) * args.zl_rs : nullptr;
+      const bool has_bias = args.has_bias;
+      // Gate words for the next chunk to drain (prefetched one chunk ahead,
+      // across slice boundaries too).
+      uint32_t gn[16];
+      // Output staging: each compute warp owns a 32-row x 32-column tile (2 KB,
+      // 64-byte swizzle) that it fills from registers and writes out with one
+      // TMA tensor store; lane 0 tracks the store's bulk group.
+      const uint32_t stage_o = out_stage_addr + cw * kTcOutTileBytes;
+      auto emit = [&](int f0, const uint32_t (&o)[32], const uint32_t (&gw)[16]) {
+        const float4* b4 = reinterpret_cast<const float4*>(&ctrl->bias[f0]);
+        uint32_t pk[16];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 bb = has_bias ? b4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+          float yv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int idx = 4 * q + e;
+            float y = act_fn<ACT>(fmaf(__uint_as_float(o[idx]), inv_den, bv[e]));
+            if (zrow) y *= raw_at<T>(gw, idx);
+            yv[e] = row_ok ? y : 0.f;
+          }
+          pk[2 * q] = pack2<T>(yv[0], yv[1]);
+          pk[2 * q + 1] = pack2<T>(yv[2], yv[3]);
+        }
+        // The previous store from this tile must have finished reading it.
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int phys = q ^ ((lane >> 1) & 3);  // 64-byte swizzle
+          st_shared_v4(stage_o + lane * 64 + phys * 16, pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                       pk[4 * q + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&map_o, stage_o, f0, q_lo + wq * 32, b);
+          bulk_commit_group();
+        }
+      };
+      auto drain = [&](int s, int buf, int s_next) {
         mbar_wait(smem_u32(&ctrl->o_full[buf]), (s >> 1) & 1);
         tc_fence_after();
         const int width = min(256, D - s * 256);
-        for (int ch = 0; ch < (width + 31) / 32; ++ch) {
-          const int f0 = s * 256 + ch * 32;
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_off + buf * 256 + ch * 32, o);
-          tmem_wait_ld();
-          if (i >= C) continue;
-          float bias[32], gate[32];
-          if (args.has_bias)
-            load32<T>(static_cast<const T*>(args.bias) + f0, D - f0, b_vec, bias);
-          else
-#pragma unroll
-            for (int e = 0; e < 32; ++e) bias[e] = 0.f;
-          if (zl)
-            load32<T>(zl + static_cast<int64_t>(i) * args.zl_rs + f0, D - f0, zl_vec, gate);
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float y2[2];
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              float y = activate<float>(__uint_as_float(o[e + k]) * inv_den + bias[e + k], args.act);
-              if (zl) y *= gate[e + k];
-              y2[k] = row_ok ? y : 0.f;
-            }
-            pk[e >> 1] = pack2<T>(y2[0], y2[1]);
+        const int nch_o = (width + 31) / 32;
+        const uint32_t tb = tmem + lane_off + buf * 256;
+        // Gate words of the chunk after `f0` (the rest of this slice, then the
+        // first chunk of s_next), prefetched one chunk ahead.
+        auto next_gate = [&](int ch, int f0) {
+          if (zrow) {
+            const int fn = ch + 1 < nch_o ? f0 + 32 : (s_next < nslices ? s_next * 256 : -1);
+            if (fn >= 0) load_raw32<T>(zrow + fn, D - fn, zl_vec, gn);
           }
-          T* dst = out + static_cast<int64_t>(i) * args.o_rs + f0;
-          if (o_vec && f0 + 32 <= D) {
+        };
+        // TMEM loads run one chunk ahead of the math.
+        uint32_t oa[32], ob[32], gw[16];
+        tmem_ld32(tb, oa);
+#pragma unroll 1
+        for (int ch = 0; ch < nch_o; ch += 2) {
+          const int f0 = s * 256 + ch * 32;
+          tmem_wait_ld(oa);
+          const bool has_b = ch + 1 < nch_o;
+          if (has_b) tmem_ld32(tb + (ch + 1) * 32, ob);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<uint4*>(dst + 8 * q) =
-                  make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          } else {
-            const T* hv = reinterpret_cast<const T*>(pk);
-            for (int e = 0; e < 32 && f0 + e < D; ++e) dst[e] = hv[e];
+          for (int q = 0; q < 16; ++q) gw[q] = gn[q];
+          next_gate(ch, f0);
+          emit(f0, oa, gw);
+          if (has_b) {
+            tmem_wait_ld(ob);
+            if (ch + 2 < nch_o) tmem_ld32(tb + (ch + 2) * 32, oa);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) gw[q] = gn[q];
+            next_gate(ch + 1, f0 + 32);
+            emit(f0 + 32, ob, gw);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&ctrl->o_empty[buf]));
+        if (wq == 0 && lane == 0 && s < 6) AVEY_STAMP(8 + s);  // slice s drained
       };
+      const int s_first = fix ? 0 : h;
+      if (zrow && s_first < nslices) load_raw32<T>(zrow + s_first * 256, D - s_first * 256, zl_vec, gn);
       if (!fix) {
-        for (int s = h; s < nslices; s += 2) drain(s, h);
+        for (int s = h; s < nslices; s += 2) drain(s, h, s + 2);
+        if (lane == 0) bulk_wait_all();
       } else if (h == 0) {
-        for (int s = 0; s < nslices; ++s) drain(s, s & 1);
+        for (int s = 0; s < nslices; ++s) drain(s, s & 1, s + 1);
+        if (lane == 0) bulk_wait_all();
       } else {
         // Fix mode: zero every padded key row of each mix unit before the MMA
         // reads it (warpgroup 1), while warpgroup 0 drains all slices.
-        int u = units_a;
-        for (int s = 0; s < nslices; ++s) {
-          const int width = min(256, D - s * 256);
-          const int nbox = (width + 63) / 64;
-          for (int uu = 0; uu < nunits; ++uu) {
-            const int slot = u % nslot;
-            mbar_wait(smem_u32(&ctrl->full[slot]), (u / nslot) & 1);
-            const int key = uu * 32 + lane;
-            if (wq < nbox && key < C && !ctrl->kvalid[key]) {
-              const uint32_t ra = ring_addr + slot * kTcUnitBytes + wq * 4096 + lane * 128;
+        int slot = 0, sl = 0, uu = 0;
+        uint32_t ph = 0;
+        for (int u = 0; u < units_c; ++u) {
+          const int nbox = (min(256, D - sl * 256) + 63) / 64;
+          mbar_wait(smem_u32(&ctrl->full[slot]), ph);
+          // Warpgroup 1 (128 threads) covers the unit's nbox x 64 rows.
+          for (int idx = wq * 32 + lane; idx < nbox * kTcUnitKeys; idx += 128) {
+            const int r = idx & (kTcUnitKeys - 1), box = idx / kTcUnitKeys;
+            const int key = uu * kTcUnitKeys + r;
+            if (key < C && !ctrl->kvalid[key]) {
+              const uint32_t ra = ring_addr + slot * kTcUnitBytes + box * kTcZBoxBytes + r * 128;
 #pragma unroll
               for (int q = 0; q < 8; ++q) st_shared_v4(ra + q * 16, 0u, 0u, 0u, 0u);
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&ctrl->fixed[slot]));
-            ++u;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctrl->fixed[slot]));
+          if (++uu == nunits) {
+            uu = 0;
+            ++sl;
+          }
+          if (++slot == nslot) {
+            slot = 0;
+            ph ^= 1u;
           }
         }
       }
@@ -561,6 +688,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) AVEY_STAMP(14);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);

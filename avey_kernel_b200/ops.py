@@ -132,6 +132,13 @@ def contextualize(z_tr: torch.Tensor, v: Optional[torch.Tensor], z_tl: Optional[
     params = build_params(z_tr, v, z_tl, bias, valid, out, eps=eps, norm_eps=norm_eps,
                           causal=causal, normalize=normalize, activation_id=activation,
                           kernel=variant)
+    nbytes = _native.workspace_size(params)
+    workspace = None
+    if nbytes:
+        # Scratch from torch's caching allocator (stream-ordered, graph-safe).
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=z_tr.device)
+        params.workspace = workspace.data_ptr()
+        params.workspace_bytes = nbytes
     with torch.cuda.device(z_tr.device):
         _native.forward(params, torch.cuda.current_stream(z_tr.device).cuda_stream)
     return out

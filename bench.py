@@ -1,0 +1,528 @@
+"""Contextualizer forward benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c3|c4|c5]
+
+A step is one contextualizer forward over one batch of synthetic input shaped
+like a BASELINE config (default c2: Avey causal, bf16, B=64 per GPU, N=512,
+head/tail d'=768, bias and gate). With N GPUs (one process per GPU under
+torchrun) every rank runs its own batch shard: no collective on the data path
+("scaling": "weak" for c2-c4; c5 keeps the global batch of 1024 fixed and
+splits it, "strong").
+
+value  device time: K steps replayed from CUDA graphs between CUDA events on
+       the launching stream, inputs resident in HBM and rotating over three
+       sets larger than L2; whole-job tokens/s over the max across ranks.
+e2e    the same metric through the public API (avey / avey_b) with pinned
+       host buffers: every step copies its inputs host->device and reads the
+       output back, inside the timed region.
+--impl reference  times the CPU implementation of the path (the NumPy port of
+       the reference's _reference in oracle/, fp32, all host threads) on a
+       bounded sample of the same workload; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: (batch per GPU or global, context, features, op, causal, bias, ragged, boost, scaling)
+    'c2': dict(batch=64, n=512, d=768, op='avey', bias=True, ragged=False, boost=False,
+               scaling='weak', desc='Avey causal contextualizer, bf16, B=64 per GPU, N=512, '
+                                    "head/tail d'=768, W_mix~N(0,0.02), bias~N(0,0.01)"),
+    'c3': dict(batch=128, n=512, d=384, op='avey_b', bias=False, ragged=True, boost=False,
+               scaling='weak', desc='Avey-B bidirectional, bf16, B=128 per GPU, N=512, '
+                                    "d'=384, padding lengths ~U[N/4, N]"),
+    'c4': dict(batch=16, n=2048, d=1024, op='avey', bias=False, ragged=False, boost=True,
+               scaling='weak', desc="Long-context Avey causal, bf16, B=16 per GPU, N=2048, d'=1024,"
+                                    ' 5% rows x50'),
+    'c5': dict(batch=1024, n=512, d=768, op='avey', bias=False, ragged=False, boost=False,
+               scaling='strong', desc='Avey causal bf16, global B=1024 split by batch, N=512, '
+                                      "d'=768"),
+}
+METRIC = 'contextualizer fwd tokens/s'
+UNIT = 'tokens/s'
+
+
+def load_peaks():
+    path = ROOT / 'MEASURED_PEAKS.json'
+    if path.exists():
+        p = json.loads(path.read_text())
+        return dict(hbm_gbs=p['hbm_gbs'], bf16_tflops=p['bf16_tflops'],
+                    bf16_tflops_sustained=p.get('bf16_tflops_sustained'), source='measured')
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0,
+                source='fallback')
+
+
+def rank_env():
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    return world, rank, local
+
+
+def shard_batch(cfg, world):
+    if cfg['scaling'] == 'strong':
+        if cfg['batch'] % world:
+            raise SystemExit(f'global batch {cfg["batch"]} does not split over {world} GPUs')
+        return cfg['batch'] // world
+    return cfg['batch']
+
+
+def make_inputs(cfg, batch, seed, device='cpu'):
+    """Seeded synthetic inputs (fixed draw order: x, W, bias, lengths, boost)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    n, d = cfg['n'], cfg['d']
+    x = torch.randn(batch, n, 2 * d, generator=g)
+    w = torch.randn(n, n, generator=g) * 0.02
+    bias = torch.randn(d, generator=g) * 0.01 if cfg['bias'] else None
+    valid = None
+    if cfg['ragged']:
+        lengths = torch.randint(n // 4, n + 1, (batch,), generator=g)
+        valid = torch.arange(n)[None, :] < lengths[:, None]
+    if cfg['boost']:
+        rows = torch.rand(batch, n, 1, generator=g) < 0.05
+        x = torch.where(rows, x * 50, x)
+    bf = torch.bfloat16
+    out = dict(x=x.to(bf), w=w.to(bf) if cfg['op'] == 'avey' else None,
+               bias=bias.to(bf) if bias is not None else None, valid=valid)
+    if device != 'cpu':
+        out = {k: (v.to(device) if v is not None else None) for k, v in out.items()}
+    return out
+
+
+def algorithmic(cfg, batch, valid):
+    """Bytes and useful FLOPs of one launch: z_tr, z_tl read, out written, V,
+    bias, valid; 4 d' FLOPs per allowed (query, key) pair."""
+    import numpy as np
+    n, d, es = cfg['n'], cfg['d'], 2
+    causal = cfg['op'] == 'avey'
+    if valid is None:
+        pairs = batch * (n * (n + 1) // 2 if causal else n * n)
+    else:
+        ok = valid.cpu().numpy().astype(bool)
+        cnt = ok.sum(axis=1).astype(np.int64)
+        pairs = int((cnt * cnt).sum()) if not causal else int(
+            (np.cumsum(ok, axis=1) * ok).sum())
+    nbytes = es * batch * n * d * 3 + (es * n * n if causal else 0) + (es * d if cfg['bias'] else 0)
+    nbytes += batch * n if valid is not None else 0
+    return nbytes, 4 * d * pairs
+
+
+def nvml_handle(nv, cuda_index):
+    """NVML handle of a CUDA device (CUDA_VISIBLE_DEVICES may renumber GPUs)."""
+    import torch
+    props = torch.cuda.get_device_properties(cuda_index)
+    uuid = getattr(props, 'uuid', None)
+    if uuid is not None:
+        text = str(uuid)
+        for cand in (text if text.startswith('GPU-') else 'GPU-' + text, text):
+            try:
+                return nv.nvmlDeviceGetHandleByUUID(cand)
+            except Exception:
+                pass
+    bus = getattr(props, 'pci_bus_id', None)
+    if bus is not None:
+        pci = (f'{getattr(props, "pci_domain_id", 0):08x}:{bus:02x}:'
+               f'{getattr(props, "pci_device_id", 0):02x}.0')
+        try:
+            return nv.nvmlDeviceGetHandleByPciBusId(pci)
+        except Exception:
+            pass
+    return nv.nvmlDeviceGetHandleByIndex(cuda_index)
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons through NVML."""
+
+    REASONS = {  # NVML clocks-event reason bits
+        0x1: 'gpu_idle', 0x2: 'applications_clocks_setting', 0x4: 'sw_power_cap',
+        0x8: 'hw_slowdown', 0x10: 'sync_boost', 0x20: 'sw_thermal_slowdown',
+        0x40: 'hw_thermal_slowdown', 0x80: 'hw_power_brake_slowdown',
+        0x100: 'display_clock_setting',
+    }
+
+    def __init__(self, index, period=0.01):
+        self.index, self.period = index, period
+        self.samples, self.error = [], None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = nvml_handle(pynvml, self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._sample()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as exc:  # pragma: no cover - reported, not fatal
+            self.error = repr(exc)
+            self.max_mhz = None
+        return self
+
+    def _sample(self):
+        nv = self._nvml
+        sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        power = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0
+        self.samples.append((sm, reasons, power))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception as exc:  # pragma: no cover
+                self.error = repr(exc)
+                return
+            time.sleep(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self):
+        if not self.samples:
+            return {'sm_mhz': None, 'sm_max_mhz': self.max_mhz, 'reasons': [],
+                    'samples': 0, 'error': self.error}
+        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        reasons = 0
+        for s in busy:
+            reasons |= s[1]
+        names = [name for bit, name in self.REASONS.items() if reasons & bit and bit != 0x1]
+        return {'sm_mhz': statistics.median(s[0] for s in busy), 'sm_max_mhz': self.max_mhz,
+                'reasons': names, 'samples': len(self.samples),
+                'power_w_max': max(s[2] for s in self.samples)}
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        info = threadpool_info()
+        if info:
+            return max(i.get('num_threads', 1) for i in info)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def time_cpu_port(cfg, seconds=10.0, max_steps=None, warmup=1, rows=1):
+    """Time the NumPy port of the reference (oracle/, fp32 accumulation, all
+    BLAS threads) on `rows` batch rows per step. Returns tokens/s, steps, rows."""
+    import numpy as np
+    import oracle
+    inp = make_inputs(cfg, rows, seed=0)
+    d = cfg['d']
+    x = inp['x'].float().numpy()
+    zl, zt = x[..., :d], x[..., d:]
+    w = inp['w'].float().numpy() if inp['w'] is not None else None
+    bias = inp['bias'].float().numpy() if inp['bias'] is not None else None
+    valid = inp['valid'].numpy() if inp['valid'] is not None else None
+
+    def step():
+        if cfg['op'] == 'avey':
+            return oracle.avey(zt, w, z_tl=zl, bias=bias, valid=valid, accum=np.float32)
+        return oracle.avey_b(zt, z_tl=zl, bias=bias, valid=valid, accum=np.float32)
+
+    for _ in range(warmup):
+        step()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (max_steps is None and time.perf_counter() < t_end) or (
+            max_steps is not None and len(times) < max_steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    tokens = rows * cfg['n']
+    return tokens / statistics.median(times), len(times), sum(times)
+
+
+def run_reference(args, cfg):
+    world, rank, _ = rank_env()
+    if rank != 0:
+        return 0  # the CPU reference arm runs once, on rank 0
+    batch = shard_batch(cfg, world)
+    t0 = time.perf_counter()
+    value, steps, busy = time_cpu_port(cfg, max_steps=args.steps, warmup=args.warmup, rows=1)
+    cores = cpu_threads()
+    sample = (f'{steps} steps x 1 of {batch} batch rows ({cfg["n"]} tokens) of {args.config}, '
+              f'fp32 NumPy port of avey_kernels/ops.py::_reference (oracle/)')
+    line = {
+        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': 1e3 * cfg['n'] / value,
+        'higher_is_better': True, 'scaling': cfg['scaling'], 'vs_baseline': None,
+        'dtype': 'f32', 'data': 'synthetic',
+        'config': {'workload': f'{args.config}: {cfg["desc"]}', 'context': cfg['n'],
+                   'features': cfg['d'], 'batch_per_gpu': batch,
+                   'global_batch': batch * world},
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                         'sample': sample},
+        'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+        'wall_s': time.perf_counter() - t0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+    from avey_kernel_b200 import _native, avey, avey_b, ops
+
+    world, rank, local = rank_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device('cuda', torch.cuda.current_device())
+    batch = shard_batch(cfg, world)
+    d = cfg['d']
+    peaks = load_peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+
+    # Three input sets (each > 1/3 of L2) rotate so no step finds its inputs in L2.
+    nsets = 3
+    sets = [make_inputs(cfg, batch, seed=1000 * rank + s, device=dev) for s in range(nsets)]
+    outs = [None] * nsets
+
+    def call(s):
+        t = sets[s]
+        head, tail = t['x'][..., :d], t['x'][..., d:]
+        if cfg['op'] == 'avey':
+            return avey(tail, t['w'], z_tl=head, bias=t['bias'], valid=t['valid'])
+        return avey_b(tail, z_tl=head, bias=t['bias'], valid=t['valid'])
+
+    t0 = time.perf_counter()
+    # Verification first (outside any timed region): sampled rows vs the oracle.
+    import numpy as np
+    import oracle
+    y = call(0)
+    torch.cuda.synchronize()
+    t = sets[0]
+    verify_err = 0.0
+    for r in sorted({0, batch - 1}):
+        x = t['x'][r:r + 1].float().cpu().numpy()
+        kw = dict(z_tl=x[..., :d], bias=t['bias'].float().cpu().numpy() if t['bias'] is not None else None,
+                  valid=t['valid'][r:r + 1].cpu().numpy() if t['valid'] is not None else None)
+        ref = (oracle.avey(x[..., d:], t['w'].float().cpu().numpy(), **kw) if cfg['op'] == 'avey'
+               else oracle.avey_b(x[..., d:], **kw))
+        got = y[r:r + 1].float().cpu().numpy()
+        verify_err = max(verify_err, float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30)))
+    # Gather each rank's first output row to rank 0 (verification only, NCCL).
+    if world > 1:
+        row = y[0].contiguous()
+        gathered = [torch.empty_like(row) for _ in range(world)] if rank == 0 else None
+        dist.gather(row, gathered, dst=0)
+        errs = torch.tensor([verify_err], device=dev)
+        dist.all_reduce(errs, op=dist.ReduceOp.MAX)
+        verify_err = float(errs.item())
+    plan = ops.plan(sets[0]['x'][..., d:], sets[0]['w'], sets[0]['x'][..., :d], sets[0]['bias'],
+                    sets[0]['valid'], causal=cfg['op'] == 'avey', normalize=cfg['op'] != 'avey')
+    kernel_name = {1: 'simt_contextualize', 2: 'tc_contextualize'}[plan.kernel]
+
+    # Warm-up (untimed), then capture chunks of steps into CUDA graphs.
+    for i in range(max(args.warmup, 3)):
+        outs[i % nsets] = call(i % nsets)
+    torch.cuda.synchronize()
+    chunk = min(args.steps, 60)
+    graphs = []
+    remaining = args.steps
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    launches_captured = 0
+    keep = []
+    while remaining > 0:
+        n_steps = min(chunk, remaining)
+        if graphs and n_steps == graphs[0][1]:
+            graphs.append((graphs[0][0], n_steps))
+        else:
+            g = torch.cuda.CUDAGraph()
+            before = _native.launch_count()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(n_steps):
+                    keep.append(call(i % nsets))
+            launches_captured += _native.launch_count() - before
+            graphs.append((g, n_steps))
+        remaining -= n_steps
+    torch.cuda.synchronize()
+    gpu_launches = sum(n for _, n in graphs) * plan.launches  # native kernels per step
+    for g, _ in graphs[:2]:  # warm the graph executables
+        g.replay()
+    torch.cuda.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for g, _ in graphs:
+                g.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_total = start.elapsed_time(end)
+    ms_step = ms_total / args.steps
+    if world > 1:
+        tt = torch.tensor([ms_step], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_step = float(tt.item())
+    tokens_per_step = batch * cfg['n'] * world
+    value = tokens_per_step / (ms_step / 1e3)
+
+    # End to end through the public API with pinned host buffers.
+    e2e_steps = max(3, min(args.steps, 30))
+    t = sets[0]
+    x_host = t['x'].cpu().pin_memory()
+    w_host = t['w'].cpu().pin_memory() if t['w'] is not None else None
+    b_host = t['bias'].cpu().pin_memory() if t['bias'] is not None else None
+    v_host = t['valid'].cpu().pin_memory() if t['valid'] is not None else None
+    out_host = torch.empty(batch, cfg['n'], d, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(t['x'])
+    w_dev = torch.empty_like(t['w']) if w_host is not None else None
+    b_dev = torch.empty_like(t['bias']) if b_host is not None else None
+    v_dev = torch.empty_like(t['valid']) if v_host is not None else None
+    h2d = sum(h.numel() * h.element_size() for h in (x_host, w_host, b_host, v_host) if h is not None)
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        for dst, src in ((w_dev, w_host), (b_dev, b_host), (v_dev, v_host)):
+            if src is not None:
+                dst.copy_(src, non_blocking=True)
+        head, tail = x_dev[..., :d], x_dev[..., d:]
+        if cfg['op'] == 'avey':
+            o = avey(tail, w_dev, z_tl=head, bias=b_dev, valid=v_dev)
+        else:
+            o = avey_b(tail, z_tl=head, bias=b_dev, valid=v_dev)
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_value = tokens_per_step / (e2e_ms / 1e3)
+
+    # Roofline of the dominant (only) kernel.
+    nbytes, flops = algorithmic(cfg, batch, sets[0]['valid'])
+    t_launch = ms_step / 1e3
+    gbs = nbytes / t_launch / 1e9
+    tflops = flops / t_launch / 1e12
+    hbm_time = nbytes / (peaks['hbm_gbs'] * 1e9)
+    tc_time = flops / (peaks['bf16_tflops'] * 1e12)
+    bound = 'hbm' if hbm_time >= tc_time else 'tensor'
+    traffic = None
+    prof = ROOT / 'profiles' / 'traffic.json'
+    if prof.exists():
+        entry = json.loads(prof.read_text()).get(args.config, {})
+        if entry.get('kernel') == kernel_name:
+            traffic = entry.get('dram_bytes_per_launch')
+    if bound == 'hbm':
+        roof = {'bound': 'hbm', 'achieved': gbs, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
+                'frac': gbs / peaks['hbm_gbs']}
+    else:
+        roof = {'bound': 'tensor', 'achieved': tflops, 'peak': peaks['bf16_tflops'],
+                'unit': 'TFLOP/s', 'frac': tflops / peaks['bf16_tflops']}
+    roof.update({'traffic': traffic, 'kernel': kernel_name, 'peak_source': peaks['source'],
+                 'algorithmic_bytes': nbytes, 'useful_flops': flops,
+                 'hbm_frac': gbs / peaks['hbm_gbs'], 'tensor_frac': tflops / peaks['bf16_tflops'],
+                 'tensor_tflops': tflops, 'binding_floor_us': 1e6 * max(hbm_time, tc_time),
+                 'binding_frac': max(hbm_time, tc_time) / t_launch})
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu_value, cpu_steps, cpu_busy = time_cpu_port(cfg, seconds=args.cpu_seconds, rows=1)
+        cpu = {'value': cpu_value, 'unit': UNIT, 'cores': cpu_threads(), 'kind': 'port',
+               'sample': f'{cpu_steps} runs of 1 batch row ({cfg["n"]} tokens) of {args.config}, '
+                         f'{cpu_busy:.1f} s, fp32 NumPy port of avey_kernels/ops.py::_reference'}
+
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms_step,
+            'higher_is_better': True, 'scaling': cfg['scaling'], 'vs_baseline': None,
+            'dtype': 'bf16', 'data': 'synthetic (seeded randn, BASELINE config shapes)',
+            'config': {'workload': f'{args.config}: {cfg["desc"]}', 'context': cfg['n'],
+                       'features': cfg['d'], 'batch_per_gpu': batch,
+                       'global_batch': batch * world, 'parallelism': f'dp{world} (batch shards)',
+                       'l2': f'inputs rotate over {nsets} sets of '
+                             f'{nsets * sets[0]["x"].numel() * 2 / 1e6:.0f} MB total > 126 MB L2',
+                       'timing': 'CUDA graphs replayed between CUDA events, max over ranks'},
+            'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': h2d * world,
+                    'd2h_bytes_per_step': d2h * world, 'ms_per_step': e2e_ms,
+                    'api': f'avey_kernel_b200.{cfg["op"]} (pinned host buffers)'},
+            'roofline': roof,
+            'cpu_baseline': cpu,
+            'clocks': clocks.summary(),
+            'gpu_launches': gpu_launches * world,
+            'verify': {'max_norm_rel_err_vs_oracle': verify_err, 'rows_per_rank': 2,
+                       'tolerance': 2e-2},
+            'wall_s': time.perf_counter() - t0,
+        }
+        print(json.dumps(line), flush=True)
+    del graphs, keep
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=3000)
+    ap.add_argument('--warmup', type=int, default=10)
+    ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    ap.add_argument('--config', choices=tuple(CONFIGS), default='c2')
+    ap.add_argument('--cpu-seconds', type=float, default=10.0)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    if args.steps < 1 or args.warmup < 0:
+        ap.error('--steps must be >= 1 and --warmup >= 0')
+    world, _, _ = rank_env()
+    if world != args.gpus and args.impl == 'ours':
+        ap.error(f'--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun')
+    cfg = CONFIGS[args.config]
+    if args.impl == 'reference':
+        return run_reference(args, cfg)
+    return run_ours(args, cfg)
+
+
+if __name__ == '__main__':
+    sys.exit(main())

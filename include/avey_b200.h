@@ -13,7 +13,9 @@
  * strides and sizes, no framework types. It never throws; every entry point
  * returns an AveyStatus and avey_last_error() describes the last failure on
  * the calling thread. Calls only enqueue work on the given stream: they do not
- * synchronise and do not allocate, so they can be captured in a CUDA graph.
+ * synchronise and do not allocate (scratch memory, when a kernel needs it, is
+ * passed in by the caller as `workspace`), so they can be captured in a CUDA
+ * graph.
  */
 #ifndef AVEY_B200_H
 #define AVEY_B200_H
@@ -24,7 +26,7 @@
 extern "C" {
 #endif
 
-#define AVEY_ABI_VERSION 1
+#define AVEY_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define AVEY_API __attribute__((visibility("default")))
@@ -99,12 +101,15 @@ typedef struct AveyFwdParams {
   int32_t normalize;  /* divide by the signed row sum + eps (Avey-B) */
   int32_t activation; /* AveyActivation */
   int32_t kernel;     /* AveyKernel */
+  void* workspace;          /* device scratch, >= avey_fwd_workspace_size() bytes */
+  uint64_t workspace_bytes; /* size of `workspace` in bytes */
 } AveyFwdParams;
 
 /* What avey_fwd_v1 would launch for these parameters. */
 typedef struct AveyPlan {
   int32_t kernel;        /* AVEY_KERNEL_SIMT or AVEY_KERNEL_TCGEN05 */
-  int32_t launches;      /* kernel launches per call */
+  int32_t launches;      /* kernel launches per call (2 on the tcgen05 path:
+                            the row-norm pre-pass and the fused kernel) */
   int32_t grid;          /* CTAs of the main launch */
   int32_t block;         /* threads per CTA of the main launch */
   int32_t smem_bytes;    /* dynamic shared memory per CTA */
@@ -125,6 +130,12 @@ AVEY_API int avey_fwd_v1(const AveyFwdParams* params, void* stream);
 /* Fill *plan with the launch avey_fwd_v1 would make; launches nothing.
  * Has no reference counterpart (introspection for tests and benchmarks). */
 AVEY_API int avey_fwd_plan(const AveyFwdParams* params, AveyPlan* plan);
+
+/* Device workspace avey_fwd_v1 needs for these parameters, in bytes: 4 per row
+ * of z_tr (batch x context) for the tcgen05 kernel, 0 for the CUDA-core kernel.
+ * The reference allocates its normalisation buffer itself (ops.py:113); this
+ * library leaves allocation to the caller. Launches nothing. */
+AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* bytes);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */
 AVEY_API const char* avey_last_error(void);

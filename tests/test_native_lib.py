@@ -22,7 +22,7 @@ def header_functions():
 
 def test_library_loads_and_reports_abi_version():
     dll = _native.lib()
-    assert dll.avey_abi_version() == _native.ABI_VERSION == 1
+    assert dll.avey_abi_version() == _native.ABI_VERSION == 2
 
 
 def test_every_header_function_is_exported():
@@ -83,7 +83,7 @@ def test_plan_chooses_tcgen05_for_aligned_16bit_inputs():
     z = torch.randn(4, 512, 768).to(torch.bfloat16)
     plan = ops.plan(z, torch.randn(512, 512).to(torch.bfloat16), z_tl=z)
     assert plan.kernel == _native.KERNEL_TCGEN05 and plan.reason == 0
-    assert plan.grid == 4 * 4 and plan.block == 384
+    assert plan.grid == 4 * 4 and plan.block == 384 and plan.launches == 2
     assert 200_000 < plan.smem_bytes <= 232_448
 
 
@@ -119,5 +119,17 @@ def test_ctypes_struct_matches_header_field_order():
     names = re.findall(r'\b(\w+)\s*[;,]', re.sub(r'/\*.*?\*/', '', body, flags=re.S))
     names = [n for n in names if n not in ('AveyFwdParams',)]
     assert names == [f for f, _ in _native.AveyFwdParams._fields_]
-    # The library rejects any other size (test_struct_size_guard); 184 bytes on LP64.
-    assert ctypes.sizeof(_native.AveyFwdParams) == 184
+    # The library rejects any other size (test_struct_size_guard); 200 bytes on LP64.
+    assert ctypes.sizeof(_native.AveyFwdParams) == 200
+
+
+def test_workspace_size_is_four_bytes_per_row_on_the_tcgen05_path():
+    z = torch.randn(3, 384, 256).to(torch.bfloat16)
+    out = torch.empty_like(z)
+    p = ops.build_params(z, None, None, None, None, out, eps=1e-6, norm_eps=1e-12, causal=False,
+                         normalize=True, activation_id=0)
+    assert _native.workspace_size(p) == 3 * 384 * 4
+    z32 = z.float()
+    p = ops.build_params(z32, None, None, None, None, z32.clone(), eps=1e-6, norm_eps=1e-12,
+                         causal=False, normalize=True, activation_id=0)
+    assert _native.workspace_size(p) == 0
