@@ -22,8 +22,9 @@ STATUS_NAMES = {
 }
 
 # Exported symbols, mirrored from include/avey_b200.h (tests check the header).
-EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_fwd_workspace_size', 'avey_last_error',
-           'avey_device_status', 'avey_launch_count', 'avey_abi_version')
+EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_fwd_workspace_size', 'avey_fwd_noalloc_v1',
+           'avey_last_error', 'avey_device_status', 'avey_launch_count', 'avey_abi_version')
+NOALLOC_MAX_ROWS = 1 << 20
 ABI_VERSION = 2
 
 
@@ -109,6 +110,8 @@ def lib() -> ctypes.CDLL:
         dll.avey_fwd_workspace_size.argtypes = [ctypes.POINTER(AveyFwdParams),
                                                 ctypes.POINTER(ctypes.c_uint64)]
         dll.avey_fwd_workspace_size.restype = ctypes.c_int
+        dll.avey_fwd_noalloc_v1.argtypes = [ctypes.POINTER(AveyFwdParams), ctypes.c_void_p]
+        dll.avey_fwd_noalloc_v1.restype = ctypes.c_int
         dll.avey_last_error.argtypes = []
         dll.avey_last_error.restype = ctypes.c_char_p
         dll.avey_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
@@ -131,6 +134,11 @@ def _check(status: int) -> None:
 
 def forward(params: AveyFwdParams, stream: int) -> None:
     _check(lib().avey_fwd_v1(ctypes.byref(params), ctypes.c_void_p(stream)))
+
+
+def forward_noalloc(params: AveyFwdParams, stream: int) -> None:
+    """avey_fwd_noalloc_v1: like forward() but with the library's own scratch."""
+    _check(lib().avey_fwd_noalloc_v1(ctypes.byref(params), ctypes.c_void_p(stream)))
 
 
 def plan(params: AveyFwdParams) -> AveyPlan:

@@ -359,6 +359,52 @@ int avey_fwd_v1(const AveyFwdParams* p, void* stream_ptr) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// No-allocation entry point: scratch in a file-scope device array.
+}  // extern "C"
+
+namespace {
+
+// One float (row sum of squares) per row of z_tr. Host code must not use the
+// name as a device address; its address comes from cudaGetSymbolAddress.
+__device__ __align__(256) float g_noalloc_sumsq[AVEY_NOALLOC_MAX_ROWS];
+
+constexpr int kMaxDevices = 64;
+std::once_flag g_noalloc_once[kMaxDevices];
+void* g_noalloc_ptr[kMaxDevices];
+cudaError_t g_noalloc_err[kMaxDevices];
+
+}  // namespace
+
+extern "C" {
+
+int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
+  AveyPlan plan;
+  int rc = avey_fwd_plan(p, &plan);
+  if (rc != AVEY_OK) return rc;
+  const uint64_t rows = static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context);
+  if (rows > AVEY_NOALLOC_MAX_ROWS)
+    return fail(AVEY_ERR_ARGUMENT,
+                "batch x context = %llu rows exceeds the no-allocation limit of %u rows",
+                (unsigned long long)rows, AVEY_NOALLOC_MAX_ROWS);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(AVEY_ERR_CUDA, "cannot determine the current device");
+  // Once per device, with that device current: the array's device address.
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* ptr = nullptr;
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&ptr, g_noalloc_sumsq);
+    g_noalloc_ptr[dev] = g_noalloc_err[dev] == cudaSuccess ? ptr : nullptr;
+  });
+  if (g_noalloc_err[dev] != cudaSuccess || !g_noalloc_ptr[dev])
+    return fail(AVEY_ERR_CUDA, "cudaGetSymbolAddress(no-allocation scratch): %s",
+                cudaGetErrorString(g_noalloc_err[dev]));
+  AveyFwdParams q = *p;
+  q.workspace = g_noalloc_ptr[dev];
+  q.workspace_bytes = static_cast<uint64_t>(AVEY_NOALLOC_MAX_ROWS) * sizeof(float);
+  return avey_fwd_v1(&q, stream);
+}
+
 const char* avey_last_error(void) { return g_last_error.c_str(); }
 
 int avey_device_status(uint32_t* flags, int clear) {

@@ -137,6 +137,27 @@ AVEY_API int avey_fwd_plan(const AveyFwdParams* params, AveyPlan* plan);
  * library leaves allocation to the caller. Launches nothing. */
 AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* bytes);
 
+/*
+ * avey_fwd_v1 for callers that cannot allocate device memory: no counterpart
+ * in the reference. Some callers hold no device allocator of their own -- an
+ * FFI host (cgo, JNI, a plugin ABI) that only passes raw pointers in, or code
+ * that runs while a stream is being captured into a CUDA graph, where
+ * allocation is not allowed -- so they cannot provide `workspace`. This entry
+ * point ignores params->workspace and uses a scratch array that lives inside
+ * the library instead (file-scope device memory, present on every GPU that
+ * loads the library until the process exits). It allocates nothing.
+ *
+ * Limit: batch * context <= AVEY_NOALLOC_MAX_ROWS (1,048,576 rows; the
+ * array holds one float per row, 4 MiB per GPU); larger inputs are rejected
+ * with AVEY_ERR_ARGUMENT. The first call on each device looks up the array's
+ * device address (with that device current); make that first call before
+ * any stream capture. All calls share the one array, so calls whose kernels
+ * overlap on the GPU (for example on two streams) race; each call rewrites
+ * every row it reads, so nothing needs clearing between calls.
+ */
+#define AVEY_NOALLOC_MAX_ROWS (1u << 20)
+AVEY_API int avey_fwd_noalloc_v1(const AveyFwdParams* params, void* stream);
+
 /* Message for the last non-OK status returned on this thread ("" if none). */
 AVEY_API const char* avey_last_error(void);
 

@@ -1,0 +1,90 @@
+"""avey_fwd_noalloc_v1: the entry point for callers that cannot allocate.
+
+Some callers hold no device allocator of their own (an FFI host that only
+hands raw pointers over, or code running while a stream is captured into a
+CUDA graph, where allocation is not allowed). For them the library keeps its
+scratch -- one float per row of z_tr -- in an array of its own, up to
+AVEY_NOALLOC_MAX_ROWS rows. These tests call that entry point through the C
+ABI and check it against avey_fwd_v1 (which takes the scratch from the
+caller), on two calls in a row: the second call finds the first call's sums
+still in the shared array and must not depend on them.
+
+This file is collected last on purpose, so a run that stops at the first
+failure has already run every other test.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from avey_kernel_b200 import _native, ops
+from helpers import TOL, norm_rel_err, to_numpy
+
+
+def _call(z_tr, v, z_tl, bias, valid, *, causal, normalize, act, noalloc):
+    out = torch.empty(z_tr.shape, dtype=z_tr.dtype, device=z_tr.device)
+    params = ops.build_params(z_tr, v, z_tl, bias, valid, out, eps=1e-6, norm_eps=1e-12,
+                              causal=causal, normalize=normalize, activation_id=act)
+    stream = torch.cuda.current_stream().cuda_stream
+    if noalloc:
+        _native.forward_noalloc(params, stream)  # params.workspace stays NULL
+    else:
+        nbytes = _native.workspace_size(params)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=z_tr.device)
+        params.workspace = ws.data_ptr()
+        params.workspace_bytes = nbytes
+        _native.forward(params, stream)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.gpu
+def test_noalloc_entry_point_matches_the_workspace_entry_point_on_two_calls():
+    g = torch.Generator().manual_seed(11)
+    cases = [
+        # Avey causal, bf16, BASELINE-config-2-like (tcgen05 path, uses scratch)
+        dict(b=8, n=512, d=768, causal=True, normalize=False, act=0, weight=True, mask=False),
+        # Avey-B, bf16, ragged padding, gelu -- fewer rows than the first call,
+        # so the array still holds the first call's sums past these rows
+        dict(b=3, n=384, d=256, causal=False, normalize=True, act=4, weight=False, mask=True),
+    ]
+    for c in cases:
+        x = torch.randn(c['b'], c['n'], 2 * c['d'], generator=g).to(torch.bfloat16).cuda()
+        head, tail = x[..., :c['d']], x[..., c['d']:]
+        v = ((torch.randn(c['n'], c['n'], generator=g) * 0.02).to(torch.bfloat16).cuda()
+             if c['weight'] else None)
+        valid = None
+        if c['mask']:
+            lengths = torch.randint(c['n'] // 4, c['n'] + 1, (c['b'],), generator=g)
+            valid = (torch.arange(c['n'])[None, :] < lengths[:, None]).cuda()
+        plan = ops.plan(tail, v, head, None, valid, causal=c['causal'], normalize=c['normalize'])
+        assert plan.kernel == _native.KERNEL_TCGEN05
+        kw = dict(causal=c['causal'], normalize=c['normalize'], act=c['act'])
+        want = _call(tail, v, head, None, valid, noalloc=False, **kw)
+        got = _call(tail, v, head, None, valid, noalloc=True, **kw)
+        assert np.isfinite(to_numpy(got)).all()
+        assert norm_rel_err(to_numpy(got), to_numpy(want)) <= TOL['bfloat16']
+        # Same kernels, same arithmetic: the results agree bit for bit.
+        assert torch.equal(got, want)
+    assert _native.device_status(clear=True) == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_entry_point_on_the_cuda_core_path():
+    z = torch.rand(2, 35, 37, device='cuda')
+    want = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=False)
+    got = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=True)
+    assert norm_rel_err(to_numpy(got), to_numpy(want)) <= TOL['float32']
+
+
+def test_noalloc_entry_point_rejects_inputs_beyond_its_limit():
+    # 2 x 524289 rows is one past the limit; rejected before anything launches.
+    rows = _native.NOALLOC_MAX_ROWS + 2
+    z = torch.empty(2, rows // 2, 8, dtype=torch.bfloat16)
+    out = torch.empty_like(z)
+    params = ops.build_params(z, None, None, None, None, out, eps=1e-6, norm_eps=1e-12,
+                              causal=False, normalize=True, activation_id=0)
+    before = _native.launch_count()
+    with pytest.raises(_native.NativeError, match='no-allocation limit'):
+        _native.forward_noalloc(params, 0)
+    assert _native.launch_count() == before
