@@ -121,27 +121,24 @@ struct TcLayout {
   int smem;
 };
 
-// Shared memory: [P region | phase-C ring | control block]. The phase-A
-// stages (query chunk + every key tile's chunk, 16 KB each) live in the P
-// region and the ring; phase B writes P (16 KB per 64 keys) into the P region.
+// Shared memory: [phase-C ring | output staging | control block]. The phase-A
+// stages (query chunk + every key tile's chunk, 16 KB each) use the ring's
+// space before phase C; P itself lives in tensor memory.
 TcLayout tc_layout(const AveyFwdParams* p) {
   TcLayout l{};
   const int ctx = static_cast<int>(p->context);
   const int nk_max = (ctx + 127) / 128;
-  l.geom.p_bytes = nk_max * 2 * avey::kTcPChunkBytes;
-  const int room =
-      kMaxDynSmem - 1024 - avey::kTcCtrlBytes - avey::kTcOutStageBytes - l.geom.p_bytes;
+  const int room = kMaxDynSmem - 1024 - avey::kTcCtrlBytes - avey::kTcOutStageBytes;
   int nslot = room / avey::kTcUnitBytes;
   if (nslot > avey::kTcMaxSlots) nslot = avey::kTcMaxSlots;
   l.geom.nslot = nslot;
-  // Phase-A stages use the P region and the phase-C ring together.
+  // Phase-A stages use the space of the phase-C ring.
   l.geom.a_stage_bytes = (1 + nk_max) * avey::kTcTileBytesA;
-  int nst = (l.geom.p_bytes + nslot * avey::kTcUnitBytes) / l.geom.a_stage_bytes;
+  int nst = (nslot * avey::kTcUnitBytes) / l.geom.a_stage_bytes;
   if (nst > avey::kTcMaxStages) nst = avey::kTcMaxStages;
   l.geom.a_nstage = nst;
   l.geom.n_qtiles = nk_max;
-  l.smem = 1024 + l.geom.p_bytes + nslot * avey::kTcUnitBytes + avey::kTcOutStageBytes +
-           avey::kTcCtrlBytes;
+  l.smem = 1024 + nslot * avey::kTcUnitBytes + avey::kTcOutStageBytes + avey::kTcCtrlBytes;
   return l;
 }
 

@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(kPrepassThreads) norm_prepass(const FwdArgs ar
   const int nwarps = (gridDim.x * kPrepassThreads) >> 5;
   const int rows = args.batch * args.ctx;
   const int nvec = args.feat / 8;  // 16-byte vectors per row (feat % 8 == 0 here)
+  const uint64_t keep = l2_policy_evict_last();  // the fused kernel reads z_tr next
   for (int r = warp; r < rows; r += nwarps) {
     const int b = r / args.ctx, n = r - b * args.ctx;
     const uint4* row = reinterpret_cast<const uint4*>(static_cast<const T*>(args.z_tr) +
@@ -31,7 +32,7 @@ __global__ void __launch_bounds__(kPrepassThreads) norm_prepass(const FwdArgs ar
                                                       static_cast<int64_t>(n) * args.zr_rs);
     float s = 0.f;
     for (int v = lane; v < nvec; v += 32) {
-      const uint4 q = __ldg(row + v);
+      const uint4 q = ld_global_nc_v4_hint(row + v, keep);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {

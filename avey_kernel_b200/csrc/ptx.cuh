@@ -122,6 +122,21 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// L2 eviction-priority policies for the .L2::cache_hint forms below. Data read
+// again soon (z_tr, V) is kept with evict_last; data touched once (the gate,
+// the output) keeps the normal priority -- marking it evict_first measured
+// slower on B200 than leaving it alone.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // 3-D tiled load of one box into shared memory; completion is signalled as
 // transaction bytes on `bar`. x (the innermost coordinate) must be a multiple
 // of 16 bytes worth of elements.
@@ -133,6 +148,23 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
+// The same with an L2 eviction policy.
+__device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void* tmap, uint32_t bar,
+                                                 int x, int y, int z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+// 16-byte read-only global load with an L2 eviction policy.
+__device__ __forceinline__ uint4 ld_global_nc_v4_hint(const void* ptr, uint64_t policy) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr), "l"(policy));
+  return v;
+}
 
 // Bring [src, src + bytes) into L2 without a destination (16-byte aligned
 // address, size a multiple of 16).
@@ -142,12 +174,14 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
                : "memory");
 }
 
-// 3-D tiled store of one box from shared memory (bulk-group completion).
-__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int x, int y, int z) {
+// 3-D tiled store of one box from shared memory (bulk-group completion), with
+// an L2 eviction policy.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int x, int y, int z,
+                                             uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
-          reinterpret_cast<uint64_t>(tmap)),
-      "r"(x), "r"(y), "r"(z), "r"(src)
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+      " [%0, {%1, %2, %3}], [%4], %5;" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+      "r"(x), "r"(y), "r"(z), "r"(src), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() {
@@ -197,6 +231,18 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]: A is M x K in TMEM (lane = row, two 16-bit
+// elements per 32-bit column, the lower K index in the low half).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op issued so far by this thread is done.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile(
@@ -217,6 +263,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+
+// Each thread of the warp writes 16 consecutive 32-bit columns of its own TMEM
+// lane (lane = 32 * (warp % 4) + laneid).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() {

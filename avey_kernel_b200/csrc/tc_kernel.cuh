@@ -5,8 +5,8 @@
 // the similarity matrix on chip:
 //
 //  A. Gram phase. TMA streams 64-feature chunks of the query tile and of every
-//     needed key tile (128-byte swizzle) into chunk stages that live in the P
-//     region and the phase-C ring (both unused until later). The MMA warp
+//     needed key tile (128-byte swizzle) into chunk stages that live in the
+//     space of the phase-C ring (unused until phase C). The MMA warp
 //     accumulates the raw Gram block G = Z_q Z_k^T (fp32) in TMEM, two key
 //     tiles per MMA (N = 256), up to 512 keys = all 512 TMEM columns. The L2
 //     normalisation is applied to G in phase B from per-row sums of squares
@@ -16,15 +16,16 @@
 //  B. P phase. The compute warps read G from TMEM (thread = query row), form
 //     P = G * rinv_i * rinv_j * V[i, j] under the causal / padding masks
 //     (select, so NaN padding cannot leak), accumulate the signed row sum for
-//     Avey-B in fp32, and write P as bf16 / f16 into the P region in the
-//     K-major 128-byte-swizzle layout the tensor core reads. P never reaches
-//     global memory.
-//  C. Mix phase. TMA streams z_tr again as 32-key x 256-feature units (MN-major
-//     B operand, 128-byte swizzle) through a ring that is filled during phase
-//     A already. The MMA warp computes O = P Z for 256-feature slices into two
-//     TMEM buffers (256 columns each, reusing the Gram columns). The compute
-//     warps drain each slice: divide by (den + eps), add the bias, apply the
-//     activation, multiply by the gate, zero padded rows, store.
+//     Avey-B in fp32, and write P back into TMEM as packed bf16 / f16 pairs
+//     (tcgen05.st), over Gram columns the same thread has already read. P never
+//     leaves the tensor memory.
+//  C. Mix phase. TMA streams z_tr again as 64-key x 128-feature units (MN-major
+//     B operand, 128-byte swizzle) through a 12-slot ring. The MMA warp computes
+//     O = P Z with P read from TMEM (tcgen05.mma A-from-TMEM) for 128-feature
+//     slices into two 128-column TMEM buffers. The compute warps drain each
+//     slice: divide by (den + eps), add the bias, apply the activation,
+//     multiply by the gate, zero padded rows, and write the tile through
+//     shared memory with a TMA tensor store.
 //
 // Roles: warp 0 issues TMA (and L2 prefetches of the item's V rows and gate
 // rows), warp 1 owns TMEM and issues MMAs, warps 4-11 are the compute warps
@@ -50,26 +51,37 @@ namespace avey {
 
 constexpr int kTcThreads = 384;
 constexpr int kTcMaxKeys = 512;      // keys per work item (TMEM holds 512 fp32 columns)
-constexpr int kTcUnitBytes = 32768;  // one phase-C ring slot (64 keys x 256 features)
+constexpr int kTcUnitBytes = 16384;  // one phase-C ring slot (64 keys x 128 features)
 constexpr int kTcUnitKeys = 64;      // keys per phase-C unit
-constexpr int kTcPChunkBytes = 16384; // P for 64 keys x 128 rows (bf16 / f16)
+constexpr int kTcSliceCols = 128;    // output features per phase-C slice (TMEM buffer)
 constexpr int kTcOutTileBytes = 2048; // one warp's 32 x 32 output staging tile
 constexpr int kTcOutStageBytes = 8 * kTcOutTileBytes;
 constexpr int kTcZBoxBytes = 8192;   // one {64 features x 64 keys} box of a unit
-constexpr int kTcMaxSlots = 8;
+constexpr int kTcMaxSlots = 12;
 constexpr int kTcMaxStages = 8;
 constexpr int kTcChunk = 64;                      // phase-A feature chunk (128-byte rows)
 constexpr int kTcTileBytesA = 128 * kTcChunk * 2; // one 128-row tile of a chunk (16 KB)
 constexpr int kTcMaxFeatures = 2048;  // bias staged in shared memory
-constexpr int kTcCtrlBytes = 12288;
+constexpr int kTcCtrlBytes = 13312;
 
 struct TcGeom {
   int nslot;          // phase-C ring slots
-  int p_bytes;        // bytes of the P region (16 KB per 64 keys)
   int n_qtiles;       // query tiles per batch row
-  int a_nstage;       // phase-A stages inside the P region + phase-C ring
-  int a_stage_bytes;  // (1 + key tiles) x 8 KB
+  int a_nstage;       // phase-A stages inside the phase-C ring space
+  int a_stage_bytes;  // (1 + key tiles) x 16 KB
 };
+
+// TMEM column of the packed P pair holding key j (two keys per 32-bit column).
+// With three or four key tiles, keys below 256 pack into [0, 128) and the rest
+// into [256, 384): each warpgroup then writes only Gram columns it has already
+// read, and [128, 256) / [384, 512) hold the two O buffers. With one or two key
+// tiles P goes to [256, 384) and the O buffers to [0, 128) / [128, 256).
+__device__ __forceinline__ uint32_t p_col(int j, int nk) {
+  return nk >= 3 ? (j < 256 ? j >> 1 : 128 + (j >> 1)) : 256 + (j >> 1);
+}
+__device__ __forceinline__ uint32_t o_col(int buf, int nk) {
+  return nk >= 3 ? (buf ? 384u : 128u) : (buf ? 128u : 0u);
+}
 
 // Shared-memory control block.
 struct TcCtrl {
@@ -81,11 +93,11 @@ struct TcCtrl {
   int last_valid;
   int fix;
   int pad_[1];
-  float rinv[kTcMaxKeys];  // sums of squares, then inverse norms
+  alignas(16) float rinv[kTcMaxKeys];  // sums of squares, then inverse norms (read as float4)
   float den[2][128];
   uint32_t kbits[kTcMaxKeys / 32];
   uint8_t kvalid[kTcMaxKeys];
-  float bias[kTcMaxFeatures];
+  alignas(16) float bias[kTcMaxFeatures];  // read as float4
 };
 static_assert(sizeof(TcCtrl) <= kTcCtrlBytes, "control block too large");
 
@@ -145,11 +157,12 @@ __device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
 // 32 consecutive 16-bit elements starting at p into w[16] (p 16-byte aligned
 // when vec); elements at or past n_ok read as zero.
 template <typename T>
-__device__ __forceinline__ void load_raw32(const T* p, int n_ok, bool vec, uint32_t (&w)[16]) {
+__device__ __forceinline__ void load_raw32(const T* p, int n_ok, bool vec, uint32_t (&w)[16],
+                                           uint64_t policy) {
   if (vec && n_ok >= 32) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const uint4 v = ld_global_nc_v4(p + 8 * q);
+      const uint4 v = ld_global_nc_v4_hint(p + 8 * q, policy);
       w[4 * q] = v.x;
       w[4 * q + 1] = v.y;
       w[4 * q + 2] = v.z;
@@ -176,12 +189,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw_addr);
-  const uint32_t p_addr = base;  // P region; phase-A stages before phase B
-  const uint32_t ring_addr = base + static_cast<uint32_t>(geom.p_bytes);
-  // [P region | phase-C ring | output staging | control block]
+  // [phase-C ring (phase-A stages before it) | output staging | control block]
+  const uint32_t ring_addr = base;
+  const uint32_t stage_addr = base;
   const uint32_t out_stage_addr = ring_addr + static_cast<uint32_t>(geom.nslot * kTcUnitBytes);
-  TcCtrl* ctrl = reinterpret_cast<TcCtrl*>(base_ptr + geom.p_bytes + geom.nslot * kTcUnitBytes +
-                                           kTcOutStageBytes);
+  TcCtrl* ctrl = reinterpret_cast<TcCtrl*>(base_ptr + geom.nslot * kTcUnitBytes + kTcOutStageBytes);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -254,7 +266,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nkeys = args.causal ? min(kv_end, q_lo + 128) : kv_end;
   const int nk = skip ? 0 : (nkeys + 127) / 128;       // key tiles
   const int nchunk = (D + kTcChunk - 1) / kTcChunk;     // phase-A feature chunks
-  const int nslices = (D + 255) / 256;                  // output slices (phase C)
+  const int nslices = (D + kTcSliceCols - 1) / kTcSliceCols;  // output slices (phase C)
   const int nunits = skip ? 0 : (nkeys + kTcUnitKeys - 1) / kTcUnitKeys;  // units per slice
   const int units_c = nslices * nunits;
   const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
@@ -265,21 +277,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // barrier parities advance incrementally (no divisions in the hot loop).
     if (!skip) {
       const bool leader = lane == 0;
+      const uint64_t keep = l2_policy_evict_last();  // z_tr is read again (phase C, other CTAs)
       // Phase-A stage state.
       int a_st = 0, a_use = 0, c = 0;
       // Phase-C ring state.
       int c_slot = 0, c_use = 0, u = 0, sl = 0, uu = 0;
-      int nbox = (min(256, D) + 63) / 64;
+      int nbox = (min(kTcSliceCols, D) + 63) / 64;
       auto load_stage = [&]() {
         if (a_use > 0) mbar_wait(smem_u32(&ctrl->a_empty[a_st]), (a_use - 1) & 1);
         if (leader) AVEY_STAMP_UNIT(c, 0);
         if (leader) {
           const uint32_t full = smem_u32(&ctrl->a_full[a_st]);
-          const uint32_t st = p_addr + a_st * geom.a_stage_bytes;
+          const uint32_t st = stage_addr + a_st * geom.a_stage_bytes;
           mbar_arrive_expect_tx(full, (1 + nk) * kTcTileBytesA);
-          tma_load_3d(st, &map_q, full, c * kTcChunk, q_lo, b);
+          tma_load_3d_hint(st, &map_q, full, c * kTcChunk, q_lo, b, keep);
           for (int t = 0; t < nk; ++t)
-            tma_load_3d(st + (1 + t) * kTcTileBytesA, &map_q, full, c * kTcChunk, t * 128, b);
+            tma_load_3d_hint(st + (1 + t) * kTcTileBytesA, &map_q, full, c * kTcChunk, t * 128, b,
+                             keep);
         }
         __syncwarp();
         ++c;
@@ -296,24 +310,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t dst = ring_addr + c_slot * kTcUnitBytes;
           mbar_arrive_expect_tx(full, nbox * kTcZBoxBytes);
           for (int i = 0; i < nbox; ++i)
-            tma_load_3d(dst + i * kTcZBoxBytes, &map_z, full, sl * 256 + i * 64, uu * kTcUnitKeys, b);
+            tma_load_3d_hint(dst + i * kTcZBoxBytes, &map_z, full, sl * kTcSliceCols + i * 64,
+                             uu * kTcUnitKeys, b, keep);
         }
         __syncwarp();
         ++u;
         if (++uu == nunits) {
           uu = 0;
           ++sl;
-          nbox = (min(256, D - sl * 256) + 63) / 64;
+          nbox = (min(kTcSliceCols, D - sl * kTcSliceCols) + 63) / 64;
         }
         if (++c_slot == nslot) {
           c_slot = 0;
           ++c_use;
         }
       };
-      // Phase-A stages span the P region and the phase-C ring, so the ring is
-      // filled only once every stage has been released for the last time (the
-      // MMA warp is done with it); phase B, which writes P into the low part of
-      // the same space, overlaps the first ring loads.
+      // Phase-A stages occupy the ring space, so the ring is filled only once
+      // every stage has been released for the last time (the MMA warp is done
+      // with it); the first ring loads overlap phase B.
       while (c < nchunk) load_stage();
       {
         // Final release of every stage slot s: its last use is use index
@@ -331,7 +345,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool leader = lane == 0;
       // Descriptors are advanced by adding (byte offset >> 4) to the start
       // address field; every address stays below 2^18, so nothing carries out.
-      const uint64_t dq0 = smem_desc_sw128(p_addr, 16, 1024);
+      const uint64_t dq0 = smem_desc_sw128(stage_addr, 16, 1024);
       const uint32_t stage_adv = static_cast<uint32_t>(geom.a_stage_bytes) >> 4;
       const uint32_t idesc_g256 = idesc_f16(fmt, 128, 256, 0, 0);
       const uint32_t idesc_g128 = idesc_f16(fmt, 128, 128, 0, 0);
@@ -373,7 +387,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       if (leader) AVEY_STAMP(3);  // P observed by the MMA warp
       const bool fix = ctrl->fix != 0;
-      const uint64_t dp0 = smem_desc_sw128(p_addr, 16, 1024);
       const uint64_t dz0 = smem_desc_sw128(ring_addr, kTcZBoxBytes, 1024);
       int slot = 0;
       ph = 0;
@@ -383,22 +396,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           mbar_wait(smem_u32(&ctrl->o_empty[buf]), ((s >> 1) - 1) & 1);
           tc_fence_after();
         }
-        const int width = min(256, D - s * 256);
+        const int width = min(kTcSliceCols, D - s * kTcSliceCols);
         const uint32_t idesc_o = idesc_f16(fmt, 128, static_cast<uint32_t>((width + 15) & ~15), 0, 1);
-        const uint32_t d_tmem = tmem + buf * 256;
+        const uint32_t d_tmem = tmem + o_col(buf, nk);
         for (int uu = 0; uu < nunits; ++uu) {
           mbar_wait(smem_u32(fix ? &ctrl->fixed[slot] : &ctrl->full[slot]), ph);
           tc_fence_after();
           if (leader) AVEY_STAMP_UNIT(128 + s * nunits + uu, 1);
           if (leader) {
-            // P keys 64 uu .. +63 are P chunk uu (16 KB, K-major); K steps of 16
-            // keys advance 32 bytes in P and 16 rows (2 KB) in the Z unit.
-            const uint64_t dp = dp0 + uu * (kTcPChunkBytes >> 4);
+            // P keys 64 uu .. +63 start at TMEM column p_col(64 uu); K steps of
+            // 16 keys advance 8 columns of P and 16 rows (2 KB) of the Z unit.
+            const uint32_t a_tmem = tmem + p_col(uu * kTcUnitKeys, nk);
             const uint64_t dz = dz0 + slot * (kTcUnitBytes >> 4);
 #pragma unroll
             for (int k = 0; k < kTcUnitKeys / 16; ++k)
-              tc_mma_f16(d_tmem, dp + 2 * k, dz + k * (2048 >> 4), idesc_o,
-                         (uu != 0 || k != 0) ? 1u : 0u);
+              tc_mma_f16_ts(d_tmem, a_tmem + 8 * k, dz + k * (2048 >> 4), idesc_o,
+                            (uu != 0 || k != 0) ? 1u : 0u);
             tc_commit(smem_u32(&ctrl->empty[slot]));
             AVEY_STAMP_UNIT(128 + s * nunits + uu, 2);
           }
@@ -477,7 +490,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       named_bar_sync(1, 256);
 
-      // ---------------- phase B: P = G * rinv_i * rinv_j * V, masked, into smem
+      // ---------------- phase B: P = G * rinv_i * rinv_j * V, masked, into TMEM
       mbar_wait(smem_u32(&ctrl->s_full), 0);
       tc_fence_after();
       if (cw == 0 && lane == 0) AVEY_STAMP(6);  // Gram complete
@@ -486,25 +499,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const T* vrow = (args.has_v && i < C) ? static_cast<const T*>(args.v) + static_cast<int64_t>(i) * args.v_rs
                                             : nullptr;
       const bool v_vec = (reinterpret_cast<uintptr_t>(args.v) & 15u) == 0 && (args.v_rs & 7) == 0;
+      const uint64_t keep = l2_policy_evict_last();    // V: read by every batch row
+      const uint64_t stream = l2_policy_evict_normal(); // gate and output: touched once
       float den = 0.f;
       {
-        const int c_begin = h * nk * 64;
-        const int nch = nk * 2;
+        // Key ranges of the two warpgroups (see p_col): with three or four key
+        // tiles warpgroup 0 takes keys [0, 256) and warpgroup 1 the rest.
+        const int split = nk >= 3 ? 256 : nk * 64;
+        const int c_begin = h ? split : 0;
+        const int nch = ((h ? nk * 128 : split) - c_begin) / 32;
         // V without a weight matrix is 1.0 everywhere (packed 16-bit ones).
         const uint32_t one2 = pack2<T>(1.f, 1.f);
         uint32_t vw[16], vn[16], vnn[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) vw[q] = vn[q] = vnn[q] = one2;
         if (vrow) {
-          load_raw32<T>(vrow + c_begin, C - c_begin, v_vec, vw);
-          if (nch > 1) load_raw32<T>(vrow + c_begin + 32, C - c_begin - 32, v_vec, vn);
+          load_raw32<T>(vrow + c_begin, C - c_begin, v_vec, vw, keep);
+          if (nch > 1) load_raw32<T>(vrow + c_begin + 32, C - c_begin - 32, v_vec, vn, keep);
         }
 #pragma unroll 1
         for (int ch = 0; ch < nch; ++ch) {
           const int c0 = c_begin + ch * 32;
           uint32_t g[32];
           tmem_ld32(tmem + lane_off + c0, g);
-          if (vrow && ch + 2 < nch) load_raw32<T>(vrow + c0 + 64, C - c0 - 64, v_vec, vnn);
+          if (vrow && ch + 2 < nch) load_raw32<T>(vrow + c0 + 64, C - c0 - 64, v_vec, vnn, keep);
           // Allowed keys of this chunk: valid, below nkeys, and j <= i if causal.
           uint32_t okb = row_ok ? ctrl->kbits[c0 >> 5] : 0u;
           if (args.causal) {
@@ -529,13 +547,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             pk[2 * q] = pack2<T>(pv[0], pv[1]);
             pk[2 * q + 1] = pack2<T>(pv[2], pv[3]);
           }
-          const uint32_t chunk = p_addr + (c0 >> 6) * kTcPChunkBytes + row * 128;
-          const int ubase = (c0 & 63) >> 3;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int phys = (ubase + q) ^ (row & 7);
-            st_shared_v4(chunk + phys * 16, pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
+          // Packed pairs into TMEM columns this thread has already read.
+          tmem_st16(tmem + lane_off + p_col(c0, nk), pk);
           if (vrow) {
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
@@ -546,7 +559,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       ctrl->den[h][row] = den;
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctrl->p_ready));
@@ -598,22 +611,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_3d(&map_o, stage_o, f0, q_lo + wq * 32, b);
+          tma_store_3d(&map_o, stage_o, f0, q_lo + wq * 32, b, stream);
           bulk_commit_group();
         }
       };
       auto drain = [&](int s, int buf, int s_next) {
         mbar_wait(smem_u32(&ctrl->o_full[buf]), (s >> 1) & 1);
         tc_fence_after();
-        const int width = min(256, D - s * 256);
+        const int width = min(kTcSliceCols, D - s * kTcSliceCols);
         const int nch_o = (width + 31) / 32;
-        const uint32_t tb = tmem + lane_off + buf * 256;
+        const uint32_t tb = tmem + lane_off + o_col(buf, nk);
         // Gate words of the chunk after `f0` (the rest of this slice, then the
         // first chunk of s_next), prefetched one chunk ahead.
         auto next_gate = [&](int ch, int f0) {
           if (zrow) {
-            const int fn = ch + 1 < nch_o ? f0 + 32 : (s_next < nslices ? s_next * 256 : -1);
-            if (fn >= 0) load_raw32<T>(zrow + fn, D - fn, zl_vec, gn);
+            const int fn = ch + 1 < nch_o ? f0 + 32 : (s_next < nslices ? s_next * kTcSliceCols : -1);
+            if (fn >= 0) load_raw32<T>(zrow + fn, D - fn, zl_vec, gn, stream);
           }
         };
         // TMEM loads run one chunk ahead of the math.
@@ -621,7 +634,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_ld32(tb, oa);
 #pragma unroll 1
         for (int ch = 0; ch < nch_o; ch += 2) {
-          const int f0 = s * 256 + ch * 32;
+          const int f0 = s * kTcSliceCols + ch * 32;
           tmem_wait_ld(oa);
           const bool has_b = ch + 1 < nch_o;
           if (has_b) tmem_ld32(tb + (ch + 1) * 32, ob);
@@ -644,7 +657,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (wq == 0 && lane == 0 && s < 6) AVEY_STAMP(8 + s);  // slice s drained
       };
       const int s_first = fix ? 0 : h;
-      if (zrow && s_first < nslices) load_raw32<T>(zrow + s_first * 256, D - s_first * 256, zl_vec, gn);
+      if (zrow && s_first < nslices)
+        load_raw32<T>(zrow + s_first * kTcSliceCols, D - s_first * kTcSliceCols, zl_vec, gn, stream);
       if (!fix) {
         for (int s = h; s < nslices; s += 2) drain(s, h, s + 2);
         if (lane == 0) bulk_wait_all();
@@ -657,7 +671,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int slot = 0, sl = 0, uu = 0;
         uint32_t ph = 0;
         for (int u = 0; u < units_c; ++u) {
-          const int nbox = (min(256, D - sl * 256) + 63) / 64;
+          const int nbox = (min(kTcSliceCols, D - sl * kTcSliceCols) + 63) / 64;
           mbar_wait(smem_u32(&ctrl->full[slot]), ph);
           // Warpgroup 1 (128 threads) covers the unit's nbox x 64 rows.
           for (int idx = wq * 32 + lane; idx < nbox * kTcUnitKeys; idx += 128) {
