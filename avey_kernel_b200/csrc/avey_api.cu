@@ -122,8 +122,8 @@ struct TcLayout {
 };
 
 // Shared memory: [phase-C ring | output staging | control block]. The phase-A
-// stages (query chunk + every key tile's chunk, 16 KB each) use the ring's
-// space before phase C; P itself lives in tensor memory.
+// stages (every key tile's chunk, 16 KB each; the query tile is one of the key
+// tiles) use the ring's space before phase C; P itself lives in tensor memory.
 TcLayout tc_layout(const AveyFwdParams* p) {
   TcLayout l{};
   const int ctx = static_cast<int>(p->context);
@@ -133,7 +133,7 @@ TcLayout tc_layout(const AveyFwdParams* p) {
   if (nslot > avey::kTcMaxSlots) nslot = avey::kTcMaxSlots;
   l.geom.nslot = nslot;
   // Phase-A stages use the space of the phase-C ring.
-  l.geom.a_stage_bytes = (1 + nk_max) * avey::kTcTileBytesA;
+  l.geom.a_stage_bytes = nk_max * avey::kTcTileBytesA;
   int nst = (nslot * avey::kTcUnitBytes) / l.geom.a_stage_bytes;
   if (nst > avey::kTcMaxStages) nst = avey::kTcMaxStages;
   l.geom.a_nstage = nst;

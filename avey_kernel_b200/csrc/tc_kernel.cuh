@@ -51,13 +51,13 @@ namespace avey {
 
 constexpr int kTcThreads = 384;
 constexpr int kTcMaxKeys = 512;      // keys per work item (TMEM holds 512 fp32 columns)
-constexpr int kTcUnitBytes = 16384;  // one phase-C ring slot (64 keys x 128 features)
-constexpr int kTcUnitKeys = 64;      // keys per phase-C unit
+constexpr int kTcUnitBytes = 32768;  // one phase-C ring slot (128 keys x 128 features)
+constexpr int kTcUnitKeys = 128;     // keys per phase-C unit (one key tile)
 constexpr int kTcSliceCols = 128;    // output features per phase-C slice (TMEM buffer)
 constexpr int kTcOutTileBytes = 2048; // one warp's 32 x 32 output staging tile
 constexpr int kTcOutStageBytes = 8 * kTcOutTileBytes;
-constexpr int kTcZBoxBytes = 8192;   // one {64 features x 64 keys} box of a unit
-constexpr int kTcMaxSlots = 12;
+constexpr int kTcZBoxBytes = 16384;  // one {64 features x 128 keys} box of a unit
+constexpr int kTcMaxSlots = 6;
 constexpr int kTcMaxStages = 8;
 constexpr int kTcChunk = 64;                      // phase-A feature chunk (128-byte rows)
 constexpr int kTcTileBytesA = 128 * kTcChunk * 2; // one 128-row tile of a chunk (16 KB)
@@ -68,7 +68,7 @@ struct TcGeom {
   int nslot;          // phase-C ring slots
   int n_qtiles;       // query tiles per batch row
   int a_nstage;       // phase-A stages inside the phase-C ring space
-  int a_stage_bytes;  // (1 + key tiles) x 16 KB
+  int a_stage_bytes;  // key tiles x 16 KB
 };
 
 // TMEM column of the packed P pair holding key j (two keys per 32-bit column).
@@ -208,7 +208,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int b = item % B;
   const int q_lo = qt * 128;
 #ifdef AVEY_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) g_trace[blockIdx.x][15] = qt * 100000ull + b;
+  if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) {
+    g_trace[blockIdx.x][15] = qt * 100000ull + b;
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_trace[blockIdx.x][13] = smid;
+  }
 #endif
 
   const uint8_t* va = args.has_valid ? args.valid + static_cast<int64_t>(b) * args.va_bs : nullptr;
@@ -289,11 +294,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (leader) {
           const uint32_t full = smem_u32(&ctrl->a_full[a_st]);
           const uint32_t st = stage_addr + a_st * geom.a_stage_bytes;
-          mbar_arrive_expect_tx(full, (1 + nk) * kTcTileBytesA);
-          tma_load_3d_hint(st, &map_q, full, c * kTcChunk, q_lo, b, keep);
+          // Key tiles 0 .. nk-1; the query tile is key tile qt (qt < nk in
+          // both modes), so it is not loaded a second time.
+          mbar_arrive_expect_tx(full, nk * kTcTileBytesA);
           for (int t = 0; t < nk; ++t)
-            tma_load_3d_hint(st + (1 + t) * kTcTileBytesA, &map_q, full, c * kTcChunk, t * 128, b,
-                             keep);
+            tma_load_3d_hint(st + t * kTcTileBytesA, &map_q, full, c * kTcChunk, t * 128, b, keep);
         }
         __syncwarp();
         ++c;
@@ -347,6 +352,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // address field; every address stays below 2^18, so nothing carries out.
       const uint64_t dq0 = smem_desc_sw128(stage_addr, 16, 1024);
       const uint32_t stage_adv = static_cast<uint32_t>(geom.a_stage_bytes) >> 4;
+      const uint32_t q_adv = static_cast<uint32_t>(qt * kTcTileBytesA) >> 4;
       const uint32_t idesc_g256 = idesc_f16(fmt, 128, 256, 0, 0);
       const uint32_t idesc_g128 = idesc_f16(fmt, 128, 128, 0, 0);
       const uint32_t idesc_g1 = nk >= 2 ? idesc_g256 : idesc_g128;
@@ -358,15 +364,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         if (leader) AVEY_STAMP_UNIT(c, 1);
         if (leader) {
-          const uint64_t dq = dq0 + st * stage_adv;
+          const uint64_t dk = dq0 + st * stage_adv;  // key tile 0 of this stage
+          const uint64_t dq = dk + q_adv;              // the query tile (key tile qt)
           // Four 16-feature K steps (32 bytes each inside the 128-byte swizzled
           // rows); key tiles (0,1) and (2,3) are each one N = 256 MMA.
 #pragma unroll
           for (int k = 0; k < kTcChunk / 16; ++k) {
             const uint32_t acc = (c != 0 || k != 0) ? 1u : 0u;
-            tc_mma_f16(tmem, dq + 2 * k, dq + (kTcTileBytesA >> 4) + 2 * k, idesc_g1, acc);
+            tc_mma_f16(tmem, dq + 2 * k, dk + 2 * k, idesc_g1, acc);
             if (nk > 2)
-              tc_mma_f16(tmem + 256, dq + 2 * k, dq + (3 * kTcTileBytesA >> 4) + 2 * k, idesc_g2,
+              tc_mma_f16(tmem + 256, dq + 2 * k, dk + (2 * kTcTileBytesA >> 4) + 2 * k, idesc_g2,
                          acc);
           }
           tc_commit(smem_u32(&ctrl->a_empty[st]));
@@ -404,8 +411,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_after();
           if (leader) AVEY_STAMP_UNIT(128 + s * nunits + uu, 1);
           if (leader) {
-            // P keys 64 uu .. +63 start at TMEM column p_col(64 uu); K steps of
-            // 16 keys advance 8 columns of P and 16 rows (2 KB) of the Z unit.
+            // P keys 128 uu .. +127 start at TMEM column p_col(128 uu); K steps
+            // of 16 keys advance 8 columns of P and 16 rows (2 KB) of the Z unit.
             const uint32_t a_tmem = tmem + p_col(uu * kTcUnitKeys, nk);
             const uint64_t dz = dz0 + slot * (kTcUnitBytes >> 4);
 #pragma unroll
@@ -446,13 +453,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         out[static_cast<int64_t>(q_lo + r) * args.o_rs + f] = store_cast<T, float>(0.f);
       }
     } else {
-      // Warm L2 with this thread's half of its gate row (read in phase C).
-      if (args.has_zl && i < C) {
-        const char* grow = reinterpret_cast<const char*>(zl + static_cast<int64_t>(i) * args.zl_rs);
-        const int nlines = (D * 2 + 127) / 128;
-        const int half = (nlines + 1) / 2;
-        for (int l = h * half; l < min(nlines, (h + 1) * half); ++l)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(grow + l * 128));
+      // Warm L2 with the gate of the first output slice this thread drains
+      // (slice h); each drain warms the slice two further on. Warming the whole
+      // row here measured slower: the lines are evicted again before phase C.
+      if (args.has_zl && i < C && h * kTcSliceCols < D) {
+        const char* grow = reinterpret_cast<const char*>(zl + static_cast<int64_t>(i) * args.zl_rs +
+                                                         h * kTcSliceCols);
+        const int nbytes = min(kTcSliceCols, D - h * kTcSliceCols) * 2;
+        for (int l = 0; l < nbytes; l += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(grow + l));
       }
       // ---------------- phase A (compute warps): sums of squares of the key rows
       // from norm_prepass, which may still be running (programmatic dependent
@@ -616,6 +624,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       };
       auto drain = [&](int s, int buf, int s_next) {
+        if (zrow && s + 2 < nslices) {
+          const char* g2 = reinterpret_cast<const char*>(zrow + (s + 2) * kTcSliceCols);
+          const int nbytes = min(kTcSliceCols, D - (s + 2) * kTcSliceCols) * 2;
+          for (int l = 0; l < nbytes; l += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g2 + l));
+        }
         mbar_wait(smem_u32(&ctrl->o_full[buf]), (s >> 1) & 1);
         tc_fence_after();
         const int width = min(kTcSliceCols, D - s * kTcSliceCols);
@@ -654,7 +667,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&ctrl->o_empty[buf]));
-        if (wq == 0 && lane == 0 && s < 6) AVEY_STAMP(8 + s);  // slice s drained
+        if (wq == 0 && lane == 0 && s < 4) AVEY_STAMP(8 + s);  // slice s drained
       };
       const int s_first = fix ? 0 : h;
       if (zrow && s_first < nslices)
