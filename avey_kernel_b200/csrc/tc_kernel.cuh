@@ -92,7 +92,7 @@ struct TcCtrl {
   uint32_t tmem_base;
   int last_valid;
   int fix;
-  int pad_[1];
+  int exact;  // some key row's sum of squares is not finite: mask every P chunk exactly
   alignas(16) float rinv[kTcMaxKeys];  // sums of squares, then inverse norms (read as float4)
   float den[2][128];
   uint32_t kbits[kTcMaxKeys / 32];
@@ -125,12 +125,52 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// With bf16 the query row's inverse norm rq is not multiplied into P: P/rq
+// keeps bf16's relative precision (same exponent range as fp32), and the
+// drain multiplies O by rq instead. fp16 keeps rq in P, whose range bounds it.
+template <typename T>
+constexpr bool kRowScaleInP = !std::is_same<T, __nv_bfloat16>::value;
+
+// One 32-key chunk of P for this thread's row: P = G * rq * rk * V (rq only
+// if kRowScaleInP), packed to 16-bit pairs. MASKED applies the allowed-key
+// bits `okb` with a select (so a non-finite product of a masked key still
+// gives 0); otherwise keys outside the allowed set already carry rk = 0. NORM
+// accumulates the row sums of P; HAS_V multiplies by the weight row.
+template <typename T, bool MASKED, bool NORM, bool HAS_V>
+__device__ __forceinline__ void p_chunk(const uint32_t (&g)[32], const float4* rk4, float rqi,
+                                        const uint32_t (&vw)[16], uint32_t okb, uint32_t (&pk)[16],
+                                        float (&den)[4]);
+
 // Element e (0..31) of 32 packed 16-bit values.
 template <typename T>
 __device__ __forceinline__ float raw_at(const uint32_t (&w)[16], int e) {
   const uint32_t word = w[e >> 1];
   const uint16_t h = static_cast<uint16_t>((e & 1) ? (word >> 16) : (word & 0xFFFFu));
   return to_f32<T>(*reinterpret_cast<const T*>(&h));
+}
+
+template <typename T, bool MASKED, bool NORM, bool HAS_V>
+__device__ __forceinline__ void p_chunk(const uint32_t (&g)[32], const float4* rk4, float rqi,
+                                        const uint32_t (&vw)[16], uint32_t okb, uint32_t (&pk)[16],
+                                        float (&den)[4]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 rk = rk4[q];
+    const float r[4] = {rk.x, rk.y, rk.z, rk.w};
+    float pv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int idx = 4 * q + e;
+      float p = __uint_as_float(g[idx]) * r[e];
+      if (kRowScaleInP<T>) p *= rqi;
+      if (HAS_V) p *= raw_at<T>(vw, idx);
+      if (MASKED) p = ((okb >> idx) & 1u) ? p : 0.f;
+      if (NORM) den[e] += p;
+      pv[e] = p;
+    }
+    pk[2 * q] = pack2<T>(pv[0], pv[1]);
+    pk[2 * q + 1] = pack2<T>(pv[2], pv[3]);
+  }
 }
 
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
@@ -237,6 +277,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     ctrl->last_valid = -1;
     ctrl->fix = 0;
+    ctrl->exact = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -475,14 +516,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       {
         const int tid_c = cw * 32 + lane;
         const float norm_eps = args.norm_eps_f;
-        int bad = 0;
+        int bad = 0, nonfinite = 0;
         for (int j = tid_c; j < nk * 128; j += 256) {
           const float s2 = ctrl->rinv[j];
-          // Padded rows holding Inf / NaN would poison P.Z (0 * NaN): flag them.
-          if (j < C && !ctrl->kvalid[j] && !isfinite(s2)) bad = 1;
-          ctrl->rinv[j] = 1.f / fmaxf(sqrtf(s2), norm_eps);
+          if (j < C && !isfinite(s2)) {
+            nonfinite = 1;
+            // Padded rows holding Inf / NaN would poison P.Z (0 * NaN): flag them.
+            if (!ctrl->kvalid[j]) bad = 1;
+          }
+          // Keys outside the allowed set (padding, past nkeys) get a zero
+          // inverse norm, which zeroes their P column without a select.
+          ctrl->rinv[j] = (j < nkeys && ctrl->kvalid[j]) ? 1.f / fmaxf(sqrtf(s2), norm_eps) : 0.f;
         }
         if (bad) ctrl->fix = 1;
+        if (nonfinite) ctrl->exact = 1;
         // Key bitmask: bit e of word w <=> key 32 w + e is valid and < nkeys.
         if (tid_c < kTcMaxKeys / 32) {
           uint32_t m = 0u;
@@ -499,9 +546,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       named_bar_sync(1, 256);
 
       // ---------------- phase B: P = G * rinv_i * rinv_j * V, masked, into TMEM
-      mbar_wait(smem_u32(&ctrl->s_full), 0);
-      tc_fence_after();
-      if (cw == 0 && lane == 0) AVEY_STAMP(6);  // Gram complete
       const bool row_ok = i < C && ctrl->kvalid[i];
       const float rqi = row_ok ? ctrl->rinv[i] : 0.f;
       const T* vrow = (args.has_v && i < C) ? static_cast<const T*>(args.v) + static_cast<int64_t>(i) * args.v_rs
@@ -509,7 +553,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool v_vec = (reinterpret_cast<uintptr_t>(args.v) & 15u) == 0 && (args.v_rs & 7) == 0;
       const uint64_t keep = l2_policy_evict_last();    // V: read by every batch row
       const uint64_t stream = l2_policy_evict_normal(); // gate and output: touched once
-      float den = 0.f;
+      float den4[4] = {0.f, 0.f, 0.f, 0.f};
       {
         // Key ranges of the two warpgroups (see p_col): with three or four key
         // tiles warpgroup 0 takes keys [0, 256) and warpgroup 1 the rest.
@@ -521,39 +565,58 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t vw[16], vn[16], vnn[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) vw[q] = vn[q] = vnn[q] = one2;
+        // The first two V chunks do not depend on the Gram: load them while
+        // the MMAs still run.
         if (vrow) {
           load_raw32<T>(vrow + c_begin, C - c_begin, v_vec, vw, keep);
           if (nch > 1) load_raw32<T>(vrow + c_begin + 32, C - c_begin - 32, v_vec, vn, keep);
         }
+        mbar_wait(smem_u32(&ctrl->s_full), 0);
+        tc_fence_after();
+        if (cw == 0 && lane == 0) AVEY_STAMP(6);  // Gram complete
+        // Chunks need per-key selects only where a mask bit can be 0 for a key
+        // whose zero inverse norm does not already zero the product: keys above
+        // the causal diagonal, non-finite rows (0 * Inf), and padded keys when a
+        // weight matrix may hold non-finite values there. The choice is uniform
+        // per warp (i0 = the warp's first row).
+        const bool exact = ctrl->exact != 0 || (args.has_valid && args.has_v);
+        const int i0 = q_lo + wq * 32;
+        const bool norm = args.normalize;
 #pragma unroll 1
         for (int ch = 0; ch < nch; ++ch) {
           const int c0 = c_begin + ch * 32;
           uint32_t g[32];
           tmem_ld32(tmem + lane_off + c0, g);
           if (vrow && ch + 2 < nch) load_raw32<T>(vrow + c0 + 64, C - c0 - 64, v_vec, vnn, keep);
-          // Allowed keys of this chunk: valid, below nkeys, and j <= i if causal.
-          uint32_t okb = row_ok ? ctrl->kbits[c0 >> 5] : 0u;
-          if (args.causal) {
-            const int lim = i - c0 + 1;
-            okb &= lim >= 32 ? 0xFFFFFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+          const bool masked = exact || (args.causal && c0 + 31 > i0);
+          uint32_t okb = 0u;
+          if (masked) {
+            // Allowed keys of this chunk: valid, below nkeys, and j <= i if causal.
+            okb = row_ok ? ctrl->kbits[c0 >> 5] : 0u;
+            if (args.causal) {
+              const int lim = i - c0 + 1;
+              okb &= lim >= 32 ? 0xFFFFFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+            }
           }
           tmem_wait_ld(g);
           const float4* rk4 = reinterpret_cast<const float4*>(&ctrl->rinv[c0]);
           uint32_t pk[16];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 rk = rk4[q];
-            const float r[4] = {rk.x, rk.y, rk.z, rk.w};
-            float pv[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int idx = 4 * q + e;
-              const float p = __uint_as_float(g[idx]) * rqi * r[e] * raw_at<T>(vw, idx);
-              pv[e] = ((okb >> idx) & 1u) ? p : 0.f;
-              den += pv[e];
+          if (args.has_v) {  // uniform; rows past the context multiply by ones
+            if (masked) {
+              if (norm) p_chunk<T, true, true, true>(g, rk4, rqi, vw, okb, pk, den4);
+              else p_chunk<T, true, false, true>(g, rk4, rqi, vw, okb, pk, den4);
+            } else {
+              if (norm) p_chunk<T, false, true, true>(g, rk4, rqi, vw, okb, pk, den4);
+              else p_chunk<T, false, false, true>(g, rk4, rqi, vw, okb, pk, den4);
             }
-            pk[2 * q] = pack2<T>(pv[0], pv[1]);
-            pk[2 * q + 1] = pack2<T>(pv[2], pv[3]);
+          } else {
+            if (masked) {
+              if (norm) p_chunk<T, true, true, false>(g, rk4, rqi, vw, okb, pk, den4);
+              else p_chunk<T, true, false, false>(g, rk4, rqi, vw, okb, pk, den4);
+            } else {
+              if (norm) p_chunk<T, false, true, false>(g, rk4, rqi, vw, okb, pk, den4);
+              else p_chunk<T, false, false, false>(g, rk4, rqi, vw, okb, pk, den4);
+            }
           }
           // Packed pairs into TMEM columns this thread has already read.
           tmem_st16(tmem + lane_off + p_col(c0, nk), pk);
@@ -566,6 +629,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
+      const float den = (den4[0] + den4[1]) + (den4[2] + den4[3]);
       ctrl->den[h][row] = den;
       tmem_wait_st();
       tc_fence_before();
@@ -573,8 +637,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&ctrl->p_ready));
       named_bar_sync(1, 256);
       if (cw == 0 && lane == 0) AVEY_STAMP(7);  // P written
+      // O (and the row sums) carry rq only if it went into P.
+      const float o_scale = kRowScaleInP<T> ? 1.f : rqi;
       const float inv_den =
-          args.normalize ? 1.f / (ctrl->den[0][row] + ctrl->den[1][row] + args.eps_f) : 1.f;
+          args.normalize ? o_scale / (o_scale * (ctrl->den[0][row] + ctrl->den[1][row]) + args.eps_f)
+                         : o_scale;
       const bool fix = ctrl->fix != 0;
 
       // ---------------- phase C: drain O slices (and, in fix mode, clean units)
