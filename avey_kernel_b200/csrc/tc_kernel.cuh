@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(smem_u32(&ctrl->p_ready), 8);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&ctrl->o_full[i]), 1);
-      mbar_init(smem_u32(&ctrl->o_empty[i]), 4);
+      mbar_init(smem_u32(&ctrl->o_empty[i]), 8);  // every compute warp, once per slice
     }
     ctrl->last_valid = -1;
     ctrl->fix = 0;
@@ -319,10 +319,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     // ============================================================ TMA producer
-    // The whole warp walks the schedule; one lane issues. Slot indices and
-    // barrier parities advance incrementally (no divisions in the hot loop).
-    if (!skip) {
-      const bool leader = lane == 0;
+    // One lane walks the whole schedule (a per-step branch on the lane index
+    // would cost a reconvergence every step). Slot indices and barrier
+    // parities advance incrementally (no divisions in the hot loop).
+    if (!skip && lane == 0) {
       const uint64_t keep = l2_policy_evict_last();  // z_tr is read again (phase C, other CTAs)
       // Phase-A stage state.
       int a_st = 0, a_use = 0, c = 0;
@@ -331,8 +331,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int nbox = (min(kTcSliceCols, D) + 63) / 64;
       auto load_stage = [&]() {
         if (a_use > 0) mbar_wait(smem_u32(&ctrl->a_empty[a_st]), (a_use - 1) & 1);
-        if (leader) AVEY_STAMP_UNIT(c, 0);
-        if (leader) {
+        AVEY_STAMP_UNIT(c, 0);
+        {
           const uint32_t full = smem_u32(&ctrl->a_full[a_st]);
           const uint32_t st = stage_addr + a_st * geom.a_stage_bytes;
           // Key tiles 0 .. nk-1; the query tile is key tile qt (qt < nk in
@@ -341,7 +341,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int t = 0; t < nk; ++t)
             tma_load_3d_hint(st + t * kTcTileBytesA, &map_q, full, c * kTcChunk, t * 128, b, keep);
         }
-        __syncwarp();
         ++c;
         if (++a_st == nst) {
           a_st = 0;
@@ -350,8 +349,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       auto load_unit = [&]() {
         if (c_use > 0) mbar_wait(smem_u32(&ctrl->empty[c_slot]), (c_use - 1) & 1);
-        if (leader) AVEY_STAMP_UNIT(128 + u, 0);
-        if (leader) {
+        AVEY_STAMP_UNIT(128 + u, 0);
+        {
           const uint32_t full = smem_u32(&ctrl->full[c_slot]);
           const uint32_t dst = ring_addr + c_slot * kTcUnitBytes;
           mbar_arrive_expect_tx(full, nbox * kTcZBoxBytes);
@@ -359,7 +358,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_3d_hint(dst + i * kTcZBoxBytes, &map_z, full, sl * kTcSliceCols + i * 64,
                              uu * kTcUnitKeys, b, keep);
         }
-        __syncwarp();
         ++u;
         if (++uu == nunits) {
           uu = 0;
@@ -387,8 +385,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
-    if (!skip) {
-      const bool leader = lane == 0;
+    // One lane issues everything (see the producer).
+    if (!skip && lane == 0) {
       // Descriptors are advanced by adding (byte offset >> 4) to the start
       // address field; every address stays below 2^18, so nothing carries out.
       const uint64_t dq0 = smem_desc_sw128(stage_addr, 16, 1024);
@@ -403,8 +401,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < nchunk; ++c) {
         mbar_wait(smem_u32(&ctrl->a_full[st]), ph);
         tc_fence_after();
-        if (leader) AVEY_STAMP_UNIT(c, 1);
-        if (leader) {
+        AVEY_STAMP_UNIT(c, 1);
+        {
           const uint64_t dk = dq0 + st * stage_adv;  // key tile 0 of this stage
           const uint64_t dq = dk + q_adv;              // the query tile (key tile qt)
           // Four 16-feature K steps (32 bytes each inside the 128-byte swizzled
@@ -420,20 +418,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_commit(smem_u32(&ctrl->a_empty[st]));
           AVEY_STAMP_UNIT(c, 2);
         }
-        __syncwarp();
         if (++st == nst) {
           st = 0;
           ph ^= 1u;
         }
       }
-      if (leader) {
-        tc_commit(smem_u32(&ctrl->s_full));
-        AVEY_STAMP(2);  // last Gram MMA issued
-      }
-      __syncwarp();
+      tc_commit(smem_u32(&ctrl->s_full));
+      AVEY_STAMP(2);  // last Gram MMA issued
       mbar_wait(smem_u32(&ctrl->p_ready), 0);
       tc_fence_after();
-      if (leader) AVEY_STAMP(3);  // P observed by the MMA warp
+      AVEY_STAMP(3);  // P observed by the MMA warp
       const bool fix = ctrl->fix != 0;
       const uint64_t dz0 = smem_desc_sw128(ring_addr, kTcZBoxBytes, 1024);
       int slot = 0;
@@ -450,8 +444,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int uu = 0; uu < nunits; ++uu) {
           mbar_wait(smem_u32(fix ? &ctrl->fixed[slot] : &ctrl->full[slot]), ph);
           tc_fence_after();
-          if (leader) AVEY_STAMP_UNIT(128 + s * nunits + uu, 1);
-          if (leader) {
+          AVEY_STAMP_UNIT(128 + s * nunits + uu, 1);
+          {
             // P keys 128 uu .. +127 start at TMEM column p_col(128 uu); K steps
             // of 16 keys advance 8 columns of P and 16 rows (2 KB) of the Z unit.
             const uint32_t a_tmem = tmem + p_col(uu * kTcUnitKeys, nk);
@@ -463,16 +457,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_commit(smem_u32(&ctrl->empty[slot]));
             AVEY_STAMP_UNIT(128 + s * nunits + uu, 2);
           }
-          __syncwarp();
           if (++slot == nslot) {
             slot = 0;
             ph ^= 1u;
           }
         }
-        if (leader) tc_commit(smem_u32(&ctrl->o_full[buf]));
-        __syncwarp();
+        tc_commit(smem_u32(&ctrl->o_full[buf]));
       }
-      if (leader) AVEY_STAMP(4);  // last mix MMA issued
+      AVEY_STAMP(4);  // last mix MMA issued
     }
   } else if (warp >= 4) {
     // ============================================================ compute warps
@@ -494,13 +486,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         out[static_cast<int64_t>(q_lo + r) * args.o_rs + f] = store_cast<T, float>(0.f);
       }
     } else {
-      // Warm L2 with the gate of the first output slice this thread drains
-      // (slice h); each drain warms the slice two further on. Warming the whole
-      // row here measured slower: the lines are evicted again before phase C.
-      if (args.has_zl && i < C && h * kTcSliceCols < D) {
+      // Warm L2 with the gate of this warpgroup's part of the first output
+      // slice (columns 64 h .. 64 h + 63); each drain warms the next slice's.
+      // Warming the whole row here measured slower: the lines are evicted
+      // again before phase C.
+      if (args.has_zl && i < C && h * 64 < D) {
         const char* grow = reinterpret_cast<const char*>(zl + static_cast<int64_t>(i) * args.zl_rs +
-                                                         h * kTcSliceCols);
-        const int nbytes = min(kTcSliceCols, D - h * kTcSliceCols) * 2;
+                                                         h * 64);
+        const int nbytes = min(64, D - h * 64) * 2;
         for (int l = 0; l < nbytes; l += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(grow + l));
       }
       // ---------------- phase A (compute warps): sums of squares of the key rows
@@ -690,30 +683,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           bulk_commit_group();
         }
       };
-      auto drain = [&](int s, int buf, int s_next) {
-        if (zrow && s + 2 < nslices) {
-          const char* g2 = reinterpret_cast<const char*>(zrow + (s + 2) * kTcSliceCols);
-          const int nbytes = min(kTcSliceCols, D - (s + 2) * kTcSliceCols) * 2;
+      // Drain slice s: chunks [ch_lo, ch_hi) of its 32-column chunks (both
+      // warpgroups split every slice, so a slice is drained in half the time
+      // and the MMA can refill its buffer sooner). Every compute warp waits
+      // for and releases every slice, even with no chunk of it, which keeps
+      // the two buffers' phases in step. In fix mode warpgroup 0 drains every
+      // chunk alone and releases for both warpgroups.
+      const int ch_lo = fix ? 0 : 2 * h, ch_hi = fix ? 4 : 2 * h + 2;
+      const uint32_t rel_cnt = fix ? 2u : 1u;
+      auto drain = [&](int s) {
+        const int buf = s & 1;
+        if (zrow && s + 1 < nslices) {
+          const int f = (s + 1) * kTcSliceCols + ch_lo * 32;
+          const int nbytes = min((ch_hi - ch_lo) * 32, D - f) * 2;
+          const char* g2 = reinterpret_cast<const char*>(zrow + f);
           for (int l = 0; l < nbytes; l += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g2 + l));
         }
         mbar_wait(smem_u32(&ctrl->o_full[buf]), (s >> 1) & 1);
         tc_fence_after();
         const int width = min(kTcSliceCols, D - s * kTcSliceCols);
-        const int nch_o = (width + 31) / 32;
+        const int nch_o = min(ch_hi, (width + 31) / 32);
         const uint32_t tb = tmem + lane_off + o_col(buf, nk);
-        // Gate words of the chunk after `f0` (the rest of this slice, then the
-        // first chunk of s_next), prefetched one chunk ahead.
+        // Gate words of the chunk after `f0` (the rest of this slice's range,
+        // then the first chunk of the next slice), prefetched one chunk ahead.
         auto next_gate = [&](int ch, int f0) {
           if (zrow) {
-            const int fn = ch + 1 < nch_o ? f0 + 32 : (s_next < nslices ? s_next * kTcSliceCols : -1);
-            if (fn >= 0) load_raw32<T>(zrow + fn, D - fn, zl_vec, gn, stream);
+            const int fn = ch + 1 < nch_o ? f0 + 32
+                                          : (s + 1 < nslices ? (s + 1) * kTcSliceCols + ch_lo * 32 : D);
+            if (fn < D) load_raw32<T>(zrow + fn, D - fn, zl_vec, gn, stream);
           }
         };
         // TMEM loads run one chunk ahead of the math.
         uint32_t oa[32], ob[32], gw[16];
-        tmem_ld32(tb, oa);
+        if (ch_lo < nch_o) tmem_ld32(tb + ch_lo * 32, oa);
 #pragma unroll 1
-        for (int ch = 0; ch < nch_o; ch += 2) {
+        for (int ch = ch_lo; ch < nch_o; ch += 2) {
           const int f0 = s * kTcSliceCols + ch * 32;
           tmem_wait_ld(oa);
           const bool has_b = ch + 1 < nch_o;
@@ -733,17 +737,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctrl->o_empty[buf]));
+        if (lane == 0) mbar_arrive_cnt(smem_u32(&ctrl->o_empty[buf]), rel_cnt);
         if (wq == 0 && lane == 0 && s < 4) AVEY_STAMP(8 + s);  // slice s drained
       };
-      const int s_first = fix ? 0 : h;
-      if (zrow && s_first < nslices)
-        load_raw32<T>(zrow + s_first * kTcSliceCols, D - s_first * kTcSliceCols, zl_vec, gn, stream);
-      if (!fix) {
-        for (int s = h; s < nslices; s += 2) drain(s, h, s + 2);
-        if (lane == 0) bulk_wait_all();
-      } else if (h == 0) {
-        for (int s = 0; s < nslices; ++s) drain(s, s & 1, s + 1);
+      if (zrow && ch_lo * 32 < D)
+        load_raw32<T>(zrow + ch_lo * 32, D - ch_lo * 32, zl_vec, gn, stream);
+      if (!fix || h == 0) {
+        for (int s = 0; s < nslices; ++s) drain(s);
         if (lane == 0) bulk_wait_all();
       } else {
         // Fix mode: zero every padded key row of each mix unit before the MMA
