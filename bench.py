@@ -67,17 +67,20 @@ def load_peaks():
 
 
 def rank_env():
-    world = int(os.environ.get('WORLD_SIZE', '1'))
-    rank = int(os.environ.get('RANK', '0'))
-    local = int(os.environ.get('LOCAL_RANK', '0'))
-    return world, rank, local
+    from avey_kernel_b200.shard import rank_env as env
+    return env()
 
 
 def shard_batch(cfg, world):
+    """Batch rows per rank: fixed per GPU (weak scaling) or the global batch
+    split evenly (strong scaling, config 5)."""
     if cfg['scaling'] == 'strong':
-        if cfg['batch'] % world:
-            raise SystemExit(f'global batch {cfg["batch"]} does not split over {world} GPUs')
-        return cfg['batch'] // world
+        from avey_kernel_b200.shard import shard_bounds
+        try:
+            start, stop = shard_bounds(cfg['batch'], world, 0)
+        except ValueError as e:
+            raise SystemExit(str(e))
+        return stop - start
     return cfg['batch']
 
 
@@ -334,13 +337,11 @@ def run_ours(args, cfg):
         got = y[r:r + 1].float().cpu().numpy()
         verify_err = max(verify_err, float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30)))
     # Gather each rank's first output row to rank 0 (verification only, NCCL).
-    if world > 1:
-        row = y[0].contiguous()
-        gathered = [torch.empty_like(row) for _ in range(world)] if rank == 0 else None
-        dist.gather(row, gathered, dst=0)
-        errs = torch.tensor([verify_err], device=dev)
-        dist.all_reduce(errs, op=dist.ReduceOp.MAX)
-        verify_err = float(errs.item())
+    from avey_kernel_b200.shard import gather_to_rank0, max_over_ranks
+    gathered = gather_to_rank0(y[0])
+    if rank == 0 and gathered is not None:
+        assert len(gathered) == world and all(torch.isfinite(g.float()).all() for g in gathered)
+    verify_err = max_over_ranks(verify_err, device=dev)
     plan = ops.plan(sets[0]['x'][..., d:], sets[0]['w'], sets[0]['x'][..., :d], sets[0]['bias'],
                     sets[0]['valid'], causal=cfg['op'] == 'avey', normalize=cfg['op'] != 'avey')
     kernel_name = {1: 'simt_contextualize', 2: 'tc_contextualize'}[plan.kernel]
@@ -387,11 +388,7 @@ def run_ours(args, cfg):
         torch.cuda.synchronize()
     barrier()
     ms_total = start.elapsed_time(end)
-    ms_step = ms_total / args.steps
-    if world > 1:
-        tt = torch.tensor([ms_step], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_step = float(tt.item())
+    ms_step = max_over_ranks(ms_total / args.steps, device=dev)
     tokens_per_step = batch * cfg['n'] * world
     value = tokens_per_step / (ms_step / 1e3)
 
@@ -433,11 +430,7 @@ def run_ours(args, cfg):
     e_end.record()
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
-    if world > 1:
-        tt = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e2e_steps, device=dev)
     e2e_value = tokens_per_step / (e2e_ms / 1e3)
 
     # Roofline of the dominant (only) kernel.
