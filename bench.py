@@ -218,6 +218,13 @@ class ClockSampler:
                 'power_w_max': max(s[2] for s in self.samples)}
 
 
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_threads():
     try:
         from threadpoolctl import threadpool_info
@@ -226,7 +233,25 @@ def cpu_threads():
             return max(i.get('num_threads', 1) for i in info)
     except Exception:
         pass
-    return os.cpu_count() or 1
+    return host_cores()
+
+
+class all_host_threads:
+    """Let the BLAS pools use every core this process may run on (torchrun
+    exports OMP_NUM_THREADS=1 to its children)."""
+
+    def __enter__(self):
+        self._ctl = None
+        try:
+            from threadpoolctl import threadpool_limits
+            self._ctl = threadpool_limits(limits=host_cores())
+        except Exception:
+            pass
+        return self
+
+    def __exit__(self, *exc):
+        if self._ctl is not None:
+            self._ctl.restore_original_limits()
 
 
 def time_cpu_port(cfg, seconds=10.0, max_steps=None, warmup=1, rows=1):
@@ -266,8 +291,9 @@ def run_reference(args, cfg):
         return 0  # the CPU reference arm runs once, on rank 0
     batch = shard_batch(cfg, world)
     t0 = time.perf_counter()
-    value, steps, busy = time_cpu_port(cfg, max_steps=args.steps, warmup=args.warmup, rows=1)
-    cores = cpu_threads()
+    with all_host_threads():
+        value, steps, busy = time_cpu_port(cfg, max_steps=args.steps, warmup=args.warmup, rows=1)
+        cores = cpu_threads()
     sample = (f'{steps} steps x 1 of {batch} batch rows ({cfg["n"]} tokens) of {args.config}, '
               f'fp32 NumPy port of avey_kernels/ops.py::_reference (oracle/)')
     line = {
@@ -461,8 +487,10 @@ def run_ours(args, cfg):
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        cpu_value, cpu_steps, cpu_busy = time_cpu_port(cfg, seconds=args.cpu_seconds, rows=1)
-        cpu = {'value': cpu_value, 'unit': UNIT, 'cores': cpu_threads(), 'kind': 'port',
+        with all_host_threads():
+            cpu_value, cpu_steps, cpu_busy = time_cpu_port(cfg, seconds=args.cpu_seconds, rows=1)
+            cpu_cores = cpu_threads()
+        cpu = {'value': cpu_value, 'unit': UNIT, 'cores': cpu_cores, 'kind': 'port',
                'sample': f'{cpu_steps} runs of 1 batch row ({cfg["n"]} tokens) of {args.config}, '
                          f'{cpu_busy:.1f} s, fp32 NumPy port of avey_kernels/ops.py::_reference'}
 
