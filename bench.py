@@ -1,6 +1,6 @@
 """Contextualizer forward benchmark (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton]
                     [--config c2|c3|c4|c5]
 
 A step is one contextualizer forward over one batch of synthetic input shaped
@@ -19,6 +19,11 @@ e2e    the same metric through the public API (avey / avey_b) with pinned
 --impl reference  times the CPU implementation of the path (the NumPy port of
        the reference's _reference in oracle/, fp32, all host threads) on a
        bounded sample of the same workload; rank 0 only.
+--impl triton  (informational, one GPU) times the reference's own GPU kernel
+       through its public API (avey_kernels.ops, backend='triton', from the
+       unmodified install in baseline/_ref): normalisation pre-pass,
+       contiguous copies and the Triton mix kernel, device time with CUDA
+       events over K calls on the same inputs as --impl ours.
 """
 
 from __future__ import annotations
@@ -524,12 +529,88 @@ def run_ours(args, cfg):
     return 0
 
 
+def run_triton(args, cfg):
+    """The reference's GPU path (Triton) on this GPU, for comparison only."""
+    world, rank, _ = rank_env()
+    if rank != 0:
+        return 0
+    ref_dir = ROOT / 'baseline' / '_ref'
+    try:
+        sys.path.insert(0, str(ref_dir))
+        from avey_kernels import ops as ref_ops
+    except Exception as e:  # not installed on this box
+        print(json.dumps({'impl': 'triton', 'unavailable': f'reference not importable from '
+                                                           f'baseline/_ref: {e}'}), flush=True)
+        return 0
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    batch = shard_batch(cfg, world)
+    d = cfg['d']
+    nsets = 3
+    sets = [make_inputs(cfg, batch, seed=s, device=dev) for s in range(nsets)]
+    kw = dict(backend='triton', output_tile=args.triton_tile, autotune=args.triton_autotune)
+
+    def call(s):
+        t = sets[s]
+        head, tail = t['x'][..., :d], t['x'][..., d:]
+        if cfg['op'] == 'avey':
+            return ref_ops.avey(tail, t['w'], z_tl=head, bias=t['bias'], valid=t['valid'], **kw)
+        return ref_ops.avey_b(tail, z_tl=head, bias=t['bias'], valid=t['valid'], **kw)
+
+    t0 = time.perf_counter()
+    y = call(0)
+    torch.cuda.synchronize()
+    compile_s = time.perf_counter() - t0
+    # Parity of this run against the oracle on two rows (sanity of the baseline).
+    import numpy as np
+    import oracle
+    t = sets[0]
+    err = 0.0
+    for r in sorted({0, batch - 1}):
+        x = t['x'][r:r + 1].float().cpu().numpy()
+        okw = dict(z_tl=x[..., :d], bias=t['bias'].float().cpu().numpy() if t['bias'] is not None else None,
+                   valid=t['valid'][r:r + 1].cpu().numpy() if t['valid'] is not None else None)
+        ref = (oracle.avey(x[..., d:], t['w'].float().cpu().numpy(), **okw) if cfg['op'] == 'avey'
+               else oracle.avey_b(x[..., d:], **okw))
+        got = y[r:r + 1].float().cpu().numpy()
+        err = max(err, float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30)))
+    for i in range(max(args.warmup, 3)):
+        call(i % nsets)
+    torch.cuda.synchronize()
+    steps = args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        start.record()
+        for i in range(steps):
+            call(i % nsets)
+        end.record()
+        torch.cuda.synchronize()
+    ms_step = start.elapsed_time(end) / steps
+    value = batch * cfg['n'] / (ms_step / 1e3)
+    line = {
+        'impl': 'triton', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': 1,
+        'steps': steps, 'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True,
+        'dtype': 'bf16 inputs, fp32 arithmetic (tf32x3 MMA)', 'data': 'synthetic',
+        'config': {'workload': f'{args.config}: {cfg["desc"]}', 'context': cfg['n'],
+                   'features': cfg['d'], 'batch_per_gpu': batch, 'output_tile': args.triton_tile,
+                   'autotune': args.triton_autotune,
+                   'timing': 'eager calls between CUDA events (pre-pass, copies and kernel)'},
+        'first_call_s': compile_s, 'clocks': clocks.summary(),
+        'verify': {'max_norm_rel_err_vs_oracle': err, 'rows': 2},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=3000)
     ap.add_argument('--warmup', type=int, default=10)
-    ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    ap.add_argument('--impl', choices=('ours', 'reference', 'triton'), default='ours')
+    ap.add_argument('--triton-tile', type=int, choices=(32, 64, 128), default=128)
+    ap.add_argument('--triton-autotune', action='store_true')
     ap.add_argument('--config', choices=tuple(CONFIGS), default='c2')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
@@ -542,6 +623,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == 'reference':
         return run_reference(args, cfg)
+    if args.impl == 'triton':
+        return run_triton(args, cfg)
     return run_ours(args, cfg)
 
 
