@@ -19,6 +19,7 @@
 #include "norm_prepass.cuh"
 #include "simt_kernel.cuh"
 #include "tc_kernel.cuh"
+#include "tc_long.cuh"
 
 namespace {
 
@@ -43,7 +44,7 @@ int ok() {
 enum Reason {
   kReasonNone = 0,
   kReasonDtype = 1,      // tcgen05 kernel needs bf16 or f16
-  kReasonContext = 2,    // more than 512 tokens per row
+  kReasonContext = 2,    // more than 8192 tokens per row (or more than 512 without a workspace)
   kReasonAlignment = 3,  // base / strides not 16-byte aligned (TMA, vector I/O)
   kReasonForced = 4,     // caller asked for the CUDA-core kernel
   kReasonFeatures = 5,   // more than 2048 features (bias is staged in shared memory)
@@ -101,10 +102,13 @@ int device_arch_ok(int* major_out) {
   return AVEY_OK;
 }
 
-int tc_reason(const AveyFwdParams* p) {
+// Contexts up to 512 run the fused kernel; longer ones (up to 8192) the
+// two-kernel path of tc_long.cuh, whose P round trip needs a large workspace;
+// `allow_long` is false for the no-allocation entry point.
+int tc_reason(const AveyFwdParams* p, bool allow_long = true) {
   if (p->kernel == AVEY_KERNEL_SIMT) return kReasonForced;
   if (p->dtype != AVEY_BF16 && p->dtype != AVEY_F16) return kReasonDtype;
-  if (p->context > avey::kTcMaxKeys) return kReasonContext;
+  if (p->context > (allow_long ? avey::kLongMaxContext : avey::kTcMaxKeys)) return kReasonContext;
   if (p->features > avey::kTcMaxFeatures) return kReasonFeatures;
   const bool a = aligned16(p->z_tr) && aligned16(p->out) && (!p->z_tl || aligned16(p->z_tl)) &&
                  (p->z_tr_row_stride % 8 == 0) && (p->out_row_stride % 8 == 0) &&
@@ -139,6 +143,46 @@ TcLayout tc_layout(const AveyFwdParams* p) {
   l.geom.a_nstage = nst;
   l.geom.n_qtiles = nk_max;
   l.smem = 1024 + nslot * avey::kTcUnitBytes + avey::kTcOutStageBytes + avey::kTcCtrlBytes;
+  return l;
+}
+
+bool is_long(const AveyFwdParams* p) { return p->context > avey::kTcMaxKeys; }
+
+// Long-context path: grid shapes, shared memory and the workspace layout
+// [row sums of squares | partial row sums of P | P (bf16/f16, rows padded to
+// 64 elements)], each part 256-byte aligned.
+struct LongLayout {
+  avey::LongGeom geom;
+  int gp_items;
+  int smem_gp, smem_pv;
+  uint64_t off_den, off_p, total;
+};
+
+uint64_t align256(uint64_t x) { return (x + 255u) & ~uint64_t(255); }
+
+LongLayout long_layout(const AveyFwdParams* p) {
+  LongLayout l{};
+  const int64_t B = p->batch, C = p->context, D = p->features;
+  l.geom.n_qtiles = static_cast<int>((C + 127) / 128);
+  l.geom.n_groups = static_cast<int>((C + avey::kLgGroupKeys - 1) / avey::kLgGroupKeys);
+  int items = 0;
+  for (int qt = 0; qt < l.geom.n_qtiles; ++qt) {
+    const int64_t nkeys = p->causal ? std::min<int64_t>(C, qt * 128 + 128) : C;
+    items += static_cast<int>((nkeys + avey::kLgGroupKeys - 1) / avey::kLgGroupKeys);
+  }
+  l.gp_items = items;
+  l.geom.items = items;
+  l.geom.n_fgroups = static_cast<int>((D + avey::kPvGroupCols - 1) / avey::kPvGroupCols);
+  const int64_t cp = (C + 63) / 64 * 64;
+  l.geom.p_rs = cp;
+  l.geom.p_bs = C * cp;
+  l.off_den = align256(static_cast<uint64_t>(B * C) * sizeof(float));
+  l.off_p = l.off_den + align256(static_cast<uint64_t>(B * l.geom.n_groups * C) * sizeof(float));
+  l.total = l.off_p + static_cast<uint64_t>(B * C * cp) * 2u;
+  l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes +
+              8 * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kLgCtrlBytes;
+  l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes +
+              8 * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kPvCtrlBytes;
   return l;
 }
 
@@ -218,8 +262,99 @@ int encode_map(const AveyFwdParams* p, const void* base, int64_t batch_stride, i
   return AVEY_OK;
 }
 
+// 3-D map with explicit sizes: dims {inner, rows, batch}, strides in bytes.
+int encode_map_dims(int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
+                    uint64_t row_bytes, uint64_t batch_bytes, int box_cols, int box_rows,
+                    CUtensorMap* map) {
+  auto fn = encode_fn();
+  if (!fn) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int es = elem_size(dtype);
+  cuuint64_t dims[3] = {inner, rows, batch};
+  cuuint64_t strides[2] = {row_bytes, batch > 1 ? batch_bytes : row_bytes * rows};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  const CUtensorMapSwizzle swz =
+      box_cols * es == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == AVEY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return AVEY_OK;
+}
+
+template <typename T, int ACT>
+int launch_long(const AveyFwdParams* p, cudaStream_t stream) {
+  static std::once_flag attr_once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(avey::tc_gram_p<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kMaxDynSmem);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(avey::tc_pv<T, ACT>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  });
+  if (attr_err != cudaSuccess)
+    return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  LongLayout l = long_layout(p);
+  if (!p->workspace || p->workspace_bytes < l.total ||
+      (reinterpret_cast<uintptr_t>(p->workspace) & 255u))
+    return fail(AVEY_ERR_ARGUMENT,
+                "the long-context tcgen05 path needs a 256-byte aligned workspace of %llu bytes",
+                (unsigned long long)l.total);
+  uint8_t* ws = static_cast<uint8_t*>(p->workspace);
+  l.geom.den_part = reinterpret_cast<float*>(ws + l.off_den);
+  void* pbuf = ws + l.off_p;
+  const uint64_t C = static_cast<uint64_t>(p->context), B = static_cast<uint64_t>(p->batch);
+  const uint64_t prow = static_cast<uint64_t>(l.geom.p_rs) * 2u, pbat = static_cast<uint64_t>(l.geom.p_bs) * 2u;
+  CUtensorMap map_k, map_pst, map_p, map_z, map_o;
+  int rc = encode_map(p, p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride, avey::kTcChunk, 128, &map_k);
+  if (rc == AVEY_OK) rc = encode_map_dims(p->dtype, pbuf, C, C, B, prow, pbat, 32, 32, &map_pst);
+  if (rc == AVEY_OK) rc = encode_map_dims(p->dtype, pbuf, C, C, B, prow, pbat, 64, 128, &map_p);
+  if (rc == AVEY_OK)
+    rc = encode_map(p, p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride, 64, avey::kPvChunkKeys, &map_z);
+  if (rc == AVEY_OK) rc = encode_map(p, p->out, p->out_batch_stride, p->out_row_stride, 32, 32, &map_o);
+  if (rc != AVEY_OK) return rc;
+  const avey::FwdArgs args = make_args(p);
+  // 1. Row sums of squares.
+  const int rows = static_cast<int>(p->batch * p->context);
+  const int pre_blocks = std::min(148 * 8, (rows + 7) / 8);
+  avey::norm_prepass<T><<<pre_blocks, avey::kPrepassThreads, 0, stream>>>(args);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "norm pre-pass launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  // 2. G and P per (query tile, key group), a programmatic dependent of the
+  //    pre-pass (it waits for the sums only before forming P).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(l.gp_items), static_cast<unsigned>(p->batch));
+  cfg.blockDim = dim3(avey::kLgThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(l.smem_gp);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, avey::tc_gram_p<T>, args, map_k, map_pst, l.geom);
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_gram_p launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  // 3. O = P Z and the epilogue, in plain stream order after tc_gram_p.
+  avey::tc_pv<T, ACT><<<dim3(static_cast<unsigned>(l.geom.n_qtiles * l.geom.n_fgroups),
+                             static_cast<unsigned>(p->batch)),
+                        avey::kPvThreads, static_cast<size_t>(l.smem_pv), stream>>>(
+      args, map_p, map_z, map_o, l.geom);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_pv launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ok();
+}
+
 template <typename T, int ACT>
 int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
+  if (is_long(p)) return launch_long<T, ACT>(p, stream);
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -308,7 +443,14 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
   std::memset(plan, 0, sizeof(*plan));
   plan->reason = reason;
   plan->launches = 1;
-  if (reason == kReasonNone) {
+  if (reason == kReasonNone && is_long(p)) {
+    const LongLayout l = long_layout(p);
+    plan->kernel = AVEY_KERNEL_TCGEN05;
+    plan->launches = 3;
+    plan->grid = static_cast<int32_t>(p->batch * l.gp_items);
+    plan->block = avey::kLgThreads;
+    plan->smem_bytes = std::max(l.smem_gp, l.smem_pv);
+  } else if (reason == kReasonNone) {
     const TcLayout l = tc_layout(p);
     plan->kernel = AVEY_KERNEL_TCGEN05;
     plan->launches = 2;
@@ -330,9 +472,12 @@ int avey_fwd_workspace_size(const AveyFwdParams* p, uint64_t* bytes) {
   const int rc = avey_fwd_plan(p, &plan);
   if (rc != AVEY_OK) return rc;
   if (!bytes) return fail(AVEY_ERR_ARGUMENT, "bytes is NULL");
-  *bytes = plan.kernel == AVEY_KERNEL_TCGEN05
-               ? static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context) * sizeof(float)
-               : 0u;
+  if (plan.kernel != AVEY_KERNEL_TCGEN05)
+    *bytes = 0u;
+  else if (is_long(p))
+    *bytes = long_layout(p).total;
+  else
+    *bytes = static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context) * sizeof(float);
   return ok();
 }
 
@@ -397,6 +542,14 @@ int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
     return fail(AVEY_ERR_CUDA, "cudaGetSymbolAddress(no-allocation scratch): %s",
                 cudaGetErrorString(g_noalloc_err[dev]));
   AveyFwdParams q = *p;
+  // Contexts above 512 would take the long-context tensor-core path, whose P
+  // workspace this entry point does not have: they run the CUDA-core kernel.
+  if (is_long(p)) {
+    if (p->kernel == AVEY_KERNEL_TCGEN05)
+      return fail(AVEY_ERR_UNSUPPORTED,
+                  "the no-allocation entry point runs contexts above 512 on CUDA cores only");
+    q.kernel = AVEY_KERNEL_SIMT;
+  }
   q.workspace = g_noalloc_ptr[dev];
   q.workspace_bytes = static_cast<uint64_t>(AVEY_NOALLOC_MAX_ROWS) * sizeof(float);
   return avey_fwd_v1(&q, stream);

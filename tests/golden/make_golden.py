@@ -140,6 +140,19 @@ def build_cases():
     cases.append(_case('edge_129_holes', 'avey', z, v=torch.randn(129, 129, dtype=torch.bfloat16),
                        valid=valid, z_tl=torch.rand_like(z), activation='relu2'))
     cases.append(_case('edge_129_holes_b', 'avey_b', z, valid=valid, activation='gelu'))
+    # Contexts above 512 (the long-context tensor-core path): more than one
+    # group of 512 keys, a partial last tile, prefix padding past 512.
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(2, 640, 96, generator=g)
+    lengths = torch.tensor([640, 530])
+    valid = torch.arange(640)[None, :] < lengths[:, None]
+    cases.append(_case('long_b_640', 'avey_b', x[..., 48:].to(bf).contiguous(),
+                       z_tl=x[..., :48].to(bf).contiguous(), valid=valid, activation='gelu'))
+    x = torch.randn(1, 520, 64, generator=g)
+    w = torch.randn(520, 520, generator=g) * 0.05
+    bias = torch.randn(32, generator=g) * 0.1
+    cases.append(_case('long_a_520', 'avey', x[..., 32:].to(bf).contiguous(), v=w.to(bf),
+                       z_tl=x[..., :32].to(bf).contiguous(), bias=bias.to(bf)))
     return cases
 
 

@@ -155,6 +155,61 @@ def test_exact_properties_at_full_size():
     assert torch.equal(avey(tail[8:24], w, z_tl=head[8:24]), out[8:24])
 
 
+@pytest.mark.parametrize('name', ['c4', 'b1000', 'f16_1536'])
+def test_long_context_rows_match_oracle(name):
+    """Contexts above 512: pre-pass, G/P per key group into the workspace, O = P Z."""
+    g = torch.Generator(device='cpu').manual_seed(4)
+    if name == 'c4':  # BASELINE config 4 at two batch rows: 5% of rows scaled x50
+        b, n, d, dt = 2, 2048, 1024, torch.bfloat16
+    elif name == 'b1000':
+        b, n, d, dt = 3, 1000, 384, torch.bfloat16
+    else:
+        b, n, d, dt = 1, 1536, 512, torch.float16
+    x = torch.randn(b, n, 2 * d, generator=g)
+    if name == 'c4':
+        x = torch.where(torch.rand(b, n, 1, generator=g) < 0.05, x * 50, x)
+    x = x.to(dt).to(DEV)
+    head, tail = x[..., :d], x[..., d:]
+    w = (torch.randn(n, n, generator=g) * 0.02).to(dt).to(DEV)
+    before = _native.launch_count()
+    if name == 'b1000':
+        lengths = torch.tensor([1000, 517, 300])
+        valid = (torch.arange(n)[None, :] < lengths[:, None]).to(DEV)
+        out = avey_b(tail, z_tl=head, valid=valid, activation='gelu')
+        plan = ops.plan(tail, z_tl=head, valid=valid, causal=False, normalize=True)
+    else:
+        valid = None
+        act = 'identity' if name == 'c4' else 'relu'
+        out = avey(tail, w, z_tl=head, activation=act)
+        plan = ops.plan(tail, w, z_tl=head)
+    torch.cuda.synchronize()
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.launches == 3
+    assert _native.launch_count() == before + plan.launches
+    y = to_numpy(out)
+    assert np.isfinite(y).all()
+    for r in sorted({0, b - 1}):
+        zt, zl = to_numpy(tail[r:r + 1]), to_numpy(head[r:r + 1])
+        if name == 'b1000':
+            ok = to_numpy(valid[r:r + 1].float()) > 0
+            ref = oracle.avey_b(zt, z_tl=zl, valid=ok, activation='gelu')
+            assert (y[r:r + 1][~ok] == 0).all()
+        else:
+            ref = oracle.avey(zt, to_numpy(w), z_tl=zl, activation=act)
+        err = norm_rel_err(y[r:r + 1], ref)
+        assert err <= TOL['bfloat16'], (name, r, err)
+
+
+def test_long_context_exact_properties():
+    g = torch.Generator(device='cpu').manual_seed(9)
+    x = torch.randn(4, 1100, 2 * 256, generator=g).to(torch.bfloat16).to(DEV)
+    head, tail = x[..., :256], x[..., 256:]
+    w = (torch.randn(1100, 1100, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    out = avey(tail, w, z_tl=head)
+    assert torch.equal(out, avey(tail, w, z_tl=head))
+    assert torch.equal(avey(tail * 2, w, z_tl=head), out * 2)
+    assert torch.equal(avey(tail[1:3], w, z_tl=head[1:3]), out[1:3])
+
+
 def test_noncontiguous_and_strided_views():
     z = torch.rand(2, 37, 35, device=DEV).transpose(1, 2)
     ref = oracle.avey_b(to_numpy(z))

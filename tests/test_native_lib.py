@@ -97,13 +97,34 @@ def test_plan_accepts_head_tail_views_without_copy():
 @pytest.mark.parametrize('shape,dtype,reason', [
     ((2, 35, 133), torch.float32, 1),    # fp32 -> CUDA-core kernel
     ((2, 35, 37), torch.bfloat16, 3),    # 37 features: rows not 16-byte aligned
-    ((1, 2048, 64), torch.bfloat16, 2),  # more than 512 tokens
+    ((1, 8200, 64), torch.bfloat16, 2),  # more than 8192 tokens
     ((2, 35, 40), torch.float64, 1),
 ])
 def test_plan_falls_back_to_cuda_core_kernel(shape, dtype, reason):
     z = torch.randn(*shape).to(dtype)
     plan = ops.plan(z)
     assert plan.kernel == _native.KERNEL_SIMT and plan.reason == reason
+
+
+def test_plan_takes_the_long_context_tcgen05_path_above_512_tokens():
+    z = torch.randn(2, 2048, 1024).to(torch.bfloat16)
+    plan = ops.plan(z, torch.randn(2048, 2048).to(torch.bfloat16), z_tl=z)
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.reason == 0
+    # pre-pass, G/P per (query tile, key group), O = P Z: 40 items per batch row
+    # (query tile t has ceil((t + 1) / 4) groups of 512 keys)
+    assert plan.launches == 3 and plan.grid == 2 * 40 and plan.block == 384
+    assert plan.smem_bytes <= 232_448
+
+
+def test_long_context_workspace_holds_sums_partial_sums_and_p():
+    b, n, d = 3, 700, 128
+    z = torch.randn(b, n, d).to(torch.bfloat16)
+    out = torch.empty_like(z)
+    p = ops.build_params(z, None, None, None, None, out, eps=1e-6, norm_eps=1e-12, causal=False,
+                         normalize=True, activation_id=0)
+    al = lambda x: (x + 255) // 256 * 256
+    groups, padded = (n + 511) // 512, (n + 63) // 64 * 64
+    assert _native.workspace_size(p) == al(b * n * 4) + al(b * groups * n * 4) + b * n * padded * 2
 
 
 def test_forcing_tcgen05_on_unsupported_inputs_fails():

@@ -88,3 +88,17 @@ def test_noalloc_entry_point_rejects_inputs_beyond_its_limit():
     with pytest.raises(_native.NativeError, match='no-allocation limit'):
         _native.forward_noalloc(params, 0)
     assert _native.launch_count() == before
+
+
+@pytest.mark.gpu
+def test_noalloc_entry_point_runs_long_contexts_on_cuda_cores():
+    # Above 512 tokens avey_fwd_v1 takes the long-context tcgen05 path, whose
+    # P workspace this entry point does not have: it runs the CUDA-core kernel.
+    z = torch.randn(1, 600, 64, device='cuda').to(torch.bfloat16)
+    plan = ops.plan(z, causal=False, normalize=True)
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.launches == 3
+    before = _native.launch_count()
+    got = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=True)
+    assert _native.launch_count() == before + 1
+    want = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=False)
+    assert norm_rel_err(to_numpy(got), to_numpy(want)) <= TOL['bfloat16']
