@@ -56,7 +56,8 @@ typedef enum AveyActivation {
 typedef enum AveyKernel {
   AVEY_KERNEL_AUTO = 0,
   AVEY_KERNEL_SIMT = 1,   /* general CUDA-core kernel: any dtype/stride/shape */
-  AVEY_KERNEL_TCGEN05 = 2 /* fused TMA + tcgen05 + TMEM kernel (bf16 / f16) */
+  AVEY_KERNEL_TCGEN05 = 2 /* TMA + tcgen05 + TMEM kernels (bf16 / f16): one fused
+                             kernel up to 512 tokens, two kernels from 513 to 8192 */
 } AveyKernel;
 
 typedef enum AveyStatus {
@@ -108,8 +109,9 @@ typedef struct AveyFwdParams {
 /* What avey_fwd_v1 would launch for these parameters. */
 typedef struct AveyPlan {
   int32_t kernel;        /* AVEY_KERNEL_SIMT or AVEY_KERNEL_TCGEN05 */
-  int32_t launches;      /* kernel launches per call (2 on the tcgen05 path:
-                            the row-norm pre-pass and the fused kernel) */
+  int32_t launches;      /* kernel launches per call: 2 on the tcgen05 path up to
+                            512 tokens (row-norm pre-pass, fused kernel), 3 above
+                            (pre-pass, G/P kernel, O = P Z kernel), 1 on CUDA cores */
   int32_t grid;          /* CTAs of the main launch */
   int32_t block;         /* threads per CTA of the main launch */
   int32_t smem_bytes;    /* dynamic shared memory per CTA */
@@ -131,9 +133,13 @@ AVEY_API int avey_fwd_v1(const AveyFwdParams* params, void* stream);
  * Has no reference counterpart (introspection for tests and benchmarks). */
 AVEY_API int avey_fwd_plan(const AveyFwdParams* params, AveyPlan* plan);
 
-/* Device workspace avey_fwd_v1 needs for these parameters, in bytes: 4 per row
- * of z_tr (batch x context) for the tcgen05 kernel, 0 for the CUDA-core kernel.
- * The reference allocates its normalisation buffer itself (ops.py:113); this
+/* Device workspace avey_fwd_v1 needs for these parameters, in bytes: 0 for the
+ * CUDA-core kernel; on the tcgen05 path 4 per row of z_tr (batch x context)
+ * up to 512 tokens, and above 512 tokens, in 256-byte aligned parts, those
+ * row sums, 4 bytes per row per group of 512 keys (partial row sums) and P
+ * itself (2 bytes per (query, key) pair, rows padded to 64 keys): 134 MB for
+ * batch 16 x 2048 tokens. The workspace must be 256-byte aligned. The
+ * reference allocates its normalisation buffer itself (ops.py:113); this
  * library leaves allocation to the caller. Launches nothing. */
 AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* bytes);
 
@@ -146,6 +152,10 @@ AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* byte
  * point ignores params->workspace and uses a scratch array that lives inside
  * the library instead (file-scope device memory, present on every GPU that
  * loads the library until the process exits). It allocates nothing.
+ *
+ * Contexts above 512 tokens run the CUDA-core kernel here (the tcgen05 path
+ * for them needs a P workspace); forcing AVEY_KERNEL_TCGEN05 for them fails
+ * with AVEY_ERR_UNSUPPORTED.
  *
  * Limit: batch * context <= AVEY_NOALLOC_MAX_ROWS (1,048,576 rows; the
  * array holds one float per row, 4 MiB per GPU); larger inputs are rejected
