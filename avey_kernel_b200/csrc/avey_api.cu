@@ -182,7 +182,7 @@ LongLayout long_layout(const AveyFwdParams* p) {
   l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes +
               8 * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kLgCtrlBytes;
   l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes +
-              8 * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kPvCtrlBytes;
+              4 * avey::kPvStageTiles * avey::kTcOutTileBytes + avey::kPvCtrlBytes;
   return l;
 }
 

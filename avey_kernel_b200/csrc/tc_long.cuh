@@ -30,13 +30,17 @@ constexpr int kLgStageTiles = 2;             // output staging tiles per compute
 constexpr int kLgCtrlBytes = 5120;
 constexpr int kLongMaxContext = 8192;
 
-constexpr int kPvThreads = 384;
+// tc_pv: 256 threads (producer warp, MMA warp, two idle warps, one compute
+// warpgroup) and ~107 KB of shared memory, so two CTAs share an SM and one's
+// epilogue overlaps the other's main loop.
+constexpr int kPvThreads = 256;
+constexpr int kPvStageTiles = 1;             // output staging tiles per compute warp
 constexpr int kPvGroupCols = 256;            // output features per tc_pv item (TMEM columns)
 constexpr int kPvChunkKeys = 64;             // keys per pipeline stage
 constexpr int kPvABytes = 128 * kPvChunkKeys * 2;  // P box {64 keys, 128 rows}: 16 KB
 constexpr int kPvBBoxBytes = 64 * kPvChunkKeys * 2;  // Z box {64 features, 64 keys}: 8 KB
 constexpr int kPvStageBytes = kPvABytes + 4 * kPvBBoxBytes;  // 48 KB
-constexpr int kPvStages = 4;
+constexpr int kPvStages = 2;
 constexpr int kPvCtrlBytes = 1536;
 
 struct LongGeom {
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
 // tc_pv: O = P Z per 256-feature group, then the epilogue.
 // ============================================================================
 template <typename T, int ACT>
-__global__ void __launch_bounds__(kPvThreads, 1)
+__global__ void __launch_bounds__(kPvThreads, 2)
     tc_pv(const FwdArgs args, const __grid_constant__ CUtensorMap map_p,
           const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_o,
           const LongGeom geom) {
@@ -368,7 +372,7 @@ __global__ void __launch_bounds__(kPvThreads, 1)
   const uint32_t ring = base;
   const uint32_t staging = base + kPvStages * kPvStageBytes;
   PvCtrl* ctrl = reinterpret_cast<PvCtrl*>(base_ptr + kPvStages * kPvStageBytes +
-                                           8 * kLgStageTiles * kTcOutTileBytes);
+                                           4 * kPvStageTiles * kTcOutTileBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = args.ctx, D = args.feat;
@@ -460,14 +464,14 @@ __global__ void __launch_bounds__(kPvThreads, 1)
       tc_commit(smem_u32(&ctrl->o_full));
     }
   } else if (warp >= 4) {
-    const int cw = warp - 4, h = cw >> 2, wq = warp & 3;
+    const int cw = warp - 4, wq = warp & 3;
     const int row = wq * 32 + lane, i = q_lo + row;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     T* out = static_cast<T*>(args.out) + static_cast<int64_t>(b) * args.o_bs;
     if (skip) {
       // No valid query row in this tile: its output rows are zero.
       const int rows = min(128, C - q_lo);
-      for (int e = cw * 32 + lane; e < rows * width; e += 256) {
+      for (int e = cw * 32 + lane; e < rows * width; e += 32 * (kPvThreads / 32 - 4)) {
         const int r = e / width, f = e % width;
         out[static_cast<int64_t>(q_lo + r) * args.o_rs + f_lo + f] = store_cast<T, float>(0.f);
       }
@@ -492,13 +496,13 @@ __global__ void __launch_bounds__(kPvThreads, 1)
                           (args.zl_rs & 7) == 0 && (args.zl_bs & 7) == 0;
       const uint64_t stream = l2_policy_evict_normal();
       const bool has_bias = args.has_bias;
-      // This warpgroup's columns: [128 h, 128 h + 128) of the group.
-      const int c_lo = 128 * h, c_hi = min(width, 128 * h + 128);
+      // The one compute warpgroup drains every column of the group.
+      const int c_lo = 0, c_hi = width;
       uint32_t gn[16];
       if (zrow && c_lo < c_hi) load_raw32<T>(zrow + f_lo + c_lo, D - f_lo - c_lo, zl_vec, gn, stream);
       mbar_wait(smem_u32(&ctrl->o_full), 0);
       tc_fence_after();
-      const uint32_t stage0 = staging + cw * kLgStageTiles * kTcOutTileBytes;
+      const uint32_t stage0 = staging + cw * kPvStageTiles * kTcOutTileBytes;
 #pragma unroll 1
       for (int c0 = c_lo, n = 0; c0 < c_hi; c0 += 32, ++n) {
         uint32_t o[32], gw[16];
@@ -524,10 +528,10 @@ __global__ void __launch_bounds__(kPvThreads, 1)
           pk[2 * q] = pack2<T>(yv[0], yv[1]);
           pk[2 * q + 1] = pack2<T>(yv[2], yv[3]);
         }
-        if (lane == 0) bulk_wait_read_1();
+        if (lane == 0) bulk_wait_read_all();  // one staging tile per warp
         __syncwarp();
         if (q_lo + wq * 32 < C)
-          warp_tile_store(stage0 + (n & 1) * kTcOutTileBytes, pk, &map_o, f_lo + c0, q_lo + wq * 32,
+          warp_tile_store(stage0, pk, &map_o, f_lo + c0, q_lo + wq * 32,
                           b, stream, lane);
       }
       if (lane == 0) bulk_wait_all();

@@ -12,6 +12,8 @@ oracle): fp32 1e-4, bf16 / fp16 2e-2. fp32 inputs are also held to the
 reference's own kernel bound against fp64 (atol = rtol = 1e-5).
 """
 
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -208,6 +210,51 @@ def test_long_context_exact_properties():
     assert torch.equal(out, avey(tail, w, z_tl=head))
     assert torch.equal(avey(tail * 2, w, z_tl=head), out * 2)
     assert torch.equal(avey(tail[1:3], w, z_tl=head[1:3]), out[1:3])
+
+
+MATRIX = [(op, act) for op in ('avey_causal', 'avey_full', 'avey_b') for act in oracle.ACTIVATIONS]
+
+
+@pytest.mark.parametrize('shape', [(2, 384, 192), (1, 640, 96)], ids=['fused', 'long'])
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16], ids=['bf16', 'f16'])
+@pytest.mark.parametrize('op,act', MATRIX, ids=[f'{o}-{a}' for o, a in MATRIX])
+def test_activation_and_mode_matrix_at_scale(shape, dtype, op, act):
+    """The reference's activation / mode / dtype matrix (tests/test_triton.py:70-95,
+    126-160) at sizes that run the tensor-core kernels: bias, gate, a mask with
+    holes, fp16 and bf16, every activation, causal and full Avey, Avey-B."""
+    b, n, d = shape
+    g = torch.Generator(device='cpu').manual_seed(zlib.crc32(f'{shape}{dtype}{op}{act}'.encode()))
+    # Non-negative tails, as in the reference's matrix tests (torch.rand): the
+    # Avey-B signed row sums stay away from -eps, so relu2 cannot overflow fp16.
+    x = torch.cat([torch.randn(b, n, d, generator=g), torch.rand(b, n, d, generator=g)], -1)
+    x = x.to(dtype).to(DEV)
+    head, tail = x[..., :d], x[..., d:]
+    v = (torch.randn(n, n, generator=g) * 0.05).to(dtype).to(DEV)
+    bias = (torch.randn(d, generator=g) * 0.1).to(dtype).to(DEV)
+    valid = (torch.rand(b, n, generator=g) > 0.15).to(DEV)
+    eps = 0.25  # as in the reference's tiled tests: keeps the signed row sum away from 0
+    if op == 'avey_b':
+        out = avey_b(tail, z_tl=head, bias=bias, valid=valid, eps=eps, activation=act)
+        plan = ops.plan(tail, None, head, bias, valid, causal=False, normalize=True)
+    else:
+        causal = op == 'avey_causal'
+        out = avey(tail, v, z_tl=head, bias=bias, valid=valid, causal=causal, activation=act)
+        plan = ops.plan(tail, v, head, bias, valid, causal=causal, normalize=False)
+    torch.cuda.synchronize()
+    assert plan.kernel == _native.KERNEL_TCGEN05
+    assert plan.launches == (3 if n > 512 else 2)
+    y = to_numpy(out)
+    for r in range(b):
+        zt, zl = to_numpy(tail[r:r + 1]), to_numpy(head[r:r + 1])
+        ok = to_numpy(valid[r:r + 1].float()) > 0
+        kw = dict(z_tl=zl, bias=to_numpy(bias), valid=ok, activation=act)
+        ref = (oracle.avey_b(zt, eps=eps, **kw) if op == 'avey_b'
+               else oracle.avey(zt, to_numpy(v), causal=op == 'avey_causal', **kw))
+        # Finite wherever the reference's result is finite in this dtype.
+        ref_cast = ref.astype(np.float16 if dtype == torch.float16 else np.float32)
+        assert np.isfinite(y[r:r + 1]).all() == np.isfinite(ref_cast).all()
+        assert norm_rel_err(y[r:r + 1], ref) <= TOL['bfloat16'], (r, norm_rel_err(y[r:r + 1], ref))
+        assert (y[r:r + 1][~ok] == 0).all()
 
 
 def test_noncontiguous_and_strided_views():
