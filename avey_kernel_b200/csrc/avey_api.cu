@@ -180,7 +180,7 @@ LongLayout long_layout(const AveyFwdParams* p) {
   l.off_p = l.off_den + align256(static_cast<uint64_t>(B * l.geom.n_groups * C) * sizeof(float));
   l.total = l.off_p + static_cast<uint64_t>(B * C * cp) * 2u;
   l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes +
-              8 * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kLgCtrlBytes;
+              4 * avey::kLgWG * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kLgCtrlBytes;
   l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes +
               4 * avey::kPvStageTiles * avey::kTcOutTileBytes + avey::kPvCtrlBytes;
   return l;

@@ -1,9 +1,9 @@
 // Tensor-core path for contexts longer than 512 tokens (two kernels after the
 // row-norm pre-pass):
 //
-//   tc_gram_p  per (batch row, 128-query tile, group of up to 4 key tiles):
-//              G = Z_q Z_k^T on tcgen05 (TMEM holds 512 fp32 columns, hence
-//              the groups), P = G * rinv_j * V (* rinv_i for fp16) under the
+//   tc_gram_p  per (batch row, 128-query tile, group of up to 2 key tiles):
+//              G = Z_q Z_k^T on tcgen05 (256 fp32 TMEM columns per CTA, two
+//              CTAs per SM), P = G * rinv_j * V (* rinv_i for fp16) under the
 //              masks, written as bf16/f16 to a [B, C, Cp] workspace, plus the
 //              group's partial row sums of P (Avey-B).
 //   tc_pv      per (batch row, 128-query tile, 256-feature group): O = P Z
@@ -22,12 +22,17 @@
 
 namespace avey {
 
-constexpr int kLgThreads = 384;
-constexpr int kLgGroupKeys = 512;            // keys per tc_gram_p item (TMEM columns)
-constexpr int kLgStageBytes = 5 * kTcTileBytesA;  // query tile + 4 key tiles, one 64-feature chunk
+// tc_gram_p: groups of 256 keys (256 TMEM columns), one compute warpgroup,
+// ~107 KB of shared memory: two CTAs share an SM, so one CTA's P phase (CUDA
+// cores, TMA stores) overlaps the other's Gram phase (TMA loads, tcgen05).
+constexpr int kLgWG = 1;                     // compute warpgroups
+constexpr int kLgThreads = 128 + 128 * kLgWG;
+constexpr int kLgGroupKeys = 256;            // keys per tc_gram_p item (TMEM columns)
+constexpr int kLgGroupTiles = kLgGroupKeys / 128;
+constexpr int kLgStageBytes = (1 + kLgGroupTiles) * kTcTileBytesA;  // query + key tiles, one chunk
 constexpr int kLgStages = 2;
-constexpr int kLgStageTiles = 2;             // output staging tiles per compute warp
-constexpr int kLgCtrlBytes = 5120;
+constexpr int kLgStageTiles = 1;             // output staging tiles per compute warp
+constexpr int kLgCtrlBytes = 2048;
 constexpr int kLongMaxContext = 8192;
 
 // tc_pv: 256 threads (producer warp, MMA warp, two idle warps, one compute
@@ -60,7 +65,6 @@ struct LgCtrl {
   int last_valid;
   int exact;
   alignas(16) float rinv[kLgGroupKeys];  // inverse norms of the group's keys (0: not allowed)
-  float den[2][128];
   uint32_t kbits[kLgGroupKeys / 32];
   uint8_t kvalid[kLgGroupKeys];
 };
@@ -119,7 +123,7 @@ __device__ __forceinline__ void warp_tile_store(uint32_t stage, const uint32_t (
 // tc_gram_p: G, then P into the workspace.
 // ============================================================================
 template <typename T>
-__global__ void __launch_bounds__(kLgThreads, 1)
+__global__ void __launch_bounds__(kLgThreads, 2)
     tc_gram_p(const FwdArgs args, const __grid_constant__ CUtensorMap map_k,
               const __grid_constant__ CUtensorMap map_pst, const LongGeom geom) {
   extern __shared__ uint8_t smem_raw[];
@@ -129,7 +133,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
   const uint32_t stage_addr = base;
   const uint32_t staging = base + kLgStages * kLgStageBytes;
   LgCtrl* ctrl = reinterpret_cast<LgCtrl*>(base_ptr + kLgStages * kLgStageBytes +
-                                           8 * kLgStageTiles * kTcOutTileBytes);
+                                           4 * kLgWG * kLgStageTiles * kTcOutTileBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = args.ctx, D = args.feat;
@@ -159,7 +163,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
     tma_prefetch_desc(&map_pst);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&ctrl->tmem_base), 512);
+    tmem_alloc(smem_u32(&ctrl->tmem_base), kLgGroupKeys);
     tmem_relinquish();
   }
   __syncthreads();
@@ -174,7 +178,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
   const int kv_end = ctrl->last_valid + 1;
   const int nkeys = args.causal ? min(kv_end, q_lo + 128) : kv_end;
   const bool skip = q_lo >= kv_end || key0 >= nkeys;
-  const int nk = skip ? 0 : min(4, (nkeys - key0 + 127) / 128);  // key tiles in this group
+  const int nk = skip ? 0 : min(kLgGroupTiles, (nkeys - key0 + 127) / 128);  // key tiles here
   const int q_in = (qt * 128 >= key0 && qt * 128 < key0 + nk * 128) ? (qt - key0 / 128) : -1;
   const int nchunk = (D + kTcChunk - 1) / kTcChunk;
   const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
@@ -209,7 +213,6 @@ __global__ void __launch_bounds__(kLgThreads, 1)
       const uint64_t d0 = smem_desc_sw128(stage_addr, 16, 1024);
       const uint32_t q_adv = static_cast<uint32_t>((q_in >= 0 ? q_in : nk) * kTcTileBytesA) >> 4;
       const uint32_t idesc_g1 = idesc_f16(fmt, 128, nk >= 2 ? 256 : 128, 0, 0);
-      const uint32_t idesc_g2 = idesc_f16(fmt, 128, nk >= 4 ? 256 : 128, 0, 0);
       int st = 0;
       uint32_t ph = 0;
       for (int c = 0; c < nchunk; ++c) {
@@ -220,9 +223,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
 #pragma unroll
         for (int k = 0; k < kTcChunk / 16; ++k) {
           const uint32_t acc = (c != 0 || k != 0) ? 1u : 0u;
-          tc_mma_f16(tmem, dq + 2 * k, dk + 2 * k, idesc_g1, acc);
-          if (nk > 2)
-            tc_mma_f16(tmem + 256, dq + 2 * k, dk + (2 * kTcTileBytesA >> 4) + 2 * k, idesc_g2, acc);
+          tc_mma_f16(tmem, dq + 2 * k, dk + 2 * k, idesc_g1, acc);  // key tiles 0 and 1
         }
         tc_commit(smem_u32(&ctrl->empty[st]));
         if (++st == kLgStages) {
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
     }
   } else if (warp >= 4) {
     // ---- compute warps: inverse norms, then P chunks into the workspace.
-    const int cw = warp - 4, h = cw >> 2, wq = warp & 3;
+    const int cw = warp - 4, wq = warp & 3;
     const int row = wq * 32 + lane, i = q_lo + row;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     if (!skip) {
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
       const float* ssq = args.sumsq + static_cast<int64_t>(b) * C;
       const int tid_c = cw * 32 + lane;
       int nonfinite = 0;
-      for (int j = tid_c; j < nk * 128; j += 256) {
+      for (int j = tid_c; j < nk * 128; j += 128 * kLgWG) {
         const int key = key0 + j;
         const float s2 = key < C ? ssq[key] : 0.f;
         if (key < C && !isfinite(s2)) nonfinite = 1;
@@ -261,7 +262,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
       const float s2q = i < C ? ssq[i] : 0.f;
       if (i < C && !isfinite(s2q)) nonfinite = 1;
       if (nonfinite) ctrl->exact = 1;
-      named_bar_sync(1, 256);
+      named_bar_sync(1, 128 * kLgWG);
       const float rqi = row_ok ? 1.f / fmaxf(sqrtf(s2q), args.norm_eps_f) : 0.f;
       const T* vrow = (args.has_v && i < C)
                           ? static_cast<const T*>(args.v) + static_cast<int64_t>(i) * args.v_rs + key0
@@ -269,9 +270,9 @@ __global__ void __launch_bounds__(kLgThreads, 1)
       const bool v_vec = (reinterpret_cast<uintptr_t>(args.v) & 15u) == 0 && (args.v_rs & 7) == 0;
       const uint64_t keep = l2_policy_evict_last();
       const uint64_t stream = l2_policy_evict_normal();
-      const int split = nk >= 3 ? 256 : nk * 64;
-      const int c_begin = h ? split : 0;
-      const int nch = ((h ? nk * 128 : split) - c_begin) / 32;
+      // The warpgroup covers every key of the group, 32 per chunk.
+      const int c_begin = 0;
+      const int nch = nk * 4;
       const uint32_t one2 = pack2<T>(1.f, 1.f);
       uint32_t vw[16], vn[16], vnn[16];
 #pragma unroll
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
       const bool norm = args.normalize;
       float den4[4] = {0.f, 0.f, 0.f, 0.f};
       const uint32_t stage0 = staging + cw * kLgStageTiles * kTcOutTileBytes;
+      static_assert(kLgStageTiles == 1, "one staging tile per warp: stores wait for the previous read");
 #pragma unroll 1
       for (int ch = 0; ch < nch; ++ch) {
         const int c0 = c_begin + ch * 32;
@@ -323,13 +325,11 @@ __global__ void __launch_bounds__(kLgThreads, 1)
             else p_chunk<T, false, false, false>(g, rk4, rqi, vw, okb, pk, den4);
           }
         }
-        // Two staging tiles per warp: the store issued two chunks ago must
-        // have finished reading the tile this chunk reuses.
-        if (lane == 0) bulk_wait_read_1();
+        // The previous store from this warp's staging tile must have read it.
+        if (lane == 0) bulk_wait_read_all();
         __syncwarp();
         if (key0 + c0 < C && i0 < C)  // the box holds some of the tensor
-          warp_tile_store(stage0 + (ch & 1) * kTcOutTileBytes, pk, &map_pst, key0 + c0, i0, b,
-                          stream, lane);
+          warp_tile_store(stage0, pk, &map_pst, key0 + c0, i0, b, stream, lane);
         if (vrow) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
@@ -338,13 +338,9 @@ __global__ void __launch_bounds__(kLgThreads, 1)
           }
         }
       }
-      if (norm) {
-        ctrl->den[h][row] = (den4[0] + den4[1]) + (den4[2] + den4[3]);
-        named_bar_sync(1, 256);
-        if (h == 0 && i < C)
-          geom.den_part[(static_cast<int64_t>(b) * geom.n_groups + kg) * C + i] =
-              ctrl->den[0][row] + ctrl->den[1][row];
-      }
+      if (norm && i < C)
+        geom.den_part[(static_cast<int64_t>(b) * geom.n_groups + kg) * C + i] =
+            (den4[0] + den4[1]) + (den4[2] + den4[3]);
       if (lane == 0) bulk_wait_all();
     }
   }
@@ -353,7 +349,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kLgGroupKeys);
   }
 }
 

@@ -136,7 +136,7 @@ AVEY_API int avey_fwd_plan(const AveyFwdParams* params, AveyPlan* plan);
 /* Device workspace avey_fwd_v1 needs for these parameters, in bytes: 0 for the
  * CUDA-core kernel; on the tcgen05 path 4 per row of z_tr (batch x context)
  * up to 512 tokens, and above 512 tokens, in 256-byte aligned parts, those
- * row sums, 4 bytes per row per group of 512 keys (partial row sums) and P
+ * row sums, 4 bytes per row per group of 256 keys (partial row sums) and P
  * itself (2 bytes per (query, key) pair, rows padded to 64 keys): 134 MB for
  * batch 16 x 2048 tokens. The workspace must be 256-byte aligned. The
  * reference allocates its normalisation buffer itself (ops.py:113); this

@@ -110,9 +110,9 @@ def test_plan_takes_the_long_context_tcgen05_path_above_512_tokens():
     z = torch.randn(2, 2048, 1024).to(torch.bfloat16)
     plan = ops.plan(z, torch.randn(2048, 2048).to(torch.bfloat16), z_tl=z)
     assert plan.kernel == _native.KERNEL_TCGEN05 and plan.reason == 0
-    # pre-pass, G/P per (query tile, key group), O = P Z: 40 items per batch row
-    # (query tile t has ceil((t + 1) / 4) groups of 512 keys)
-    assert plan.launches == 3 and plan.grid == 2 * 40 and plan.block == 384
+    # pre-pass, G/P per (query tile, key group), O = P Z: 72 items per batch row
+    # (query tile t has ceil((t + 1) / 2) groups of 256 keys)
+    assert plan.launches == 3 and plan.grid == 2 * 72 and plan.block == 256
     assert plan.smem_bytes <= 232_448
 
 
@@ -123,7 +123,7 @@ def test_long_context_workspace_holds_sums_partial_sums_and_p():
     p = ops.build_params(z, None, None, None, None, out, eps=1e-6, norm_eps=1e-12, causal=False,
                          normalize=True, activation_id=0)
     al = lambda x: (x + 255) // 256 * 256
-    groups, padded = (n + 511) // 512, (n + 63) // 64 * 64
+    groups, padded = (n + 255) // 256, (n + 63) // 64 * 64
     assert _native.workspace_size(p) == al(b * n * 4) + al(b * groups * n * 4) + b * n * padded * 2
 
 
