@@ -18,6 +18,7 @@
 #include "ptx.cuh"
 #include "norm_prepass.cuh"
 #include "simt_kernel.cuh"
+#include "simt2_kernel.cuh"
 #include "tc_kernel.cuh"
 #include "tc_long.cuh"
 
@@ -416,6 +417,33 @@ int launch_tc_act(const AveyFwdParams* p, cudaStream_t stream) {
   }
 }
 
+// The two-phase CUDA-core kernel takes fp32 and 16-bit inputs up to 512 tokens.
+bool use_simt2(const AveyFwdParams* p) {
+  return p->dtype != AVEY_F64 && p->context <= avey::kS2MaxCtx;
+}
+
+template <typename T>
+int launch_simt2(const AveyFwdParams* p, cudaStream_t stream) {
+  static std::once_flag attr_once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(avey::simt2_contextualize<T>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, avey::kS2SmemBytes);
+  });
+  if (attr_err != cudaSuccess)
+    return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  const avey::FwdArgs args = make_args(p);
+  const dim3 grid(static_cast<unsigned>((p->context + avey::kS2Rows - 1) / avey::kS2Rows),
+                  static_cast<unsigned>(p->batch));
+  avey::simt2_contextualize<T><<<grid, avey::kS2Threads, avey::kS2SmemBytes, stream>>>(args);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "CUDA-core kernel launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ok();
+}
+
 template <typename T, typename A>
 int launch_simt(const AveyFwdParams* p, cudaStream_t stream) {
   const avey::FwdArgs args = make_args(p);
@@ -457,6 +485,11 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
     plan->grid = static_cast<int32_t>(p->batch * l.geom.n_qtiles);
     plan->block = avey::kTcThreads;
     plan->smem_bytes = l.smem;
+  } else if (use_simt2(p)) {
+    plan->kernel = AVEY_KERNEL_SIMT;
+    plan->grid = static_cast<int32_t>(((p->context + avey::kS2Rows - 1) / avey::kS2Rows) * p->batch);
+    plan->block = avey::kS2Threads;
+    plan->smem_bytes = avey::kS2SmemBytes;
   } else {
     plan->kernel = AVEY_KERNEL_SIMT;
     plan->grid = static_cast<int32_t>(((p->context + 15) / 16) * ((p->features + 127) / 128) *
@@ -491,6 +524,13 @@ int avey_fwd_v1(const AveyFwdParams* p, void* stream_ptr) {
   if (plan.kernel == AVEY_KERNEL_TCGEN05) {
     return p->dtype == AVEY_BF16 ? launch_tc_act<__nv_bfloat16>(p, stream)
                                  : launch_tc_act<__half>(p, stream);
+  }
+  if (use_simt2(p)) {
+    switch (p->dtype) {
+      case AVEY_F32: return launch_simt2<float>(p, stream);
+      case AVEY_F16: return launch_simt2<__half>(p, stream);
+      default: return launch_simt2<__nv_bfloat16>(p, stream);
+    }
   }
   switch (p->dtype) {
     case AVEY_F32: return launch_simt<float, float>(p, stream);
