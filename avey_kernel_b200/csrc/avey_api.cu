@@ -417,19 +417,18 @@ int launch_tc_act(const AveyFwdParams* p, cudaStream_t stream) {
   }
 }
 
-// The two-phase CUDA-core kernel takes fp32 and 16-bit inputs up to 512 tokens.
-bool use_simt2(const AveyFwdParams* p) {
-  return p->dtype != AVEY_F64 && p->context <= avey::kS2MaxCtx;
-}
+// The two-phase CUDA-core kernel takes every fp32 and 16-bit input the
+// tensor-core kernels do not; fp64 keeps simt_contextualize.
+bool use_simt2(const AveyFwdParams* p) { return p->dtype != AVEY_F64; }
 
-template <typename T>
+template <typename T, bool LONG>
 int launch_simt2(const AveyFwdParams* p, cudaStream_t stream) {
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(avey::simt2_contextualize<T>,
+    attr_err = cudaFuncSetAttribute(avey::simt2_contextualize<T, LONG>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, avey::kS2SmemBytes);
   });
   if (attr_err != cudaSuccess)
@@ -437,7 +436,7 @@ int launch_simt2(const AveyFwdParams* p, cudaStream_t stream) {
   const avey::FwdArgs args = make_args(p);
   const dim3 grid(static_cast<unsigned>((p->context + avey::kS2Rows - 1) / avey::kS2Rows),
                   static_cast<unsigned>(p->batch));
-  avey::simt2_contextualize<T><<<grid, avey::kS2Threads, avey::kS2SmemBytes, stream>>>(args);
+  avey::simt2_contextualize<T, LONG><<<grid, avey::kS2Threads, avey::kS2SmemBytes, stream>>>(args);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "CUDA-core kernel launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -526,10 +525,13 @@ int avey_fwd_v1(const AveyFwdParams* p, void* stream_ptr) {
                                  : launch_tc_act<__half>(p, stream);
   }
   if (use_simt2(p)) {
+    const bool lng = p->context > avey::kS2MaxCtx;
     switch (p->dtype) {
-      case AVEY_F32: return launch_simt2<float>(p, stream);
-      case AVEY_F16: return launch_simt2<__half>(p, stream);
-      default: return launch_simt2<__nv_bfloat16>(p, stream);
+      case AVEY_F32: return lng ? launch_simt2<float, true>(p, stream) : launch_simt2<float, false>(p, stream);
+      case AVEY_F16: return lng ? launch_simt2<__half, true>(p, stream) : launch_simt2<__half, false>(p, stream);
+      default:
+        return lng ? launch_simt2<__nv_bfloat16, true>(p, stream)
+                   : launch_simt2<__nv_bfloat16, false>(p, stream);
     }
   }
   switch (p->dtype) {

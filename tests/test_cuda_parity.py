@@ -257,6 +257,33 @@ def test_activation_and_mode_matrix_at_scale(shape, dtype, op, act):
         assert (y[r:r + 1][~ok] == 0).all()
 
 
+@pytest.mark.parametrize('op', ['avey', 'avey_b'])
+def test_fp32_long_context_cuda_core_path(op):
+    """fp32 rows above 512 tokens: the CUDA-core kernel's 512-key super-blocks."""
+    g = torch.Generator(device='cpu').manual_seed(21)
+    b, n, d = 2, 1100, 72
+    x = torch.randn(b, n, 2 * d, generator=g).to(DEV)
+    if op == 'avey_b':  # non-negative tails keep the signed row sums well away from -eps
+        x[..., d:] = x[..., d:].abs()
+    head, tail = x[..., :d], x[..., d:]
+    valid = (torch.rand(b, n, generator=g) > 0.1).to(DEV)
+    plan = ops.plan(tail, z_tl=head, causal=op == 'avey', normalize=op == 'avey_b')
+    assert plan.kernel == _native.KERNEL_SIMT and plan.block == 256
+    if op == 'avey':
+        v = torch.randn(n, n, generator=g).to(DEV) * 0.05
+        out = avey(tail, v, z_tl=head, valid=valid, activation='silu')
+    else:
+        out = avey_b(tail, z_tl=head, valid=valid, eps=0.25, activation='gelu')
+    torch.cuda.synchronize()
+    y = to_numpy(out)
+    for r in range(b):
+        zt, zl = to_numpy(tail[r:r + 1]), to_numpy(head[r:r + 1])
+        ok = to_numpy(valid[r:r + 1].float()) > 0
+        ref = (oracle.avey(zt, to_numpy(v), z_tl=zl, valid=ok, activation='silu') if op == 'avey'
+               else oracle.avey_b(zt, z_tl=zl, valid=ok, eps=0.25, activation='gelu'))
+        assert norm_rel_err(y[r:r + 1], ref) <= TOL['float32'], (r, norm_rel_err(y[r:r + 1], ref))
+
+
 def test_noncontiguous_and_strided_views():
     z = torch.rand(2, 37, 35, device=DEV).transpose(1, 2)
     ref = oracle.avey_b(to_numpy(z))
