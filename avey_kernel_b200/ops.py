@@ -21,6 +21,7 @@ otherwise ignored: the CUDA kernels pick their tiling from the shape.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -133,15 +134,38 @@ def contextualize(z_tr: torch.Tensor, v: Optional[torch.Tensor], z_tl: Optional[
                           causal=causal, normalize=normalize, activation_id=activation,
                           kernel=variant)
     nbytes = _native.workspace_size(params)
+    batch = z_tr.shape[0]
+    # The workspace grows linearly with the batch (above 512 tokens it holds
+    # P, 2 bytes per (query, key) pair); past the cap, batch slices run one
+    # after the other on one workspace, so memory stays bounded.
+    per_row = -(-nbytes // batch) if nbytes else 0
+    step = batch if nbytes <= _workspace_cap() else max(1, _workspace_cap() // max(per_row, 1))
+    stream = torch.cuda.current_stream(z_tr.device).cuda_stream
     workspace = None
-    if nbytes:
-        # Scratch from torch's caching allocator (stream-ordered, graph-safe).
-        workspace = torch.empty(nbytes, dtype=torch.uint8, device=z_tr.device)
-        params.workspace = workspace.data_ptr()
-        params.workspace_bytes = nbytes
     with torch.cuda.device(z_tr.device):
-        _native.forward(params, torch.cuda.current_stream(z_tr.device).cuda_stream)
+        for b0 in range(0, batch, step):
+            b1 = min(batch, b0 + step)
+            if step != batch:
+                sl = slice(b0, b1)
+                params = build_params(z_tr[sl], v, z_tl[sl] if z_tl is not None else None, bias,
+                                      valid[sl] if valid is not None else None, out[sl], eps=eps,
+                                      norm_eps=norm_eps, causal=causal, normalize=normalize,
+                                      activation_id=activation, kernel=variant)
+                nbytes = _native.workspace_size(params)
+            if nbytes:
+                if workspace is None or workspace.numel() < nbytes:
+                    # Scratch from torch's caching allocator (stream-ordered, graph-safe).
+                    workspace = torch.empty(nbytes, dtype=torch.uint8, device=z_tr.device)
+                params.workspace = workspace.data_ptr()
+                params.workspace_bytes = nbytes
+            _native.forward(params, stream)
     return out
+
+
+def _workspace_cap() -> int:
+    """Largest workspace one launch sequence may use (bytes); the
+    AVEY_B200_MAX_WORKSPACE_MB environment variable overrides 2048 MB."""
+    return int(os.environ.get('AVEY_B200_MAX_WORKSPACE_MB', '2048')) << 20
 
 
 @contextualize.register_fake

@@ -284,6 +284,22 @@ def test_fp32_long_context_cuda_core_path(op):
         assert norm_rel_err(y[r:r + 1], ref) <= TOL['float32'], (r, norm_rel_err(y[r:r + 1], ref))
 
 
+def test_long_context_batch_slices_under_a_workspace_cap(monkeypatch):
+    """Above the workspace cap the op runs batch slices on one workspace;
+    batch rows are independent, so the result is bitwise the same."""
+    g = torch.Generator(device='cpu').manual_seed(13)
+    x = torch.randn(5, 700, 2 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(700, 700, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    head, tail = x[..., :64], x[..., 64:]
+    whole = avey(tail, w, z_tl=head)
+    monkeypatch.setenv('AVEY_B200_MAX_WORKSPACE_MB', '2')  # ~1 MB per batch row: slices of 2
+    before = _native.launch_count()
+    sliced = avey(tail, w, z_tl=head)
+    torch.cuda.synchronize()
+    assert _native.launch_count() == before + 3 * 3  # three slices, three launches each
+    assert torch.equal(sliced, whole)
+
+
 def test_noncontiguous_and_strided_views():
     z = torch.rand(2, 37, 35, device=DEV).transpose(1, 2)
     ref = oracle.avey_b(to_numpy(z))
