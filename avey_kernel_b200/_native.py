@@ -23,9 +23,11 @@ STATUS_NAMES = {
 
 # Exported symbols, mirrored from include/avey_b200.h (tests check the header).
 EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_fwd_workspace_size', 'avey_fwd_noalloc_v1',
+           'avey_bwd_step_v1', 'avey_bwd_workspace_size',
            'avey_last_error', 'avey_device_status', 'avey_launch_count', 'avey_abi_version')
+BWD_PREP, BWD_SCORES, BWD_EPILOGUE, BWD_DSCORES, BWD_FINAL = range(5)
 NOALLOC_MAX_ROWS = 1 << 20
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class AveyFwdParams(ctypes.Structure):
@@ -58,6 +60,55 @@ class AveyFwdParams(ctypes.Structure):
         ('kernel', ctypes.c_int32),
         ('workspace', ctypes.c_void_p),
         ('workspace_bytes', ctypes.c_uint64),
+    ]
+
+
+class AveyBwdParams(ctypes.Structure):
+    _fields_ = [
+        ('struct_size', ctypes.c_uint32),
+        ('dtype', ctypes.c_int32),
+        ('gemm_dtype', ctypes.c_int32),
+        ('causal', ctypes.c_int32),
+        ('normalize', ctypes.c_int32),
+        ('activation', ctypes.c_int32),
+        ('batch', ctypes.c_int64),
+        ('context', ctypes.c_int64),
+        ('features', ctypes.c_int64),
+        ('eps', ctypes.c_double),
+        ('norm_eps', ctypes.c_double),
+        ('z_tr', ctypes.c_void_p),
+        ('z_tr_batch_stride', ctypes.c_int64),
+        ('z_tr_row_stride', ctypes.c_int64),
+        ('v', ctypes.c_void_p),
+        ('v_row_stride', ctypes.c_int64),
+        ('z_tl', ctypes.c_void_p),
+        ('z_tl_batch_stride', ctypes.c_int64),
+        ('z_tl_row_stride', ctypes.c_int64),
+        ('bias', ctypes.c_void_p),
+        ('valid', ctypes.c_void_p),
+        ('valid_batch_stride', ctypes.c_int64),
+        ('valid_row_stride', ctypes.c_int64),
+        ('grad_out', ctypes.c_void_p),
+        ('grad_out_batch_stride', ctypes.c_int64),
+        ('grad_out_row_stride', ctypes.c_int64),
+        ('zm', ctypes.c_void_p),
+        ('norms', ctypes.c_void_p),
+        ('g', ctypes.c_void_p),
+        ('s', ctypes.c_void_p),
+        ('den', ctypes.c_void_p),
+        ('num', ctypes.c_void_p),
+        ('dnum', ctypes.c_void_p),
+        ('dden', ctypes.c_void_p),
+        ('ds0', ctypes.c_void_p),
+        ('dgsym', ctypes.c_void_p),
+        ('dzd', ctypes.c_void_p),
+        ('dzh', ctypes.c_void_p),
+        ('workspace', ctypes.c_void_p),
+        ('workspace_bytes', ctypes.c_uint64),
+        ('grad_z_tr', ctypes.c_void_p),
+        ('grad_v', ctypes.c_void_p),
+        ('grad_z_tl', ctypes.c_void_p),
+        ('grad_bias', ctypes.c_void_p),
     ]
 
 
@@ -112,6 +163,12 @@ def lib() -> ctypes.CDLL:
         dll.avey_fwd_workspace_size.restype = ctypes.c_int
         dll.avey_fwd_noalloc_v1.argtypes = [ctypes.POINTER(AveyFwdParams), ctypes.c_void_p]
         dll.avey_fwd_noalloc_v1.restype = ctypes.c_int
+        dll.avey_bwd_step_v1.argtypes = [ctypes.POINTER(AveyBwdParams), ctypes.c_int,
+                                         ctypes.c_void_p]
+        dll.avey_bwd_step_v1.restype = ctypes.c_int
+        dll.avey_bwd_workspace_size.argtypes = [ctypes.POINTER(AveyBwdParams),
+                                                ctypes.POINTER(ctypes.c_uint64)]
+        dll.avey_bwd_workspace_size.restype = ctypes.c_int
         dll.avey_last_error.argtypes = []
         dll.avey_last_error.restype = ctypes.c_char_p
         dll.avey_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
@@ -153,6 +210,17 @@ def workspace_size(params: AveyFwdParams) -> int:
     return int(out.value)
 
 
+def bwd_step(params: AveyBwdParams, step: int, stream: int) -> None:
+    """avey_bwd_step_v1: enqueue one backward step on `stream`."""
+    _check(lib().avey_bwd_step_v1(ctypes.byref(params), int(step), ctypes.c_void_p(stream)))
+
+
+def bwd_workspace_size(params: AveyBwdParams) -> int:
+    out = ctypes.c_uint64(0)
+    _check(lib().avey_bwd_workspace_size(ctypes.byref(params), ctypes.byref(out)))
+    return int(out.value)
+
+
 def device_status(clear: bool = False) -> int:
     flags = ctypes.c_uint32(0)
     _check(lib().avey_device_status(ctypes.byref(flags), int(clear)))
@@ -161,6 +229,12 @@ def device_status(clear: bool = False) -> int:
 
 def launch_count() -> int:
     return int(lib().avey_launch_count())
+
+
+def new_bwd_params() -> AveyBwdParams:
+    p = AveyBwdParams()
+    p.struct_size = ctypes.sizeof(AveyBwdParams)
+    return p
 
 
 def new_params() -> AveyFwdParams:

@@ -458,6 +458,14 @@ int launch_simt(const AveyFwdParams* p, cudaStream_t stream) {
 
 }  // namespace
 
+// Shared with the backward translation unit (avey_bwd.cu): one last-error
+// string per thread and one launch counter for the whole library.
+namespace avey_host {
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+int clear_error() { return ok(); }
+void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+}  // namespace avey_host
+
 extern "C" {
 
 int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {

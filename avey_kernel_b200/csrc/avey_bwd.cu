@@ -1,0 +1,218 @@
+// C ABI of the backward steps (declared in include/avey_b200.h): argument
+// checks, type dispatch and launches of bwd_kernels.cuh.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+
+#include "avey_b200.h"
+#include "bwd_kernels.cuh"
+
+namespace avey_host {
+int set_error(int code, const char* msg);
+int clear_error();
+void count_launches(int n);
+}  // namespace avey_host
+
+namespace {
+
+int fail(int code, const char* msg) { return avey_host::set_error(code, msg); }
+
+int expected_gemm_dtype(int dtype) {
+  switch (dtype) {
+    case AVEY_BF16: return AVEY_BF16;
+    case AVEY_F16:
+    case AVEY_F32: return AVEY_F32;
+    case AVEY_F64: return AVEY_F64;
+    default: return -1;
+  }
+}
+
+int acc_size(const AveyBwdParams* p) { return p->dtype == AVEY_F64 ? 8 : 4; }
+
+int64_t epi_blocks(const AveyBwdParams* p) {
+  return (p->batch * p->context + avey::kBwdEpiRows - 1) / avey::kBwdEpiRows;
+}
+
+// dscores grid: tile pairs x batch groups, enough CTAs to fill the GPU.
+void dscores_grid(const AveyBwdParams* p, int* pairs, int* groups, int* per_group) {
+  const int nt = static_cast<int>((p->context + avey::kBwdTile - 1) / avey::kBwdTile);
+  *pairs = nt * (nt + 1) / 2;
+  int g = std::max(1, std::min(static_cast<int>(p->batch), (1184 + *pairs - 1) / *pairs));
+  g = std::min(g, 16);  // bounds the dV partial sums (16 x C x C)
+  *per_group = static_cast<int>((p->batch + g - 1) / g);
+  *groups = static_cast<int>((p->batch + *per_group - 1) / *per_group);
+}
+
+uint64_t workspace_bytes(const AveyBwdParams* p) {
+  int pairs, groups, per;
+  dscores_grid(p, &pairs, &groups, &per);
+  const uint64_t epi = static_cast<uint64_t>(epi_blocks(p)) * p->features;
+  const uint64_t ds = p->v ? static_cast<uint64_t>(groups) * p->context * p->context : 0;
+  return std::max(epi, ds) * acc_size(p);
+}
+
+int validate(const AveyBwdParams* p) {
+  if (!p) return fail(AVEY_ERR_ARGUMENT, "params is NULL");
+  if (p->struct_size != sizeof(AveyBwdParams))
+    return fail(AVEY_ERR_ARGUMENT, "struct_size does not match sizeof(AveyBwdParams)");
+  if (expected_gemm_dtype(p->dtype) < 0) return fail(AVEY_ERR_ARGUMENT, "unknown dtype");
+  if (p->gemm_dtype != expected_gemm_dtype(p->dtype))
+    return fail(AVEY_ERR_ARGUMENT, "gemm_dtype must be bf16 for bf16 inputs, f32 for f16/f32, f64 for f64");
+  if (p->batch < 1 || p->context < 1 || p->features < 1 || p->batch > 65535 ||
+      p->context > (1 << 16) || p->features > (1 << 24))
+    return fail(AVEY_ERR_ARGUMENT, "batch, context and features out of range");
+  if (p->activation < 0 || p->activation > 4) return fail(AVEY_ERR_ARGUMENT, "unknown activation");
+  if (!std::isfinite(p->eps) || p->eps <= 0 || !std::isfinite(p->norm_eps) || p->norm_eps <= 0)
+    return fail(AVEY_ERR_ARGUMENT, "eps and norm_eps must be finite and positive");
+  if (!p->z_tr || p->z_tr_row_stride < p->features || p->z_tr_batch_stride < 0 ||
+      (p->z_tl && (p->z_tl_row_stride < p->features || p->z_tl_batch_stride < 0)) ||
+      (p->v && p->v_row_stride < p->context) || p->valid_batch_stride < 0 ||
+      p->valid_row_stride < 0)
+    return fail(AVEY_ERR_ARGUMENT, "z_tr is required and strides must cover the rows");
+  return AVEY_OK;
+}
+
+avey::BwdArgs make_args(const AveyBwdParams* p) {
+  avey::BwdArgs a{};
+  a.z_tr = p->z_tr;
+  a.v = p->v;
+  a.z_tl = p->z_tl;
+  a.bias = p->bias;
+  a.valid = p->valid;
+  a.gout = p->grad_out;
+  a.zr_bs = p->z_tr_batch_stride;
+  a.zr_rs = p->z_tr_row_stride;
+  a.v_rs = p->v_row_stride;
+  a.zl_bs = p->z_tl_batch_stride;
+  a.zl_rs = p->z_tl_row_stride;
+  a.va_bs = p->valid_batch_stride;
+  a.va_rs = p->valid_row_stride;
+  a.go_bs = p->grad_out_batch_stride;
+  a.go_rs = p->grad_out_row_stride;
+  a.batch = static_cast<int>(p->batch);
+  a.ctx = static_cast<int>(p->context);
+  a.feat = static_cast<int>(p->features);
+  a.eps = p->eps;
+  a.norm_eps = p->norm_eps;
+  a.causal = p->causal != 0;
+  a.normalize = p->normalize != 0;
+  a.act = p->activation;
+  a.zm = p->zm;
+  a.norms = p->norms;
+  a.g = p->g;
+  a.s = p->s;
+  a.den = p->den;
+  a.num = p->num;
+  a.dnum = p->dnum;
+  a.dden = p->dden;
+  a.ds0 = p->ds0;
+  a.dgsym = p->dgsym;
+  a.dzd = p->dzd;
+  a.dzh = p->dzh;
+  a.part = p->workspace;
+  a.gz_tr = p->grad_z_tr;
+  a.gv = p->v ? p->grad_v : nullptr;
+  a.gz_tl = p->z_tl ? p->grad_z_tl : nullptr;
+  a.gbias = p->bias ? p->grad_bias : nullptr;
+  return a;
+}
+
+int launched(int n) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "backward launch: %s", cudaGetErrorString(e));
+    return fail(AVEY_ERR_LAUNCH, buf);
+  }
+  avey_host::count_launches(n);
+  return avey_host::clear_error();
+}
+
+int row_grid(const AveyBwdParams* p) {
+  const int64_t warps = p->batch * p->context;
+  return static_cast<int>(std::min<int64_t>((warps + 7) / 8, 148 * 16));
+}
+
+template <typename T, typename G, typename A>
+int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
+  const avey::BwdArgs a = make_args(p);
+  constexpr int kT = avey::kBwdThreads;
+  switch (step) {
+    case AVEY_BWD_PREP:
+      if (!p->zm || !p->norms) return fail(AVEY_ERR_ARGUMENT, "prep needs zm, norms");
+      avey::bwd_prep<T, G, A><<<row_grid(p), kT, 0, st>>>(a);
+      return launched(1);
+    case AVEY_BWD_SCORES:
+      if (!p->g || !p->s || !p->den || !p->norms)
+        return fail(AVEY_ERR_ARGUMENT, "scores needs g, s, den, norms");
+      avey::bwd_scores<T, G, A><<<row_grid(p), kT, 0, st>>>(a);
+      return launched(1);
+    case AVEY_BWD_EPILOGUE: {
+      if (!p->num || !p->den || !p->dnum || !p->dden || !p->grad_out || !p->workspace ||
+          p->workspace_bytes < workspace_bytes(p))
+        return fail(AVEY_ERR_ARGUMENT, "epilogue needs num, den, dnum, dden, grad_out, workspace");
+      const int64_t nb = epi_blocks(p);
+      avey::bwd_epilogue<T, G, A><<<static_cast<unsigned>(nb), kT, 0, st>>>(a);
+      int n = 1;
+      if (a.gbias) {
+        avey::bwd_reduce<T, A><<<static_cast<unsigned>((p->features + 31) / 32), kT, 0, st>>>(
+            static_cast<const A*>(p->workspace), static_cast<int>(nb), p->features,
+            static_cast<T*>(p->grad_bias));
+        ++n;
+      }
+      return launched(n);
+    }
+    case AVEY_BWD_DSCORES: {
+      if (!p->ds0 || !p->g || !p->dden || !p->dgsym || !p->norms || (a.gv && (!p->workspace ||
+                                                             p->workspace_bytes < workspace_bytes(p))))
+        return fail(AVEY_ERR_ARGUMENT, "dscores needs ds0, g, dden, dgsym (and workspace for grad_v)");
+      int pairs, groups, per;
+      dscores_grid(p, &pairs, &groups, &per);
+      avey::bwd_dscores<T, G, A><<<dim3(pairs, groups), kT, 0, st>>>(a, per);
+      int n = 1;
+      if (a.gv) {
+        const int64_t cc = p->context * p->context;
+        avey::bwd_reduce<T, A><<<static_cast<unsigned>((cc + 31) / 32), kT, 0, st>>>(
+            static_cast<const A*>(p->workspace), groups, cc, static_cast<T*>(p->grad_v));
+        ++n;
+      }
+      return launched(n);
+    }
+    case AVEY_BWD_FINAL:
+      if (!p->zm || !p->norms || !p->dzh || !p->dzd || !p->grad_z_tr)
+        return fail(AVEY_ERR_ARGUMENT, "final needs zm, norms, dzh, dzd, grad_z_tr");
+      avey::bwd_final<T, G, A><<<row_grid(p), kT, 0, st>>>(a);
+      return launched(1);
+    default:
+      return fail(AVEY_ERR_ARGUMENT, "unknown backward step");
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int avey_bwd_workspace_size(const AveyBwdParams* p, uint64_t* bytes) {
+  int rc = validate(p);
+  if (rc != AVEY_OK) return rc;
+  if (!bytes) return fail(AVEY_ERR_ARGUMENT, "bytes is NULL");
+  *bytes = workspace_bytes(p);
+  return avey_host::clear_error();
+}
+
+int avey_bwd_step_v1(const AveyBwdParams* p, int step, void* stream) {
+  int rc = validate(p);
+  if (rc != AVEY_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (p->dtype) {
+    case AVEY_BF16: return run_step<__nv_bfloat16, __nv_bfloat16, float>(p, step, st);
+    case AVEY_F16: return run_step<__half, float, float>(p, step, st);
+    case AVEY_F32: return run_step<float, float, float>(p, step, st);
+    case AVEY_F64: return run_step<double, double, double>(p, step, st);
+    default: return fail(AVEY_ERR_ARGUMENT, "unknown dtype");
+  }
+}
+
+}  // extern "C"

@@ -18,8 +18,9 @@ PKG = CSRC.parent
 ROOT = PKG.parent
 LIB_DIR = PKG / 'lib'
 LIB = LIB_DIR / 'libavey_b200.so'
-SOURCES = ['avey_api.cu']
-HEADERS = ['ptx.cuh', 'common.cuh', 'norm_prepass.cuh', 'simt_kernel.cuh', 'tc_kernel.cuh']
+SOURCES = ['avey_api.cu', 'avey_bwd.cu']
+HEADERS = ['ptx.cuh', 'common.cuh', 'norm_prepass.cuh', 'simt_kernel.cuh', 'simt2_kernel.cuh',
+           'tc_kernel.cuh', 'tc_long.cuh', 'bwd_kernels.cuh']
 
 NVCC_FLAGS = [
     '-gencode', 'arch=compute_100a,code=sm_100a',

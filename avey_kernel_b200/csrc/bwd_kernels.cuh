@@ -1,0 +1,428 @@
+// Backward of the contextualizer: the elementwise and reduction steps that
+// sit between the batched GEMMs of the gradient.
+//
+// Per batch row (Z = z_tr with padded rows zeroed, r = 1 / max(||Z||, ne),
+// z^ = r Z, G = z^ z^T, S = G (.) V (.) M, num = S Z, den = rowsum(S) + eps, Y0 = num /
+// den for Avey-B (num for Avey), Ypre = Y0 + bias, out = act(Ypre) (.) gate,
+// rows of padded queries zeroed), the gradient is
+//
+//   dYpre = dout (.) gate (.) act'(Ypre)     dgate = dout (.) act(Ypre)
+//   dbias = sum over rows of dYpre
+//   dnum  = dYpre / den,  dden_i = -sum_f dYpre_if Y0_if / den_i   (Avey-B)
+//   dS    = (dnum Z^T + dden 1^T) (.) M         dV = sum_b dS (.) G
+//   dG    = dS (.) V,  dz^ = (dG + dG^T) z^,    dZ = S^T dnum + dz^ through
+//           the normalisation (dz^ - z^ (z^ . dz^)) / ||Z||  (or dz^ / ne when
+//           ||Z|| < ne), zero on padded rows.
+//
+// The five products are plain batched GEMMs run by the caller between these
+// steps, all on Z itself (exact in the input type): Gr = Z Z^T (G = r_i r_j Gr),
+// num = S Z, dnum Z^T, S^T dnum and (dGsym diag(r)) Z = dz^. Folding the norms
+// into the fp32 steps instead of rounding z^ to a 16-bit GEMM operand keeps the
+// Gram exact to fp32, as in the forward kernels. Every step here is one launch
+// that streams its operands once; reductions (dbias, dV, dden) use fixed
+// orders, so gradients are bitwise reproducible.
+//
+// Reference: torch autograd through avey_kernels/ops.py:66-96 (_reference):
+// masked_fill before the arithmetic (ops.py:69-72), F.normalize (73), the
+// masks (74-82), numerator / denominator (83-85), bias (86-87), activation
+// (ops.py:54-63), gate and final row mask (89-94).
+#pragma once
+
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace avey {
+
+// Plain-old-data copy of AveyBwdParams for kernels.
+struct BwdArgs {
+  const void* z_tr;
+  const void* v;
+  const void* z_tl;
+  const void* bias;
+  const uint8_t* valid;
+  const void* gout;
+  int64_t zr_bs, zr_rs, v_rs, zl_bs, zl_rs, va_bs, va_rs, go_bs, go_rs;
+  int batch, ctx, feat;
+  double eps, norm_eps;
+  int causal, normalize, act;
+  void* zm;     // [B, C, d]  GEMM type: Z (padded rows zeroed)
+  void* norms;  // [B, C]     acc: ||Z||
+  void* g;      // [B, C, C]  acc: Z Z^T
+  void* s;      // [B, C, C]  GEMM type: S
+  void* den;    // [B, C]     acc: rowsum(S) + eps
+  void* num;    // [B, C, d]  acc: S Z
+  void* dnum;   // [B, C, d]  GEMM type
+  void* dden;   // [B, C]     acc
+  void* ds0;    // [B, C, C]  acc: dnum Z^T
+  void* dgsym;  // [B, C, C]  GEMM type: (dG + dG^T) diag(r)
+  void* dzd;    // [B, C, d]  acc: S^T dnum
+  void* dzh;    // [B, C, d]  acc: dz^ = dgsym Z
+  void* part;   // acc partial sums (dbias, dV)
+  void* gz_tr;  // [B, C, d]  input type
+  void* gv;     // [C, C]
+  void* gz_tl;  // [B, C, d]
+  void* gbias;  // [d]
+};
+
+constexpr int kBwdThreads = 256;
+constexpr int kBwdEpiRows = 64;   // rows per epilogue block (8 per warp)
+constexpr int kBwdEpiChunk = 256; // features per epilogue pass (8 per lane)
+constexpr int kBwdTile = 32;      // dscores tile edge
+
+template <typename A, typename T>
+__device__ __forceinline__ A ld_as(const T* p) {
+  if constexpr (std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value) {
+    return static_cast<A>(Elem<T>::load(p));
+  } else {
+    return static_cast<A>(__ldg(p));
+  }
+}
+
+template <typename T, typename A>
+__device__ __forceinline__ void st_as(T* p, A x) {
+  *p = store_cast<T, A>(x);
+}
+
+// r = 1 / max(||Z||, ne) of row `row` (flattened batch x context index).
+template <typename A>
+__device__ __forceinline__ A inv_norm(const BwdArgs& a, int64_t row) {
+  const A n = static_cast<const A*>(a.norms)[row];
+  const A ne = static_cast<A>(a.norm_eps);
+  return A(1) / (n > ne ? n : ne);
+}
+
+__device__ __forceinline__ bool row_valid(const BwdArgs& a, int b, int n) {
+  return !a.valid || a.valid[static_cast<int64_t>(b) * a.va_bs + static_cast<int64_t>(n) * a.va_rs] != 0;
+}
+
+template <typename A>
+__device__ __forceinline__ A warp_sum(A x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Derivative of the activations of the reference (ops.py:54-63) at x, with
+// torch's conventions: relu' = [x > 0]; relu2' = 2 max(x, 0); silu' =
+// s (1 + x (1 - s)); tanh-gelu' = 0.5 (1 + t) + 0.5 x (1 - t^2) k (1 + 3 c x^2),
+// t = tanh(k (x + c x^3)), k = sqrt(2 / pi), c = 0.044715.
+template <typename A>
+__device__ __forceinline__ A activate_grad(A x, int act) {
+  switch (act) {
+    case 1:
+      return x > A(0) ? A(1) : A(0);
+    case 2:
+      return x > A(0) ? A(2) * x : A(0);
+    case 3: {
+      const A sg = sigmoid_stable(x);
+      return sg * (A(1) + x * (A(1) - sg));
+    }
+    case 4: {
+      const A k = A(0.7978845608028654), c = A(0.044715);
+      const A t = tanh(k * (x + c * x * x * x));
+      return A(0.5) * (A(1) + t) + A(0.5) * x * (A(1) - t * t) * k * (A(1) + A(3) * c * x * x);
+    }
+    default:
+      return A(1);
+  }
+}
+
+// Step 1: Z (padded rows zeroed) in the GEMM type and ||Z|| per row. One warp
+// per row.
+template <typename T, typename G, typename A>
+__global__ void __launch_bounds__(kBwdThreads) bwd_prep(const BwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
+  const int d = a.feat;
+  const T* z = static_cast<const T*>(a.z_tr);
+  G* zm = static_cast<G*>(a.zm);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
+       r += nwarps) {
+    const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
+    const bool ok = row_valid(a, b, n);
+    const T* zr = z + static_cast<int64_t>(b) * a.zr_bs + static_cast<int64_t>(n) * a.zr_rs;
+    A ss = 0;
+    if (ok)
+      for (int f = lane; f < d; f += 32) {
+        const A x = ld_as<A>(zr + f);
+        ss += x * x;
+      }
+    ss = warp_sum(ss);
+    for (int f = lane; f < d; f += 32) st_as<G>(zm + r * d + f, ok ? ld_as<A>(zr + f) : A(0));
+    if (lane == 0) static_cast<A*>(a.norms)[r] = sqrt(ss);
+  }
+}
+
+// Step 2: S = r_i r_j Gr (.) V (.) M (GEMM type) and den = rowsum(S) + eps.
+// One warp per (batch, query) row.
+template <typename T, typename G, typename A>
+__global__ void __launch_bounds__(kBwdThreads) bwd_scores(const BwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
+  const int C = a.ctx;
+  const A* gr = static_cast<const A*>(a.g);
+  G* s = static_cast<G*>(a.s);
+  const T* v = static_cast<const T*>(a.v);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
+       r += nwarps) {
+    const int b = static_cast<int>(r / C), i = static_cast<int>(r % C);
+    const A ri = inv_norm<A>(a, r);
+    A sum = 0;
+    for (int j = lane; j < C; j += 32) {
+      const bool allowed = (!a.causal || j <= i) && row_valid(a, b, j);
+      A x = A(0);
+      if (allowed) {
+        x = gr[r * C + j] * ri * inv_norm<A>(a, static_cast<int64_t>(b) * C + j);
+        if (v) x *= ld_as<A>(v + static_cast<int64_t>(i) * a.v_rs + j);
+      }
+      st_as<G>(s + r * C + j, x);
+      sum += x;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) static_cast<A*>(a.den)[r] = sum + static_cast<A>(a.eps);
+  }
+}
+
+// Step 3: epilogue backward. A block owns 64 consecutive (batch, query) rows
+// (8 per warp) and walks the features in passes of 256 (8 per lane): it
+// writes dgate and dnum, the per-row dden, and its partial dbias (one row of
+// `part` per block, summed in block order by bwd_reduce).
+template <typename T, typename G, typename A>
+__global__ void __launch_bounds__(kBwdThreads) bwd_epilogue(const BwdArgs a) {
+  __shared__ A red[kBwdThreads / 32][kBwdEpiChunk];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int d = a.feat, C = a.ctx;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kBwdEpiRows + warp * (kBwdEpiRows / 8);
+  const A* num = static_cast<const A*>(a.num);
+  const A* den = static_cast<const A*>(a.den);
+  const T* bias = static_cast<const T*>(a.bias);
+  const T* zl = static_cast<const T*>(a.z_tl);
+  const T* go = static_cast<const T*>(a.gout);
+  G* dnum = static_cast<G*>(a.dnum);
+  T* gzl = static_cast<T*>(a.gz_tl);
+  A dd[kBwdEpiRows / 8];
+#pragma unroll
+  for (int k = 0; k < kBwdEpiRows / 8; ++k) dd[k] = 0;
+  for (int f0 = 0; f0 < d; f0 += kBwdEpiChunk) {
+    A db[kBwdEpiChunk / 32];
+#pragma unroll
+    for (int q = 0; q < kBwdEpiChunk / 32; ++q) db[q] = 0;
+#pragma unroll
+    for (int k = 0; k < kBwdEpiRows / 8; ++k) {
+      const int64_t r = r0 + k;
+      if (r >= rows) break;
+      const int b = static_cast<int>(r / C), n = static_cast<int>(r % C);
+      const bool ok = row_valid(a, b, n);
+      const A dn = a.normalize ? den[r] : A(1);
+      const T* gor = go + static_cast<int64_t>(b) * a.go_bs + static_cast<int64_t>(n) * a.go_rs;
+      const T* zlr = zl ? zl + static_cast<int64_t>(b) * a.zl_bs + static_cast<int64_t>(n) * a.zl_rs
+                        : nullptr;
+#pragma unroll
+      for (int q = 0; q < kBwdEpiChunk / 32; ++q) {
+        const int f = f0 + 32 * q + lane;
+        if (f >= d) break;
+        const A y0 = num[r * d + f] / dn;
+        const A ypre = y0 + (bias ? ld_as<A>(bias + f) : A(0));
+        const A g = ok ? ld_as<A>(gor + f) : A(0);
+        A da = g;
+        if (zlr) {
+          const A gate = ok ? ld_as<A>(zlr + f) : A(0);
+          if (gzl) st_as<T>(gzl + r * d + f, ok ? g * activate(ypre, a.act) : A(0));
+          da = g * gate;
+        }
+        const A dy = ok ? da * activate_grad(ypre, a.act) : A(0);
+        st_as<G>(dnum + r * d + f, dy / dn);
+        dd[k] += dy * y0;
+        db[q] += dy;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kBwdEpiChunk / 32; ++q) red[warp][32 * q + lane] = db[q];
+    __syncthreads();
+    {
+      const int f = f0 + threadIdx.x;
+      if (threadIdx.x < kBwdEpiChunk && f < d) {
+        A t = 0;
+#pragma unroll
+        for (int w = 0; w < kBwdThreads / 32; ++w) t += red[w][threadIdx.x];
+        static_cast<A*>(a.part)[static_cast<int64_t>(blockIdx.x) * d + f] = t;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int k = 0; k < kBwdEpiRows / 8; ++k) {
+    const int64_t r = r0 + k;
+    const A t = warp_sum(dd[k]);
+    if (lane == 0 && r < rows)
+      static_cast<A*>(a.dden)[r] = a.normalize ? -t / static_cast<const A*>(a.den)[r] : A(0);
+  }
+}
+
+// Step 4: dS = (dnum Z^T + dden) (.) M, dGsym = (dG + dG^T) diag(r) with
+// dG = dS (.) V, and the partial dV = sum over a group of batch rows of
+// dS (.) G (G = r_i r_j Gr). A block
+// owns a pair of 32 x 32 tiles (I, J), (J, I) with I <= J, so both halves of
+// the symmetrised sum are formed in one place (through shared memory), and
+// loops over its group of batch rows; blockIdx.y picks the group.
+template <typename T, typename G, typename A>
+__global__ void __launch_bounds__(kBwdThreads) bwd_dscores(const BwdArgs a, int bpg) {
+  __shared__ A tr[kBwdTile][kBwdTile + 1];
+  __shared__ A ts[kBwdTile][kBwdTile + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int C = a.ctx;
+  // Pair index -> (I, J), I <= J: row I holds pairs J = I .. nt-1.
+  const int nt = (C + kBwdTile - 1) / kBwdTile;
+  int p = blockIdx.x, I = 0;
+  while (p >= nt - I) {
+    p -= nt - I;
+    ++I;
+  }
+  const int J = I + p;
+  const bool diag = I == J;
+  const int b0 = blockIdx.y * bpg, b1 = min(a.batch, b0 + bpg);
+  const A* ds0 = static_cast<const A*>(a.ds0);
+  const A* gr = static_cast<const A*>(a.g);
+  const A* dden = static_cast<const A*>(a.dden);
+  const T* v = static_cast<const T*>(a.v);
+  G* dgs = static_cast<G*>(a.dgsym);
+  constexpr int kR = kBwdTile / 8;
+  // (i, j) of tile (I, J) and (i2, j2) of tile (J, I) for this thread.
+  A vij[kR], vji[kR], acc1[kR], acc2[kR];
+#pragma unroll
+  for (int k = 0; k < kR; ++k) {
+    const int i = I * kBwdTile + ty + 8 * k, j = J * kBwdTile + tx;
+    const int i2 = J * kBwdTile + ty + 8 * k, j2 = I * kBwdTile + tx;
+    vij[k] = (v && i < C && j < C) ? ld_as<A>(v + static_cast<int64_t>(i) * a.v_rs + j) : A(1);
+    vji[k] = (v && i2 < C && j2 < C) ? ld_as<A>(v + static_cast<int64_t>(i2) * a.v_rs + j2) : A(1);
+    acc1[k] = acc2[k] = 0;
+  }
+  for (int b = b0; b < b1; ++b) {
+    const int64_t base = static_cast<int64_t>(b) * C * C;
+    const int64_t rb = static_cast<int64_t>(b) * C;  // first row of batch b
+    // r of the key columns of both tiles: J0 + tx and I0 + tx.
+    const A rj1 = J * kBwdTile + tx < C ? inv_norm<A>(a, rb + J * kBwdTile + tx) : A(0);
+    const A rj2 = I * kBwdTile + tx < C ? inv_norm<A>(a, rb + I * kBwdTile + tx) : A(0);
+    A dg1[kR];
+#pragma unroll
+    for (int k = 0; k < kR; ++k) {
+      const int i = I * kBwdTile + ty + 8 * k, j = J * kBwdTile + tx;
+      A x = 0;
+      if (i < C && j < C && (!a.causal || j <= i) && row_valid(a, b, j)) {
+        x = ds0[base + static_cast<int64_t>(i) * C + j];
+        if (a.normalize) x += dden[rb + i];
+        if (a.gv) acc1[k] += x * gr[base + static_cast<int64_t>(i) * C + j] * inv_norm<A>(a, rb + i) * rj1;
+      }
+      dg1[k] = x * vij[k];
+      if (!diag) {
+        const int i2 = J * kBwdTile + ty + 8 * k, j2 = I * kBwdTile + tx;
+        A y = 0;
+        if (i2 < C && j2 < C && (!a.causal || j2 <= i2) && row_valid(a, b, j2)) {
+          y = ds0[base + static_cast<int64_t>(i2) * C + j2];
+          if (a.normalize) y += dden[rb + i2];
+          if (a.gv) acc2[k] += y * gr[base + static_cast<int64_t>(i2) * C + j2] * inv_norm<A>(a, rb + i2) * rj2;
+        }
+        tr[ty + 8 * k][tx] = y * vji[k];  // dG of tile (J, I) at (i2 - J0, j2 - I0)
+      } else {
+        tr[ty + 8 * k][tx] = dg1[k];
+      }
+    }
+    __syncthreads();
+    // dGsym (I, J)[r][c] = dG(I, J)[r][c] + dG(J, I)[c][r], stored with its
+    // column scaled by r of that key.
+#pragma unroll
+    for (int k = 0; k < kR; ++k) {
+      const int rr = ty + 8 * k;
+      const int i = I * kBwdTile + rr, j = J * kBwdTile + tx;
+      const A sym = dg1[k] + tr[tx][rr];
+      ts[rr][tx] = sym;
+      if (i < C && j < C) st_as<G>(dgs + base + static_cast<int64_t>(i) * C + j, sym * rj1);
+    }
+    __syncthreads();
+    if (!diag) {
+      // Tile (J, I) is the transpose of tile (I, J).
+#pragma unroll
+      for (int k = 0; k < kR; ++k) {
+        const int rr = ty + 8 * k;
+        const int i2 = J * kBwdTile + rr, j2 = I * kBwdTile + tx;
+        if (i2 < C && j2 < C)
+          st_as<G>(dgs + base + static_cast<int64_t>(i2) * C + j2, ts[tx][rr] * rj2);
+      }
+    }
+    __syncthreads();
+  }
+  if (a.gv) {
+    A* part = static_cast<A*>(a.part) + static_cast<int64_t>(blockIdx.y) * C * C;
+#pragma unroll
+    for (int k = 0; k < kR; ++k) {
+      const int i = I * kBwdTile + ty + 8 * k, j = J * kBwdTile + tx;
+      if (i < C && j < C) part[static_cast<int64_t>(i) * C + j] = acc1[k];
+      if (!diag) {
+        const int i2 = J * kBwdTile + ty + 8 * k, j2 = I * kBwdTile + tx;
+        if (i2 < C && j2 < C) part[static_cast<int64_t>(i2) * C + j2] = acc2[k];
+      }
+    }
+  }
+}
+
+// Step 5: dZ = S^T dnum + the normalisation backward of dz^, zero on padded
+// rows, in the input type. One warp per row.
+template <typename T, typename G, typename A>
+__global__ void __launch_bounds__(kBwdThreads) bwd_final(const BwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
+  const int d = a.feat;
+  const G* zm = static_cast<const G*>(a.zm);
+  const A* dzh = static_cast<const A*>(a.dzh);
+  const A* dzd = static_cast<const A*>(a.dzd);
+  T* gz = static_cast<T*>(a.gz_tr);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
+       r += nwarps) {
+    const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
+    const bool ok = row_valid(a, b, n);
+    const A norm = static_cast<const A*>(a.norms)[r];
+    const A ne = static_cast<A>(a.norm_eps);
+    const bool scaled = norm >= ne;  // F.normalize divides by the norm itself
+    const A rinv = A(1) / (scaled ? norm : ne);
+    A dot = 0;
+    if (ok && scaled)
+      for (int f = lane; f < d; f += 32) dot += ld_as<A>(zm + r * d + f) * rinv * dzh[r * d + f];
+    dot = warp_sum(dot);
+    for (int f = lane; f < d; f += 32) {
+      A g = 0;
+      if (ok) {
+        const A zhat = ld_as<A>(zm + r * d + f) * rinv;
+        g = (dzh[r * d + f] - (scaled ? zhat * dot : A(0))) * rinv + dzd[r * d + f];
+      }
+      st_as<T>(gz + r * d + f, g);
+    }
+  }
+}
+
+// out[k] = sum over p of part[p][k], p in order (8 warps take interleaved p,
+// then combine in warp order): deterministic.
+template <typename T, typename A>
+__global__ void __launch_bounds__(kBwdThreads) bwd_reduce(const A* part, int nparts, int64_t n,
+                                                          T* out) {
+  __shared__ A red[kBwdThreads / 32][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t k = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  A t = 0;
+  if (k < n)
+    for (int p = warp; p < nparts; p += kBwdThreads / 32) t += part[static_cast<int64_t>(p) * n + k];
+  red[warp][lane] = t;
+  __syncthreads();
+  if (warp == 0 && k < n) {
+    A s = 0;
+#pragma unroll
+    for (int w = 0; w < kBwdThreads / 32; ++w) s += red[w][lane];
+    st_as<T>(out + k, s);
+  }
+}
+
+}  // namespace avey

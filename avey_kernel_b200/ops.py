@@ -3,13 +3,15 @@
 Same signatures, tensor conventions and errors as the reference
 (avey_kernels/ops.py:28-152). Backends:
 
-* ``'cuda'``  the native sm_100a kernels through the C ABI (``libavey_b200.so``);
-  CUDA inference inputs only, otherwise ``ValueError``.
+* ``'cuda'``  the native sm_100a kernels through the C ABI (``libavey_b200.so``)
+  for CUDA tensors, otherwise ``ValueError``. Inputs that require grad get the
+  native backward (``backward.py``); the reference has none and sends them to
+  its PyTorch path (ops.py:99-111).
 * ``'triton'`` accepted for source compatibility: it names the fused GPU
   kernel, which here is the native CUDA one (same rules as ``'cuda'``).
 * ``'torch'`` the differentiable PyTorch path (``eager.py``).
-* ``'auto'``  ``'cuda'`` for CUDA inference inputs; the PyTorch path for CPU
-  tensors and autograd, as in the reference (ops.py:99-111).
+* ``'auto'``  ``'cuda'`` for CUDA tensors, with or without autograd; the
+  PyTorch path for CPU tensors.
 
 The native path never falls back silently: when the library is missing or the
 device is not sm_100, the call raises.
@@ -26,7 +28,7 @@ from typing import Optional
 
 import torch
 
-from . import _native, eager
+from . import _native, backward, eager
 
 _BACKENDS = ('auto', 'torch', 'cuda', 'triton')
 _ACTIVATIONS = tuple(_native.ACTIVATION_IDS)
@@ -174,6 +176,9 @@ def _contextualize_fake(z_tr, v, z_tl, bias, valid, eps, norm_eps, causal, norma
     return torch.empty(z_tr.shape, dtype=z_tr.dtype, device=z_tr.device)
 
 
+backward.register()
+
+
 def plan(z_tr, v=None, z_tl=None, bias=None, valid=None, *, causal=True, normalize=False,
          eps=1e-6, norm_eps=1e-12, activation='identity', kernel=_native.KERNEL_AUTO):
     """The launch the native op would make for these tensors (no launch)."""
@@ -189,12 +194,9 @@ def _dispatch(z_tr, v, z_tl, bias, valid, eps, norm_eps, causal, normalize, acti
               output_tile, autotune):
     _validate(z_tr, v, z_tl, bias, valid, eps, norm_eps, activation, backend, output_tile,
               autotune)
-    needs_grad = torch.is_grad_enabled() and any(
-        t is not None and t.requires_grad for t in (z_tr, v, z_tl, bias))
-    native_ok = z_tr.is_cuda and torch.version.hip is None and not needs_grad
+    native_ok = z_tr.is_cuda and torch.version.hip is None
     if backend in ('cuda', 'triton') and not native_ok:
-        raise ValueError('the CUDA backend needs CUDA inference inputs (no autograd); '
-                         'use backend="torch" for autograd or CPU tensors')
+        raise ValueError('the CUDA backend needs CUDA tensors; use backend="torch" for CPU tensors')
     if backend == 'torch' or not native_ok:
         return eager.contextualize(z_tr, v, z_tl, bias, valid, eps=eps, norm_eps=norm_eps,
                                    causal=causal, normalize=normalize, activation=activation)

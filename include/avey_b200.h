@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define AVEY_ABI_VERSION 2
+#define AVEY_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define AVEY_API __attribute__((visibility("default")))
@@ -167,6 +167,91 @@ AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* byte
  */
 #define AVEY_NOALLOC_MAX_ROWS (1u << 20)
 AVEY_API int avey_fwd_noalloc_v1(const AveyFwdParams* params, void* stream);
+
+/*
+ * Backward pass. The reference has no fused backward: autograd runs through
+ * its PyTorch path (avey_kernels/ops.py:99-111 send any input that requires
+ * grad to _reference, ops.py:66-96). This library splits the gradient into
+ * five batched GEMMs, which the caller runs with a library GEMM, and five
+ * fused steps that run here between them:
+ *
+ *   AVEY_BWD_PREP      zm = z_tr (padded rows 0), norms = ||zm||
+ *                                                          then  g = zm zm^T
+ *   AVEY_BWD_SCORES    s = g r_i r_j (.) v (.) mask, den = rowsum(s) + eps,
+ *                      r = 1 / max(norms, norm_eps)        then  num = s zm
+ *   AVEY_BWD_EPILOGUE  grad_z_tl, grad_bias, dnum, dden from grad_out
+ *                                        then  ds0 = dnum zm^T, dzd = s^T dnum
+ *   AVEY_BWD_DSCORES   dgsym = (dG + dG^T) diag(r), dG = (ds0 + dden) (.)
+ *                      mask (.) v; grad_v                  then  dzh = dgsym zm
+ *   AVEY_BWD_FINAL     grad_z_tr = dzd + normalisation backward of dzh
+ *
+ * GEMM operands (zm, s, dnum, dgsym) are of gemm_dtype: AVEY_BF16 for
+ * bf16 inputs, AVEY_F32 for f16 and f32 inputs, AVEY_F64 for f64 inputs.
+ * Accumulator arrays (norms, g, den, num, dden, ds0, dzd, dzh, workspace) are
+ * float, or double for f64 inputs; GEMM outputs are written in that type. All
+ * scratch arrays are contiguous ([B, C, d'], [B, C, C] or [B, C]); the
+ * gradients are contiguous and of the input dtype, and an output pointer left
+ * NULL is not computed (grad_v needs v, grad_z_tl needs z_tl). Reductions use
+ * fixed orders: results are bitwise reproducible.
+ */
+typedef enum AveyBwdStep {
+  AVEY_BWD_PREP = 0,
+  AVEY_BWD_SCORES = 1,
+  AVEY_BWD_EPILOGUE = 2,
+  AVEY_BWD_DSCORES = 3,
+  AVEY_BWD_FINAL = 4,
+} AveyBwdStep;
+
+typedef struct AveyBwdParams {
+  uint32_t struct_size; /* sizeof(AveyBwdParams) */
+  int32_t dtype;        /* AveyDtype of the inputs and gradients */
+  int32_t gemm_dtype;   /* AveyDtype of the GEMM operand arrays (see above) */
+  int32_t causal, normalize, activation;
+  int64_t batch, context, features;
+  double eps, norm_eps;
+
+  /* Forward inputs, strided as in AveyFwdParams. */
+  const void* z_tr;
+  int64_t z_tr_batch_stride, z_tr_row_stride;
+  const void* v;
+  int64_t v_row_stride;
+  const void* z_tl;
+  int64_t z_tl_batch_stride, z_tl_row_stride;
+  const void* bias;
+  const uint8_t* valid;
+  int64_t valid_batch_stride, valid_row_stride;
+  const void* grad_out; /* [B, C, d'] gradient of the forward output */
+  int64_t grad_out_batch_stride, grad_out_row_stride;
+
+  /* Scratch written by one step and read by later ones or by the GEMMs. */
+  void* zm;        /* [B, C, d'] gemm_dtype */
+  void* norms;     /* [B, C]     acc */
+  void* g;         /* [B, C, C]  acc (GEMM output) */
+  void* s;         /* [B, C, C]  gemm_dtype */
+  void* den;       /* [B, C]     acc */
+  void* num;       /* [B, C, d'] acc (GEMM output) */
+  void* dnum;      /* [B, C, d'] gemm_dtype */
+  void* dden;      /* [B, C]     acc */
+  void* ds0;       /* [B, C, C]  acc (GEMM output) */
+  void* dgsym;     /* [B, C, C]  gemm_dtype */
+  void* dzd;       /* [B, C, d'] acc (GEMM output) */
+  void* dzh;       /* [B, C, d'] acc (GEMM output) */
+  void* workspace; /* partial sums, >= avey_bwd_workspace_size() bytes */
+  uint64_t workspace_bytes;
+
+  /* Gradients (contiguous, input dtype); NULL = not wanted. */
+  void* grad_z_tr;
+  void* grad_v;
+  void* grad_z_tl;
+  void* grad_bias;
+} AveyBwdParams;
+
+/* Enqueue one backward step on `stream`. Returns AVEY_OK or a negative
+ * AveyStatus; the pointers a step reads or writes must be set. */
+AVEY_API int avey_bwd_step_v1(const AveyBwdParams* params, int step, void* stream);
+
+/* Bytes of `workspace` the backward steps need for these parameters. */
+AVEY_API int avey_bwd_workspace_size(const AveyBwdParams* params, uint64_t* bytes);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */
 AVEY_API const char* avey_last_error(void);

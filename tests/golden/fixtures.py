@@ -70,3 +70,31 @@ def oracle_kwargs(case: dict) -> dict:
                 norm_eps=case['norm_eps'],
                 causal=case['causal'] if case['op'] == 'avey' else False,
                 normalize=case['op'] == 'avey_b', activation=case['activation'])
+
+
+GRAD_FIELDS = ('z_tr', 'v', 'z_tl', 'bias')
+
+
+@lru_cache(maxsize=1)
+def load_grad_cases():
+    """Gradient cases of ``make_grad_golden.py``: inputs, ``grad_out`` and the
+    reference's gradients ``d_<input>`` (None where the input is absent)."""
+    manifest = json.loads((HERE / 'grad_cases.json').read_text())
+    data = np.load(HERE / 'grad_golden.npz')
+    cases = []
+    for meta in manifest:
+        case = dict(meta)
+        for field in FIELDS + ('grad_out',) + tuple('d_' + f for f in GRAD_FIELDS):
+            key = meta[field]
+            case[field] = None if key is None else _decode(data[key])
+        cases.append(case)
+    return tuple(cases)
+
+
+def grad_to_torch(case: dict, device='cpu'):
+    """Inputs and grad_out as tensors of the case dtype on ``device``."""
+    out = to_torch(case, device)
+    import torch
+    out['grad_out'] = torch.from_numpy(case['grad_out'].copy()).to(
+        device=device, dtype=getattr(torch, case['dtype']))
+    return out

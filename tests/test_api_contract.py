@@ -111,9 +111,11 @@ def test_auto_backend_preserves_autograd_on_cpu():
 
 
 @pytest.mark.parametrize('backend', ['cuda', 'triton'])
-def test_native_backend_rejects_cpu_and_autograd_inputs(backend):
-    with pytest.raises(ValueError, match='CUDA inference inputs'):
+def test_native_backend_rejects_cpu_inputs(backend):
+    with pytest.raises(ValueError, match='CUDA tensors'):
         avey_b(torch.rand(1, 5, 8), backend=backend)
+    with pytest.raises(ValueError, match='CUDA tensors'):
+        avey_b(torch.rand(1, 5, 8, requires_grad=True), backend=backend)
 
 
 @pytest.mark.parametrize('case', CASES, ids=[c['name'] for c in CASES])

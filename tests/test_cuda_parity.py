@@ -346,9 +346,14 @@ def test_fp64_inputs_run_natively():
                                atol=1e-12)
 
 
-def test_autograd_inputs_keep_the_torch_path():
+def test_autograd_inputs_run_the_native_backward():
     z = torch.rand(2, 35, 40, device=DEV, requires_grad=True)
+    before = _native.launch_count()
     avey_b(z).sum().backward()
+    torch.cuda.synchronize()
+    # forward (1) + prep, scores, epilogue, dscores, final (5)
+    assert _native.launch_count() == before + 6
     assert z.grad is not None and torch.isfinite(z.grad).all()
-    with pytest.raises(ValueError):
-        avey_b(z, backend='cuda')
+    z.grad = None
+    avey_b(z, backend='cuda').sum().backward()
+    assert z.grad is not None
