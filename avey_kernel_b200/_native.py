@@ -109,6 +109,8 @@ class AveyBwdParams(ctypes.Structure):
         ('grad_v', ctypes.c_void_p),
         ('grad_z_tl', ctypes.c_void_p),
         ('grad_bias', ctypes.c_void_p),
+        ('grad_batch_stride', ctypes.c_int64),
+        ('grad_row_stride', ctypes.c_int64),
     ]
 
 

@@ -52,9 +52,11 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 
 def contextualize_backward_impl(z_tr, v, z_tl, bias, valid, grad_out, eps, norm_eps, causal,
-                                normalize, activation, needs):
+                                normalize, activation, needs, packed_out=None):
     """Gradients (z_tr, v, z_tl, bias) of the contextualizer; entries not in
-    ``needs`` (or whose input is absent) come back as None."""
+    ``needs`` (or whose input is absent) come back as None. With
+    ``packed_out`` (a [B, C, 2d'] tensor), the z_tl and z_tr gradients are
+    written into its halves [..., :d'] and [..., d':] instead."""
     if not z_tr.is_cuda:
         raise ValueError('the native backward needs CUDA tensors')
     z_tr, z_tl, grad_out = _unit_last(z_tr), _unit_last(z_tl), _unit_last(grad_out)
@@ -108,7 +110,11 @@ def contextualize_backward_impl(z_tr, v, z_tl, bias, valid, grad_out, eps, norm_
         num = _bmm(s, zm, acc)
         dnum, dden = empty(B, C, d, dtype=gdt), empty(B, C, dtype=acc)
         workspace = empty(_native.bwd_workspace_size(p), dtype=torch.uint8)
-        gz_tl = empty(B, C, d, dtype=dt) if need_zl else None
+        if packed_out is not None:
+            gz_tl = packed_out[..., :d]
+            p.grad_batch_stride, p.grad_row_stride = packed_out.stride(0), packed_out.stride(1)
+        else:
+            gz_tl = empty(B, C, d, dtype=dt) if need_zl else None
         gbias = empty(d, dtype=dt) if need_b else None
         p.num, p.dnum, p.dden = num.data_ptr(), dnum.data_ptr(), dden.data_ptr()
         p.workspace, p.workspace_bytes = workspace.data_ptr(), workspace.numel()
@@ -126,7 +132,7 @@ def contextualize_backward_impl(z_tr, v, z_tl, bias, valid, grad_out, eps, norm_
             if need_z:
                 dzd = _bmm(s.transpose(1, 2), dnum, acc)
                 dzh = _bmm(dgsym, zm, acc)
-                gz = empty(B, C, d, dtype=dt)
+                gz = packed_out[..., d:] if packed_out is not None else empty(B, C, d, dtype=dt)
                 p.dzd, p.dzh, p.grad_z_tr = dzd.data_ptr(), dzh.data_ptr(), gz.data_ptr()
                 _native.bwd_step(p, _native.BWD_FINAL, stream)
     return gz, gv, gz_tl, gbias
@@ -172,3 +178,53 @@ def register() -> None:
     """Attach the native backward to ``avey_b200::contextualize`` (once)."""
     torch.library.register_autograd('avey_b200::contextualize', _backward,
                                     setup_context=_setup_context)
+
+
+# ---------------------------------------------------------------------------
+# Packed form: z_tl and z_tr are the halves [..., :d'] and [..., d':] of one
+# [B, C, 2d'] tensor x (the enricher output split into head and tail). Taking
+# x as the op's input gives autograd one gradient for x, written in place by
+# the backward steps, instead of two half-size gradients that autograd would
+# scatter into zero-filled copies of x and add.
+
+@torch.library.custom_op('avey_b200::contextualize_packed_backward', mutates_args=())
+def contextualize_packed_backward(x: torch.Tensor, v: Optional[torch.Tensor],
+                                  bias: Optional[torch.Tensor], valid: Optional[torch.Tensor],
+                                  grad_out: torch.Tensor, eps: float, norm_eps: float,
+                                  causal: bool, normalize: bool, activation: int,
+                                  needs: List[bool]) -> List[torch.Tensor]:
+    """[grad_x, grad_v, grad_bias] of ``avey_b200::contextualize_packed``."""
+    d = x.shape[-1] // 2
+    gx = torch.empty_like(x, memory_format=torch.contiguous_format) if needs[0] else None
+    _, gv, _, gb = contextualize_backward_impl(
+        x[..., d:], v, x[..., :d], bias, valid, grad_out, eps, norm_eps, causal, normalize,
+        activation, [needs[0], needs[1], needs[0], needs[2]], packed_out=gx)
+    return [t if t is not None else x.new_empty(0) for t in (gx, gv, gb)]
+
+
+@contextualize_packed_backward.register_fake
+def _contextualize_packed_backward_fake(x, v, bias, valid, grad_out, eps, norm_eps, causal,
+                                        normalize, activation, needs):
+    shapes = (x.shape, None if v is None else v.shape, None if bias is None else bias.shape)
+    return [x.new_empty(s) if (s is not None and n) else x.new_empty(0)
+            for s, n in zip(shapes, needs)]
+
+
+def _setup_context_packed(ctx, inputs, output):
+    x, v, bias, valid, eps, norm_eps, causal, normalize, activation = inputs
+    ctx.save_for_backward(x, v, bias, valid)
+    ctx.cfg = (eps, norm_eps, causal, normalize, activation)
+
+
+def _backward_packed(ctx, grad):
+    x, v, bias, valid = ctx.saved_tensors
+    needs = [bool(n) for n in ctx.needs_input_grad[:3]]
+    grads = contextualize_packed_backward(x, v, bias, valid, grad, *ctx.cfg, needs)
+    out = [t if (n and t.numel()) else None for t, n in zip(grads, needs)]
+    return (*out, None, None, None, None, None, None, None)
+
+
+def register_packed() -> None:
+    """Attach the native backward to ``avey_b200::contextualize_packed``."""
+    torch.library.register_autograd('avey_b200::contextualize_packed', _backward_packed,
+                                    setup_context=_setup_context_packed)

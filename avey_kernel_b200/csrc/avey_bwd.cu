@@ -4,7 +4,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
+#include <type_traits>
 
 #include "avey_b200.h"
 #include "bwd_kernels.cuh"
@@ -31,8 +33,12 @@ int expected_gemm_dtype(int dtype) {
 
 int acc_size(const AveyBwdParams* p) { return p->dtype == AVEY_F64 ? 8 : 4; }
 
+bool vec_ok(const AveyBwdParams* p);
+
+// Epilogue blocks: 64 rows each in the scalar form, 32 in the vector form.
 int64_t epi_blocks(const AveyBwdParams* p) {
-  return (p->batch * p->context + avey::kBwdEpiRows - 1) / avey::kBwdEpiRows;
+  const int rows = vec_ok(p) ? avey::kBwdEpiRowsV8 : avey::kBwdEpiRows;
+  return (p->batch * p->context + rows - 1) / rows;
 }
 
 // dscores grid: tile pairs x batch groups, enough CTAs to fill the GPU.
@@ -69,7 +75,8 @@ int validate(const AveyBwdParams* p) {
   if (!p->z_tr || p->z_tr_row_stride < p->features || p->z_tr_batch_stride < 0 ||
       (p->z_tl && (p->z_tl_row_stride < p->features || p->z_tl_batch_stride < 0)) ||
       (p->v && p->v_row_stride < p->context) || p->valid_batch_stride < 0 ||
-      p->valid_row_stride < 0)
+      p->valid_row_stride < 0 || p->grad_batch_stride < 0 ||
+      (p->grad_row_stride && p->grad_row_stride < p->features))
     return fail(AVEY_ERR_ARGUMENT, "z_tr is required and strides must cover the rows");
   return AVEY_OK;
 }
@@ -91,6 +98,9 @@ avey::BwdArgs make_args(const AveyBwdParams* p) {
   a.va_rs = p->valid_row_stride;
   a.go_bs = p->grad_out_batch_stride;
   a.go_rs = p->grad_out_row_stride;
+  // grad_z_tr / grad_z_tl: contiguous unless strides are given.
+  a.gr_rs = p->grad_row_stride ? p->grad_row_stride : p->features;
+  a.gr_bs = p->grad_batch_stride ? p->grad_batch_stride : p->context * a.gr_rs;
   a.batch = static_cast<int>(p->batch);
   a.ctx = static_cast<int>(p->context);
   a.feat = static_cast<int>(p->features);
@@ -130,6 +140,23 @@ int launched(int n) {
   return avey_host::clear_error();
 }
 
+bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
+
+// The vector forms need 8-element rows everywhere and 16-byte aligned rows
+// in every strided input (fp64 keeps the scalar forms).
+bool vec_ok(const AveyBwdParams* p) {
+  if (p->dtype == AVEY_F64 || p->context % 8 || p->features % 8) return false;
+  auto rows_ok = [](const void* q, int64_t bs, int64_t rs) {
+    return !q || (al16(q) && bs % 8 == 0 && rs % 8 == 0);
+  };
+  return rows_ok(p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride) &&
+         rows_ok(p->z_tl, p->z_tl_batch_stride, p->z_tl_row_stride) &&
+         rows_ok(p->grad_out, p->grad_out_batch_stride, p->grad_out_row_stride) &&
+         rows_ok(p->v, 0, p->v_row_stride) && (!p->bias || al16(p->bias)) &&
+         rows_ok(p->grad_z_tr, p->grad_batch_stride, p->grad_row_stride) &&
+         rows_ok(p->grad_z_tl, p->grad_batch_stride, p->grad_row_stride);
+}
+
 int row_grid(const AveyBwdParams* p) {
   const int64_t warps = p->batch * p->context;
   return static_cast<int>(std::min<int64_t>((warps + 7) / 8, 148 * 16));
@@ -139,14 +166,28 @@ template <typename T, typename G, typename A>
 int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
   const avey::BwdArgs a = make_args(p);
   constexpr int kT = avey::kBwdThreads;
+  constexpr bool kHasVec = !std::is_same<A, double>::value;
+  const bool vec = kHasVec && vec_ok(p);
   switch (step) {
     case AVEY_BWD_PREP:
       if (!p->zm || !p->norms) return fail(AVEY_ERR_ARGUMENT, "prep needs zm, norms");
+      if constexpr (kHasVec) {
+        if (vec) {
+          avey::bwd_prep_v8<T, G><<<row_grid(p), kT, 0, st>>>(a);
+          return launched(1);
+        }
+      }
       avey::bwd_prep<T, G, A><<<row_grid(p), kT, 0, st>>>(a);
       return launched(1);
     case AVEY_BWD_SCORES:
       if (!p->g || !p->s || !p->den || !p->norms)
         return fail(AVEY_ERR_ARGUMENT, "scores needs g, s, den, norms");
+      if constexpr (kHasVec) {
+        if (vec) {
+          avey::bwd_scores_v8<T, G><<<row_grid(p), kT, 0, st>>>(a);
+          return launched(1);
+        }
+      }
       avey::bwd_scores<T, G, A><<<row_grid(p), kT, 0, st>>>(a);
       return launched(1);
     case AVEY_BWD_EPILOGUE: {
@@ -154,10 +195,24 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
           p->workspace_bytes < workspace_bytes(p))
         return fail(AVEY_ERR_ARGUMENT, "epilogue needs num, den, dnum, dden, grad_out, workspace");
       const int64_t nb = epi_blocks(p);
-      avey::bwd_epilogue<T, G, A><<<static_cast<unsigned>(nb), kT, 0, st>>>(a);
+      bool done = false;
+      if constexpr (kHasVec) {
+        if (vec) {
+          const unsigned grid = static_cast<unsigned>(nb);
+          switch (p->activation) {
+            case 1: avey::bwd_epilogue_v8<T, G, 1><<<grid, kT, 0, st>>>(a); break;
+            case 2: avey::bwd_epilogue_v8<T, G, 2><<<grid, kT, 0, st>>>(a); break;
+            case 3: avey::bwd_epilogue_v8<T, G, 3><<<grid, kT, 0, st>>>(a); break;
+            case 4: avey::bwd_epilogue_v8<T, G, 4><<<grid, kT, 0, st>>>(a); break;
+            default: avey::bwd_epilogue_v8<T, G, 0><<<grid, kT, 0, st>>>(a); break;
+          }
+          done = true;
+        }
+      }
+      if (!done) avey::bwd_epilogue<T, G, A><<<static_cast<unsigned>(nb), kT, 0, st>>>(a);
       int n = 1;
       if (a.gbias) {
-        avey::bwd_reduce<T, A><<<static_cast<unsigned>((p->features + 31) / 32), kT, 0, st>>>(
+        avey::bwd_reduce<T, A><<<static_cast<unsigned>((p->features + 31) / 32), avey::kBwdReduceThreads, 0, st>>>(
             static_cast<const A*>(p->workspace), static_cast<int>(nb), p->features,
             static_cast<T*>(p->grad_bias));
         ++n;
@@ -174,7 +229,7 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
       int n = 1;
       if (a.gv) {
         const int64_t cc = p->context * p->context;
-        avey::bwd_reduce<T, A><<<static_cast<unsigned>((cc + 31) / 32), kT, 0, st>>>(
+        avey::bwd_reduce<T, A><<<static_cast<unsigned>((cc + 31) / 32), avey::kBwdReduceThreads, 0, st>>>(
             static_cast<const A*>(p->workspace), groups, cc, static_cast<T*>(p->grad_v));
         ++n;
       }
@@ -183,6 +238,12 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
     case AVEY_BWD_FINAL:
       if (!p->zm || !p->norms || !p->dzh || !p->dzd || !p->grad_z_tr)
         return fail(AVEY_ERR_ARGUMENT, "final needs zm, norms, dzh, dzd, grad_z_tr");
+      if constexpr (kHasVec) {
+        if (vec) {
+          avey::bwd_final_v8<T, G><<<row_grid(p), kT, 0, st>>>(a);
+          return launched(1);
+        }
+      }
       avey::bwd_final<T, G, A><<<row_grid(p), kT, 0, st>>>(a);
       return launched(1);
     default:

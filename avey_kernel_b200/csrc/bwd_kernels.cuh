@@ -43,6 +43,7 @@ struct BwdArgs {
   const uint8_t* valid;
   const void* gout;
   int64_t zr_bs, zr_rs, v_rs, zl_bs, zl_rs, va_bs, va_rs, go_bs, go_rs;
+  int64_t gr_bs, gr_rs;  // strides of grad_z_tr and grad_z_tl (elements)
   int batch, ctx, feat;
   double eps, norm_eps;
   int causal, normalize, act;
@@ -59,7 +60,7 @@ struct BwdArgs {
   void* dzd;    // [B, C, d]  acc: S^T dnum
   void* dzh;    // [B, C, d]  acc: dz^ = dgsym Z
   void* part;   // acc partial sums (dbias, dV)
-  void* gz_tr;  // [B, C, d]  input type
+  void* gz_tr;  // [B, C, d]  input type, strides gr_bs / gr_rs
   void* gv;     // [C, C]
   void* gz_tl;  // [B, C, d]
   void* gbias;  // [d]
@@ -90,6 +91,11 @@ __device__ __forceinline__ A inv_norm(const BwdArgs& a, int64_t row) {
   const A n = static_cast<const A*>(a.norms)[row];
   const A ne = static_cast<A>(a.norm_eps);
   return A(1) / (n > ne ? n : ne);
+}
+
+// Element offset of row (b, n) in grad_z_tr / grad_z_tl.
+__device__ __forceinline__ int64_t grad_off(const BwdArgs& a, int b, int n) {
+  return static_cast<int64_t>(b) * a.gr_bs + static_cast<int64_t>(n) * a.gr_rs;
 }
 
 __device__ __forceinline__ bool row_valid(const BwdArgs& a, int b, int n) {
@@ -231,7 +237,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_epilogue(const BwdArgs a) {
         A da = g;
         if (zlr) {
           const A gate = ok ? ld_as<A>(zlr + f) : A(0);
-          if (gzl) st_as<T>(gzl + r * d + f, ok ? g * activate(ypre, a.act) : A(0));
+          if (gzl) st_as<T>(gzl + grad_off(a, b, n) + f, ok ? g * activate(ypre, a.act) : A(0));
           da = g * gate;
         }
         const A dy = ok ? da * activate_grad(ypre, a.act) : A(0);
@@ -273,6 +279,9 @@ template <typename T, typename G, typename A>
 __global__ void __launch_bounds__(kBwdThreads) bwd_dscores(const BwdArgs a, int bpg) {
   __shared__ A tr[kBwdTile][kBwdTile + 1];
   __shared__ A ts[kBwdTile][kBwdTile + 1];
+  // Per batch row: r and key validity of the positions I0 + t and J0 + t.
+  __shared__ A rs[2][kBwdTile];
+  __shared__ int vs[2][kBwdTile];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int C = a.ctx;
   // Pair index -> (I, J), I <= J: row I holds pairs J = I .. nt-1.
@@ -304,27 +313,34 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dscores(const BwdArgs a, int 
   for (int b = b0; b < b1; ++b) {
     const int64_t base = static_cast<int64_t>(b) * C * C;
     const int64_t rb = static_cast<int64_t>(b) * C;  // first row of batch b
+    if (threadIdx.x < 2 * kBwdTile) {
+      const int side = threadIdx.x / kBwdTile, t = threadIdx.x % kBwdTile;
+      const int pos = (side ? J : I) * kBwdTile + t;
+      rs[side][t] = pos < C ? inv_norm<A>(a, rb + pos) : A(0);
+      vs[side][t] = pos < C && row_valid(a, b, pos);
+    }
+    __syncthreads();
     // r of the key columns of both tiles: J0 + tx and I0 + tx.
-    const A rj1 = J * kBwdTile + tx < C ? inv_norm<A>(a, rb + J * kBwdTile + tx) : A(0);
-    const A rj2 = I * kBwdTile + tx < C ? inv_norm<A>(a, rb + I * kBwdTile + tx) : A(0);
+    const A rj1 = rs[1][tx], rj2 = rs[0][tx];
+    const bool vj1 = vs[1][tx] != 0, vj2 = vs[0][tx] != 0;
     A dg1[kR];
 #pragma unroll
     for (int k = 0; k < kR; ++k) {
       const int i = I * kBwdTile + ty + 8 * k, j = J * kBwdTile + tx;
       A x = 0;
-      if (i < C && j < C && (!a.causal || j <= i) && row_valid(a, b, j)) {
+      if (i < C && j < C && (!a.causal || j <= i) && vj1) {
         x = ds0[base + static_cast<int64_t>(i) * C + j];
         if (a.normalize) x += dden[rb + i];
-        if (a.gv) acc1[k] += x * gr[base + static_cast<int64_t>(i) * C + j] * inv_norm<A>(a, rb + i) * rj1;
+        if (a.gv) acc1[k] += x * gr[base + static_cast<int64_t>(i) * C + j] * rs[0][ty + 8 * k] * rj1;
       }
       dg1[k] = x * vij[k];
       if (!diag) {
         const int i2 = J * kBwdTile + ty + 8 * k, j2 = I * kBwdTile + tx;
         A y = 0;
-        if (i2 < C && j2 < C && (!a.causal || j2 <= i2) && row_valid(a, b, j2)) {
+        if (i2 < C && j2 < C && (!a.causal || j2 <= i2) && vj2) {
           y = ds0[base + static_cast<int64_t>(i2) * C + j2];
           if (a.normalize) y += dden[rb + i2];
-          if (a.gv) acc2[k] += y * gr[base + static_cast<int64_t>(i2) * C + j2] * inv_norm<A>(a, rb + i2) * rj2;
+          if (a.gv) acc2[k] += y * gr[base + static_cast<int64_t>(i2) * C + j2] * rs[1][ty + 8 * k] * rj2;
         }
         tr[ty + 8 * k][tx] = y * vji[k];  // dG of tile (J, I) at (i2 - J0, j2 - I0)
       } else {
@@ -399,16 +415,326 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final(const BwdArgs a) {
         const A zhat = ld_as<A>(zm + r * d + f) * rinv;
         g = (dzh[r * d + f] - (scaled ? zhat * dot : A(0))) * rinv + dzd[r * d + f];
       }
-      st_as<T>(gz + r * d + f, g);
+      st_as<T>(gz + grad_off(a, b, n) + f, g);
     }
   }
 }
 
-// out[k] = sum over p of part[p][k], p in order (8 warps take interleaved p,
+// ---------------------------------------------------------------------------
+// Vector forms of steps 1, 2, 3 and 5 (fp32 accumulation; bf16, fp16 and fp32
+// inputs): every lane moves 8 consecutive elements per access (16-byte loads
+// and stores of 16-bit data, two of fp32). The host picks them when the row
+// lengths are multiples of 8 and every strided row starts 16-byte aligned.
+
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void ld8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    v[2 * e] = __uint_as_float(w[e] << 16);
+    v[2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void ld8<__half>(const __half* p, float (&v)[8]) {
+  const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void ld8<float>(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void st8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ void st8<__half>(__half* p, const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __half2 h = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ void st8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Step 1, vector form.
+template <typename T, typename G>
+__global__ void __launch_bounds__(kBwdThreads) bwd_prep_v8(const BwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
+  const int nv = a.feat / 8;
+  const T* z = static_cast<const T*>(a.z_tr);
+  G* zm = static_cast<G*>(a.zm);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
+       r += nwarps) {
+    const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
+    const bool ok = row_valid(a, b, n);
+    const T* zr = z + static_cast<int64_t>(b) * a.zr_bs + static_cast<int64_t>(n) * a.zr_rs;
+    float ss = 0.f;
+    for (int v = lane; v < nv; v += 32) {
+      float x[8];
+      if (ok) {
+        ld8<T>(zr + 8 * v, x);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+      st8<G>(zm + r * a.feat + 8 * v, x);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) static_cast<float*>(a.norms)[r] = sqrtf(ss);
+  }
+}
+
+// Step 2, vector form: a lane takes 8 consecutive keys.
+template <typename T, typename G>
+__global__ void __launch_bounds__(kBwdThreads) bwd_scores_v8(const BwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
+  const int C = a.ctx;
+  const float* gr = static_cast<const float*>(a.g);
+  const float* norms = static_cast<const float*>(a.norms);
+  G* s = static_cast<G*>(a.s);
+  const T* v = static_cast<const T*>(a.v);
+  const float ne = static_cast<float>(a.norm_eps);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
+       r += nwarps) {
+    const int b = static_cast<int>(r / C), i = static_cast<int>(r % C);
+    const float ri = 1.f / fmaxf(norms[r], ne);
+    const float* nb = norms + static_cast<int64_t>(b) * C;
+    float sum = 0.f;
+    for (int j0 = 8 * lane; j0 < C; j0 += 256) {
+      float x[8], nk[8], vv[8];
+      ld8<float>(gr + r * C + j0, x);
+      ld8<float>(nb + j0, nk);
+      if (v) ld8<T>(v + static_cast<int64_t>(i) * a.v_rs + j0, vv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = j0 + e;
+        const bool allowed = (!a.causal || j <= i) && row_valid(a, b, j);
+        float y = x[e] * ri * (1.f / fmaxf(nk[e], ne));
+        if (v) y *= vv[e];
+        x[e] = allowed ? y : 0.f;
+        sum += x[e];
+      }
+      st8<G>(s + r * C + j0, x);
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) static_cast<float*>(a.den)[r] = sum + static_cast<float>(a.eps);
+  }
+}
+
+// Step 3, vector form: a warp takes kBwdEpiRowsV8 rows, a lane 8 consecutive
+// features of up to 2 slots (512 features) per pass, keeping its dbias
+// partial sums in registers across the rows; the block sums its 8 warps in
+// order. The activation is a template parameter. dden is accumulated in place
+// (one warp owns a row) and finished after the last pass.
+constexpr int kBwdEpiSlots = 2;
+constexpr int kBwdEpiRowsV8 = 32;  // rows per block (4 per warp)
+
+template <int ACT>
+__device__ __forceinline__ float act_grad_fn(float x) {
+  if constexpr (ACT == 1) {
+    return x > 0.f ? 1.f : 0.f;
+  } else if constexpr (ACT == 2) {
+    return x > 0.f ? 2.f * x : 0.f;
+  } else if constexpr (ACT == 3) {
+    const float sg = sigmoid_stable(x);
+    return sg * (1.f + x * (1.f - sg));
+  } else if constexpr (ACT == 4) {
+    const float k = 0.7978845608028654f, c = 0.044715f;
+    const float t = tanhf(k * (x + c * x * x * x));
+    return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k * (1.f + 3.f * c * x * x);
+  } else {
+    return 1.f;
+  }
+}
+
+template <typename T, typename G, int ACT>
+__global__ void __launch_bounds__(kBwdThreads) bwd_epilogue_v8(const BwdArgs a) {
+  __shared__ float red[kBwdThreads / 32][kBwdEpiSlots * 256];
+  constexpr int kRows = kBwdEpiRowsV8 / (kBwdThreads / 32);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int d = a.feat, C = a.ctx, nv = d / 8;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kBwdEpiRowsV8 + warp * kRows;
+  const float* num = static_cast<const float*>(a.num);
+  const float* den = static_cast<const float*>(a.den);
+  float* dden = static_cast<float*>(a.dden);
+  const T* bias = static_cast<const T*>(a.bias);
+  const T* zl = static_cast<const T*>(a.z_tl);
+  const T* go = static_cast<const T*>(a.gout);
+  G* dnum = static_cast<G*>(a.dnum);
+  T* gzl = static_cast<T*>(a.gz_tl);
+  for (int w0 = 0; w0 < nv; w0 += 32 * kBwdEpiSlots) {
+    float db[kBwdEpiSlots][8];
+#pragma unroll
+    for (int q = 0; q < kBwdEpiSlots; ++q)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) db[q][e] = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < kRows; ++k) {
+      const int64_t r = r0 + k;
+      if (r >= rows) break;
+      const int b = static_cast<int>(r / C), n = static_cast<int>(r % C);
+      const bool ok = row_valid(a, b, n);
+      const float dn = a.normalize ? den[r] : 1.f;
+      const float rdn = 1.f / dn;
+      const T* gor = go + static_cast<int64_t>(b) * a.go_bs + static_cast<int64_t>(n) * a.go_rs;
+      const T* zlr = zl ? zl + static_cast<int64_t>(b) * a.zl_bs + static_cast<int64_t>(n) * a.zl_rs
+                        : nullptr;
+      float dsum = 0.f;
+#pragma unroll
+      for (int q = 0; q < kBwdEpiSlots; ++q) {
+        const int v = w0 + 32 * q + lane;
+        if (v >= nv) break;
+        const int f0 = 8 * v;
+        float nm[8], g[8], bb[8], gt[8], dy[8], dz[8];
+        ld8<float>(num + r * d + f0, nm);
+        if (ok) {
+          ld8<T>(gor + f0, g);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] = 0.f;
+        }
+        if (bias) {
+          ld8<T>(bias + f0, bb);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) bb[e] = 0.f;
+        }
+        if (zlr && ok) {
+          ld8<T>(zlr + f0, gt);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) gt[e] = zlr ? 0.f : 1.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float y0 = nm[e] * rdn;
+          const float ypre = y0 + bb[e];
+          dz[e] = ok ? g[e] * act_fn<ACT>(ypre) : 0.f;
+          dy[e] = ok ? g[e] * gt[e] * act_grad_fn<ACT>(ypre) : 0.f;
+          dsum = fmaf(dy[e], y0, dsum);
+          db[q][e] += dy[e];
+          dy[e] *= rdn;
+        }
+        if (gzl) st8<T>(gzl + grad_off(a, b, n) + f0, dz);
+        st8<G>(dnum + r * d + f0, dy);
+      }
+      dsum = warp_sum(dsum);
+      if (lane == 0) dden[r] = (w0 == 0 ? 0.f : dden[r]) + dsum;
+    }
+#pragma unroll
+    for (int q = 0; q < kBwdEpiSlots; ++q)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) red[warp][(32 * q + lane) * 8 + e] = db[q][e];
+    __syncthreads();
+    for (int t = threadIdx.x; t < kBwdEpiSlots * 256; t += kBwdThreads) {
+      const int f = 8 * w0 + t;
+      if (f < d) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kBwdThreads / 32; ++w) acc += red[w][t];
+        static_cast<float*>(a.part)[static_cast<int64_t>(blockIdx.x) * d + f] = acc;
+      }
+    }
+    __syncthreads();
+  }
+  if (lane == 0)
+    for (int k = 0; k < kRows; ++k) {
+      const int64_t r = r0 + k;
+      if (r < rows) dden[r] = a.normalize ? -dden[r] / den[r] : 0.f;
+    }
+}
+
+// Step 5, vector form.
+template <typename T, typename G>
+__global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
+  const int d = a.feat, nv = d / 8;
+  const G* zm = static_cast<const G*>(a.zm);
+  const float* dzh = static_cast<const float*>(a.dzh);
+  const float* dzd = static_cast<const float*>(a.dzd);
+  T* gz = static_cast<T*>(a.gz_tr);
+  const float ne = static_cast<float>(a.norm_eps);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
+       r += nwarps) {
+    const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
+    const bool ok = row_valid(a, b, n);
+    const float norm = static_cast<const float*>(a.norms)[r];
+    const bool scaled = norm >= ne;
+    const float rinv = 1.f / (scaled ? norm : ne);
+    float dot = 0.f;
+    if (ok && scaled)
+      for (int v = lane; v < nv; v += 32) {
+        float z[8], h[8];
+        ld8<G>(zm + r * d + 8 * v, z);
+        ld8<float>(dzh + r * d + 8 * v, h);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot = fmaf(z[e] * rinv, h[e], dot);
+      }
+    dot = warp_sum(dot);
+    for (int v = lane; v < nv; v += 32) {
+      float o[8];
+      if (ok) {
+        float z[8], h[8], dd[8];
+        ld8<G>(zm + r * d + 8 * v, z);
+        ld8<float>(dzh + r * d + 8 * v, h);
+        ld8<float>(dzd + r * d + 8 * v, dd);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          o[e] = (h[e] - (scaled ? z[e] * rinv * dot : 0.f)) * rinv + dd[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = 0.f;
+      }
+      st8<T>(gz + grad_off(a, b, n) + 8 * v, o);
+    }
+  }
+}
+
+// out[k] = sum over p of part[p][k], p in order (32 warps take interleaved p,
 // then combine in warp order): deterministic.
+constexpr int kBwdReduceThreads = 1024;
 template <typename T, typename A>
-__global__ void __launch_bounds__(kBwdThreads) bwd_reduce(const A* part, int nparts, int64_t n,
-                                                          T* out) {
+__global__ void __launch_bounds__(kBwdReduceThreads) bwd_reduce(const A* part, int nparts,
+                                                                int64_t n, T* out) {
+  constexpr int kBwdThreads = kBwdReduceThreads;
   __shared__ A red[kBwdThreads / 32][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t k = static_cast<int64_t>(blockIdx.x) * 32 + lane;

@@ -179,6 +179,47 @@ def _contextualize_fake(z_tr, v, z_tl, bias, valid, eps, norm_eps, causal, norma
 backward.register()
 
 
+@torch.library.custom_op('avey_b200::contextualize_packed', mutates_args=())
+def contextualize_packed(x: torch.Tensor, v: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                         valid: Optional[torch.Tensor], eps: float, norm_eps: float, causal: bool,
+                         normalize: bool, activation: int) -> torch.Tensor:
+    """``contextualize`` with z_tl = x[..., :d'] and z_tr = x[..., d':] of one
+    [B, C, 2d'] tensor: the same forward, one gradient for x in the backward."""
+    d = x.shape[-1] // 2
+    return contextualize(x[..., d:], v, x[..., :d], bias, valid, eps, norm_eps, causal, normalize,
+                         activation)
+
+
+@contextualize_packed.register_fake
+def _contextualize_packed_fake(x, v, bias, valid, eps, norm_eps, causal, normalize, activation):
+    return x.new_empty((*x.shape[:-1], x.shape[-1] // 2))
+
+
+backward.register_packed()
+
+
+def _packed_base(z_tr, z_tl):
+    """x when z_tl is x[..., :d'] and z_tr is x[..., d':] of one [B, C, 2d']
+    tensor x that requires grad (unit stride along features), else None."""
+    if z_tl is None or not (z_tr.requires_grad and z_tl.requires_grad):
+        return None
+    try:
+        base = z_tr._base
+        if base is None or z_tl._base is not base or not base.requires_grad or base.dim() != 3:
+            return None
+        b, c, d = z_tr.shape
+        if tuple(base.shape) != (b, c, 2 * d) or base.stride(-1) != 1:
+            return None
+        if z_tr.stride() != base.stride() or z_tl.stride() != base.stride():
+            return None
+        p0 = base.data_ptr()
+        if z_tl.data_ptr() != p0 or z_tr.data_ptr() != p0 + d * base.element_size():
+            return None
+        return base
+    except (AttributeError, RuntimeError):
+        return None
+
+
 def plan(z_tr, v=None, z_tl=None, bias=None, valid=None, *, causal=True, normalize=False,
          eps=1e-6, norm_eps=1e-12, activation='identity', kernel=_native.KERNEL_AUTO):
     """The launch the native op would make for these tensors (no launch)."""
@@ -200,6 +241,12 @@ def _dispatch(z_tr, v, z_tl, bias, valid, eps, norm_eps, causal, normalize, acti
     if backend == 'torch' or not native_ok:
         return eager.contextualize(z_tr, v, z_tl, bias, valid, eps=eps, norm_eps=norm_eps,
                                    causal=causal, normalize=normalize, activation=activation)
+    if torch.is_grad_enabled():
+        base = _packed_base(z_tr, z_tl)
+        if base is not None:
+            return contextualize_packed(base, v, bias, valid, float(eps), float(norm_eps),
+                                        bool(causal), bool(normalize),
+                                        _native.ACTIVATION_IDS[activation])
     return contextualize(z_tr, v, z_tl, bias, valid, float(eps), float(norm_eps), bool(causal),
                          bool(normalize), _native.ACTIVATION_IDS[activation])
 

@@ -24,6 +24,12 @@ e2e    the same metric through the public API (avey / avey_b) with pinned
        unmodified install in baseline/_ref): normalisation pre-pass,
        contiguous copies and the Triton mix kernel, device time with CUDA
        events over K calls on the same inputs as --impl ours.
+--pass train  (informational, one GPU) a step is one forward plus backward
+       (gradients of x, W and bias for an upstream gradient of the output's
+       shape): --impl ours runs the native forward and backward, --impl
+       reference the reference's only differentiable path (autograd through
+       avey_kernels.ops._reference, backend='torch', from baseline/_ref) on
+       the same GPU and inputs. Metric 'contextualizer fwd+bwd tokens/s'.
 """
 
 from __future__ import annotations
@@ -633,6 +639,136 @@ def run_triton(args, cfg):
     return 0
 
 
+def run_train(args, cfg):
+    """Forward + backward on one GPU: ours (native) or the reference's autograd."""
+    world, rank, _ = rank_env()
+    if rank != 0:
+        return 0
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    batch = shard_batch(cfg, world)
+    d, n = cfg['d'], cfg['n']
+    if args.impl == 'reference':
+        try:
+            sys.path.insert(0, str(ROOT / 'baseline' / '_ref'))
+            from avey_kernels import ops as api
+        except Exception as e:
+            print(json.dumps({'impl': 'reference', 'pass': 'train', 'unavailable':
+                              f'reference not importable from baseline/_ref: {e}'}), flush=True)
+            return 0
+        kw = dict(backend='torch')
+    else:
+        import avey_kernel_b200 as api
+        from avey_kernel_b200 import _native
+        kw = dict(backend='cuda')
+    nsets = 2
+    sets = []
+    for s_ in range(nsets):
+        t = make_inputs(cfg, batch, seed=s_, device=dev)
+        g = torch.Generator().manual_seed(100 + s_)
+        t['gout'] = torch.randn(batch, n, d, generator=g).to(torch.bfloat16).to(dev)
+        t['x'].requires_grad_(True)
+        if t['w'] is not None:
+            t['w'].requires_grad_(True)
+        if t['bias'] is not None:
+            t['bias'].requires_grad_(True)
+        sets.append(t)
+
+    def step(i):
+        t = sets[i % nsets]
+        head, tail = t['x'][..., :d], t['x'][..., d:]
+        if cfg['op'] == 'avey':
+            out = api.avey(tail, t['w'], z_tl=head, bias=t['bias'], valid=t['valid'], **kw)
+        else:
+            out = api.avey_b(tail, z_tl=head, bias=t['bias'], valid=t['valid'], **kw)
+        leaves = [x for x in (t['x'], t['w'], t['bias']) if x is not None]
+        return torch.autograd.grad(out, leaves, t['gout'])
+
+    grads = step(0)
+    torch.cuda.synchronize()
+    # Parity of the x gradient on one batch row against the gradient oracle.
+    import numpy as np
+    from oracle.backward import contextualize_backward
+    t = sets[0]
+    x = t['x'][:1].detach().float().cpu().numpy()
+    okw = dict(eps=1e-6, norm_eps=1e-12, causal=cfg['op'] == 'avey',
+               normalize=cfg['op'] == 'avey_b', activation='identity')
+    w_np = t['w'].detach().float().cpu().numpy() if t['w'] is not None else None
+    b_np = t['bias'].detach().float().cpu().numpy() if t['bias'] is not None else None
+    v_np = t['valid'][:1].cpu().numpy() if t['valid'] is not None else None
+    gz, _, gzl, _ = contextualize_backward(x[..., d:], w_np, x[..., :d], b_np, v_np,
+                                           t['gout'][:1].float().cpu().numpy(), **okw)
+    ref = np.concatenate([gzl, gz], axis=-1)
+    got = grads[0][:1].float().cpu().numpy()
+    err = float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+
+    def timed(run):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(args.steps):
+            run(i)
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / args.steps
+
+    launches0 = _native.launch_count() if args.impl != 'reference' else None
+    eager_ms = timed(step)
+    launches = _native.launch_count() - launches0 if launches0 is not None else None
+    # The same steps replayed from CUDA graphs (one per input set), which
+    # takes the host's per-op dispatch cost out of the device timeline.
+    graphs, graph_error = [], None
+    try:
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for k in range(nsets):
+                step(k)
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        for k in range(nsets):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                step(k)
+            graphs.append(gr)
+        for gr in graphs:
+            gr.replay()
+        torch.cuda.synchronize()
+    except Exception as exc:  # a path that cannot be captured keeps the eager number
+        graphs, graph_error = [], f'{type(exc).__name__}: {exc}'[:200]
+    with ClockSampler(dev.index) as clocks:
+        ms_step = timed(lambda i: graphs[i % nsets].replay()) if graphs else timed(step)
+    # Dense GEMM work of the native backward (five [N,N]x[N,d'] products per
+    # row) plus the forward's useful work.
+    _, fwd_flops = algorithmic(cfg, batch, t['valid'])
+    bwd_gemm_flops = 5 * 2 * batch * n * n * d
+    line = {
+        'impl': args.impl, 'pass': 'train', 'metric': 'contextualizer fwd+bwd tokens/s',
+        'value': batch * n / (ms_step / 1e3), 'unit': 'tokens/s', 'n_gpus': 1,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms_step,
+        'higher_is_better': True, 'dtype': 'bf16' if args.impl != 'reference' else
+        'bf16 inputs, fp32 arithmetic', 'data': 'synthetic',
+        'config': {'workload': f'{args.config}: {cfg["desc"]}', 'batch_per_gpu': batch,
+                   'grads': 'x (head and tail), W, bias',
+                   'timing': ('forward + torch.autograd.grad captured in CUDA graphs, replayed '
+                              if graphs else 'eager forward + torch.autograd.grad ') +
+                             'between CUDA events; every step streams > 1 GB, larger than L2'},
+        'eager_ms_per_step': eager_ms,
+        'tflops_fwd_useful_plus_bwd_gemm': (fwd_flops + bwd_gemm_flops) / (ms_step / 1e3) / 1e12,
+        'clocks': clocks.summary(),
+        'verify': {'grad_x_max_norm_rel_err_vs_oracle': err, 'rows': 1},
+    }
+    if graph_error:
+        line['graph_capture_error'] = graph_error
+    if launches is not None:
+        line['gpu_launches'] = launches
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -644,6 +780,7 @@ def main():
     ap.add_argument('--config', choices=tuple(CONFIGS), default='c2')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--pass', dest='pass_', choices=('fwd', 'train'), default='fwd')
     args = ap.parse_args()
     if args.steps < 1 or args.warmup < 0:
         ap.error('--steps must be >= 1 and --warmup >= 0')
@@ -651,6 +788,8 @@ def main():
     if world != args.gpus and args.impl == 'ours':
         ap.error(f'--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun')
     cfg = CONFIGS[args.config]
+    if args.pass_ == 'train':
+        return run_train(args, cfg)
     if args.impl == 'reference':
         return run_reference(args, cfg)
     if args.impl == 'triton':

@@ -190,8 +190,8 @@ AVEY_API int avey_fwd_noalloc_v1(const AveyFwdParams* params, void* stream);
  * Accumulator arrays (norms, g, den, num, dden, ds0, dzd, dzh, workspace) are
  * float, or double for f64 inputs; GEMM outputs are written in that type. All
  * scratch arrays are contiguous ([B, C, d'], [B, C, C] or [B, C]); the
- * gradients are contiguous and of the input dtype, and an output pointer left
- * NULL is not computed (grad_v needs v, grad_z_tl needs z_tl). Reductions use
+ * gradients are of the input dtype, and an output pointer left NULL is not
+ * computed (grad_v needs v, grad_z_tl needs z_tl). Reductions use
  * fixed orders: results are bitwise reproducible.
  */
 typedef enum AveyBwdStep {
@@ -239,11 +239,15 @@ typedef struct AveyBwdParams {
   void* workspace; /* partial sums, >= avey_bwd_workspace_size() bytes */
   uint64_t workspace_bytes;
 
-  /* Gradients (contiguous, input dtype); NULL = not wanted. */
+  /* Gradients (input dtype); NULL = not wanted. grad_v and grad_bias are
+   * contiguous; grad_z_tr and grad_z_tl share the element strides below
+   * (0 = contiguous [B, C, d']), so both can be the halves of one
+   * [B, C, 2d'] gradient (row stride 2d'). */
   void* grad_z_tr;
   void* grad_v;
   void* grad_z_tl;
   void* grad_bias;
+  int64_t grad_batch_stride, grad_row_stride;
 } AveyBwdParams;
 
 /* Enqueue one backward step on `stream`. Returns AVEY_OK or a negative

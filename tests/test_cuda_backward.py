@@ -175,3 +175,58 @@ def test_custom_ops_pass_opcheck():
     torch.library.opcheck(backward.contextualize_backward,
                           (z.detach(), w.detach(), zl, None, None, go, 1e-6, 1e-12, True, False, 3,
                            [True, True, True, False]))
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16, torch.float16])
+def test_vector_and_scalar_steps_agree(dtype):
+    # The same values once in 16-byte aligned rows (vector steps) and once
+    # shifted by one element (scalar steps).
+    g = torch.Generator().manual_seed(9)
+    b, n, d = 2, 64, 48
+    base = torch.randn(b, n, 2 * d + 1, generator=g).to(dtype).to(DEV)
+    w = (torch.randn(n, n, generator=g) * 0.1).to(dtype).to(DEV)
+    go = torch.randn(b, n, d, generator=g).to(dtype).to(DEV)
+    aligned = base[..., :2 * d].clone()
+    shifted = base[..., 1:].clone()
+    shifted.copy_(aligned)  # same values, rows start 2 or 4 bytes past 16
+    grads = []
+    for x in (aligned, shifted):
+        xl = x.detach().requires_grad_(True)
+        wl = w.clone().requires_grad_(True)
+        out = avey(xl[..., d:], wl, z_tl=xl[..., :d], activation='gelu')
+        grads.append(torch.autograd.grad(out, (xl, wl), go))
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    for a, c in zip(*grads):
+        assert normwise(np64(a), np64(c)) <= tol
+
+
+@pytest.mark.parametrize('op', ['avey', 'avey_b'])
+def test_packed_head_tail_views_take_one_gradient(op):
+    # z_tl / z_tr as the halves of one [B, C, 2d'] tensor: the packed op gives
+    # x one gradient; it must equal the gradients of separate tensors.
+    g = torch.Generator().manual_seed(21)
+    b, n, d = 2, 200, 96
+    x0 = torch.randn(b, n, 2 * d, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(n, n, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn(d, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    go = torch.randn(b, n, d, generator=g).to(torch.bfloat16).to(DEV)
+
+    def run(zt, zl, bb):
+        if op == 'avey':
+            return avey(zt, w, z_tl=zl, bias=bb, activation='relu')
+        return avey_b(zt, z_tl=zl, bias=bb, eps=0.5, activation='relu')
+
+    x = x0.clone().requires_grad_(True)
+    b1 = bias.clone().requires_grad_(True)
+    out = run(x[..., d:], x[..., :d], b1)
+    assert 'contextualize_packed' in out.grad_fn.name()
+    gx, gb = torch.autograd.grad(out, (x, b1), go)
+    zt = x0[..., d:].clone().requires_grad_(True)
+    zl = x0[..., :d].clone().requires_grad_(True)
+    b2 = bias.clone().requires_grad_(True)
+    out2 = run(zt, zl, b2)
+    assert 'contextualize_packed' not in out2.grad_fn.name()
+    assert torch.equal(out, out2)
+    gzt, gzl, gb2 = torch.autograd.grad(out2, (zt, zl, b2), go)
+    assert torch.equal(gx[..., d:], gzt) and torch.equal(gx[..., :d], gzl)
+    assert torch.equal(gb, gb2)
