@@ -507,17 +507,16 @@ __global__ void __launch_bounds__(kPvThreads, 2)
         for (int q = 0; q < 16; ++q) gw[q] = gn[q];
         if (zrow && c0 + 32 < c_hi) load_raw32<T>(zrow + f_lo + c0 + 32, D - f_lo - c0 - 32, zl_vec, gn, stream);
         tmem_wait_ld(o);
-        const float4* b4 = reinterpret_cast<const float4*>(&ctrl->bias[c0]);
+        float bv[32];
+        load_bias32(&ctrl->bias[c0], has_bias, bv);
         uint32_t pk[16];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float4 bb = has_bias ? b4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
           float yv[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int idx = 4 * q + e;
-            float y = act_fn<ACT>(fmaf(__uint_as_float(o[idx]), inv, bv[e]));
+            float y = act_fn<ACT>(fmaf(__uint_as_float(o[idx]), inv, bv[idx]));
             if (zrow) y *= raw_at<T>(gw, idx);
             yv[e] = row_ok ? y : 0.f;
           }
