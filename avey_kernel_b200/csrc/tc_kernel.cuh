@@ -501,11 +501,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (skip) {
       // Every query row of this tile is padding: the output rows are zero.
-      const int rows = min(128, C - q_lo);
-      for (int e = cw * 32 + lane; e < rows * D; e += 256) {
-        const int r = e / D, f = e % D;
-        out[static_cast<int64_t>(q_lo + r) * args.o_rs + f] = store_cast<T, float>(0.f);
+      // Each warp zeroes its 32 x 32 staging tile and stores it with TMA over
+      // its share of the tile's 32 x 32 boxes (the tensor map clips columns
+      // past d' and rows past the context).
+      const uint32_t stage_z = out_stage_addr + cw * kTcOutTileBytes;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) st_shared_v4(stage_z + lane * 64 + q * 16, 0u, 0u, 0u, 0u);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const uint64_t stream = l2_policy_evict_normal();
+        const int nbf = (D + 31) / 32, nbr = (min(128, C - q_lo) + 31) / 32;
+        for (int k = cw; k < nbf * nbr; k += 8)
+          tma_store_3d(&map_o, stage_z, (k % nbf) * 32, q_lo + (k / nbf) * 32, b, stream);
+        bulk_commit_group();
+        bulk_wait_all();
       }
+      (void)out;
     } else {
       // Warm L2 with the gate of this warpgroup's part of the first output
       // slice (columns 64 h .. 64 h + 63); each drain warms the next slice's.
