@@ -157,6 +157,11 @@ bool vec_ok(const AveyBwdParams* p) {
          rows_ok(p->grad_z_tl, p->grad_batch_stride, p->grad_row_stride);
 }
 
+// One warp per partial sum, up to 32 warps.
+unsigned reduce_threads(int64_t nparts) {
+  return static_cast<unsigned>(32 * std::min<int64_t>(32, std::max<int64_t>(1, nparts)));
+}
+
 int row_grid(const AveyBwdParams* p) {
   const int64_t warps = p->batch * p->context;
   return static_cast<int>(std::min<int64_t>((warps + 7) / 8, 148 * 16));
@@ -212,7 +217,7 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
       if (!done) avey::bwd_epilogue<T, G, A><<<static_cast<unsigned>(nb), kT, 0, st>>>(a);
       int n = 1;
       if (a.gbias) {
-        avey::bwd_reduce<T, A><<<static_cast<unsigned>((p->features + 31) / 32), avey::kBwdReduceThreads, 0, st>>>(
+        avey::bwd_reduce<T, A><<<static_cast<unsigned>((p->features + 31) / 32), reduce_threads(nb), 0, st>>>(
             static_cast<const A*>(p->workspace), static_cast<int>(nb), p->features,
             static_cast<T*>(p->grad_bias));
         ++n;
@@ -225,11 +230,18 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
         return fail(AVEY_ERR_ARGUMENT, "dscores needs ds0, g, dden, dgsym (and workspace for grad_v)");
       int pairs, groups, per;
       dscores_grid(p, &pairs, &groups, &per);
-      avey::bwd_dscores<T, G, A><<<dim3(pairs, groups), kT, 0, st>>>(a, per);
+      bool vdone = false;
+      if constexpr (kHasVec) {
+        if (vec) {
+          avey::bwd_dscores_v4<T, G><<<dim3(pairs, groups), kT, 0, st>>>(a, per);
+          vdone = true;
+        }
+      }
+      if (!vdone) avey::bwd_dscores<T, G, A><<<dim3(pairs, groups), kT, 0, st>>>(a, per);
       int n = 1;
       if (a.gv) {
         const int64_t cc = p->context * p->context;
-        avey::bwd_reduce<T, A><<<static_cast<unsigned>((cc + 31) / 32), avey::kBwdReduceThreads, 0, st>>>(
+        avey::bwd_reduce<T, A><<<static_cast<unsigned>((cc + 31) / 32), reduce_threads(groups), 0, st>>>(
             static_cast<const A*>(p->workspace), groups, cc, static_cast<T*>(p->grad_v));
         ++n;
       }

@@ -728,25 +728,174 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
   }
 }
 
-// out[k] = sum over p of part[p][k], p in order (32 warps take interleaved p,
-// then combine in warp order): deterministic.
+template <typename G>
+__device__ __forceinline__ void st4(G* p, const float (&v)[4]);
+template <>
+__device__ __forceinline__ void st4<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[4]) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) =
+      make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+}
+template <>
+__device__ __forceinline__ void st4<float>(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+// Step 4, vector form (fp32 accumulation, contexts a multiple of 8): a thread
+// owns 4 consecutive columns of one row of each tile (float4 loads), the
+// next batch row's operands are loaded while the current one is computed,
+// the transposes go through double-buffered shared tiles (two barriers per
+// batch row), and the norms and key validity come straight from global memory.
+struct DsIn {
+  float4 ds, g, nk;  // ds0 and Gr of 4 columns, norms of their keys
+  float nq, dd;      // norm of the row's query, its dden
+};
+
+__device__ __forceinline__ DsIn ds_load(const BwdArgs& a, int64_t base, int64_t rb, int i, int j,
+                                        bool in, bool want_g) {
+  DsIn x;
+  x.ds = x.g = x.nk = make_float4(0.f, 0.f, 0.f, 0.f);
+  x.nq = 1.f;
+  x.dd = 0.f;
+  if (in) {
+    const int64_t off = base + static_cast<int64_t>(i) * a.ctx + j;
+    x.ds = *reinterpret_cast<const float4*>(static_cast<const float*>(a.ds0) + off);
+    if (want_g) x.g = *reinterpret_cast<const float4*>(static_cast<const float*>(a.g) + off);
+    x.nk = *reinterpret_cast<const float4*>(static_cast<const float*>(a.norms) + rb + j);
+    x.nq = static_cast<const float*>(a.norms)[rb + i];
+    if (a.normalize) x.dd = static_cast<const float*>(a.dden)[rb + i];
+  }
+  return x;
+}
+
+// dG of 4 columns (j .. j+3) of query row i, the dV partial sums, and r of
+// the 4 keys.
+__device__ __forceinline__ void ds_compute(const BwdArgs& a, const DsIn& x, int b, int i, int j,
+                                           bool in, const float (&v)[4], float (&acc)[4],
+                                           float (&dg)[4], float (&rk)[4]) {
+  const float ne = static_cast<float>(a.norm_eps);
+  const float xs[4] = {x.ds.x, x.ds.y, x.ds.z, x.ds.w};
+  const float gs[4] = {x.g.x, x.g.y, x.g.z, x.g.w};
+  const float ns[4] = {x.nk.x, x.nk.y, x.nk.z, x.nk.w};
+  const float rq = 1.f / fmaxf(x.nq, ne);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    rk[e] = in ? 1.f / fmaxf(ns[e], ne) : 0.f;
+    const bool ok = in && (!a.causal || j + e <= i) && row_valid(a, b, j + e);
+    const float dsm = ok ? xs[e] + x.dd : 0.f;
+    acc[e] = fmaf(dsm, gs[e] * rq * rk[e], acc[e]);
+    dg[e] = dsm * v[e];
+  }
+}
+
+template <typename T, typename G>
+__global__ void __launch_bounds__(kBwdThreads) bwd_dscores_v4(const BwdArgs a, int bpg) {
+  __shared__ float tr[2][kBwdTile][kBwdTile + 1];
+  __shared__ float ts[2][kBwdTile][kBwdTile + 1];
+  const int row = threadIdx.x >> 3, c4 = (threadIdx.x & 7) * 4;
+  const int C = a.ctx;
+  const int nt = C / kBwdTile + (C % kBwdTile ? 1 : 0);
+  int p = blockIdx.x, I = 0;
+  while (p >= nt - I) {
+    p -= nt - I;
+    ++I;
+  }
+  const int J = I + p;
+  const bool diag = I == J;
+  const int I0 = I * kBwdTile, J0 = J * kBwdTile;
+  const int b0 = blockIdx.y * bpg, b1 = min(a.batch, b0 + bpg);
+  const T* v = static_cast<const T*>(a.v);
+  G* dgs = static_cast<G*>(a.dgsym);
+  const bool want_g = a.gv != nullptr;
+  // Tile (I, J): row i1 = I0 + row, columns j1 = J0 + c4 + e. Tile (J, I):
+  // row i2 = J0 + row, columns j2 = I0 + c4 + e. Four columns are in range
+  // together (C is a multiple of 8, tiles start at multiples of 32).
+  const int i1 = I0 + row, i2 = J0 + row, j1 = J0 + c4, j2 = I0 + c4;
+  const bool in1 = i1 < C && j1 < C, in2 = !diag && i2 < C && j2 < C;
+  float v1[4], v2[4], acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    v1[e] = (v && in1) ? ld_as<float>(v + static_cast<int64_t>(i1) * a.v_rs + j1 + e) : 1.f;
+    v2[e] = (v && in2) ? ld_as<float>(v + static_cast<int64_t>(i2) * a.v_rs + j2 + e) : 1.f;
+  }
+  DsIn n1, n2;
+  if (b0 < b1) {
+    n1 = ds_load(a, static_cast<int64_t>(b0) * C * C, static_cast<int64_t>(b0) * C, i1, j1, in1, want_g);
+    n2 = ds_load(a, static_cast<int64_t>(b0) * C * C, static_cast<int64_t>(b0) * C, i2, j2, in2, want_g);
+  }
+  int buf = 0;
+  for (int b = b0; b < b1; ++b, buf ^= 1) {
+    const int64_t base = static_cast<int64_t>(b) * C * C;
+    const DsIn x1 = n1, x2 = n2;
+    if (b + 1 < b1) {  // the next batch row's operands, in flight during this one
+      n1 = ds_load(a, base + static_cast<int64_t>(C) * C, static_cast<int64_t>(b + 1) * C, i1, j1,
+                   in1, want_g);
+      n2 = ds_load(a, base + static_cast<int64_t>(C) * C, static_cast<int64_t>(b + 1) * C, i2, j2,
+                   in2, want_g);
+    }
+    float dg1[4], r1[4], dg2[4], r2[4];
+    ds_compute(a, x1, b, i1, j1, in1, v1, acc1, dg1, r1);
+    if (!diag) {
+      ds_compute(a, x2, b, i2, j2, in2, v2, acc2, dg2, r2);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tr[buf][row][c4 + e] = dg2[e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        tr[buf][row][c4 + e] = dg1[e];
+        r2[e] = r1[e];
+      }
+    }
+    __syncthreads();
+    // dGsym (I, J)[row][c] = dG(I, J)[row][c] + dG(J, I)[c][row], column c
+    // scaled by r of key J0 + c.
+    float sym[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      sym[e] = dg1[e] + tr[buf][c4 + e][row];
+      ts[buf][row][c4 + e] = sym[e];
+      sym[e] *= r1[e];
+    }
+    if (in1) st4<G>(dgs + base + static_cast<int64_t>(i1) * C + j1, sym);
+    __syncthreads();
+    if (in2) {
+      // Tile (J, I) is the transpose of tile (I, J); column c scaled by r of
+      // key I0 + c.
+      float t4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t4[e] = ts[buf][c4 + e][row] * r2[e];
+      st4<G>(dgs + base + static_cast<int64_t>(i2) * C + j2, t4);
+    }
+  }
+  if (want_g) {
+    float* part = static_cast<float*>(a.part) + static_cast<int64_t>(blockIdx.y) * C * C;
+    if (in1)
+      *reinterpret_cast<float4*>(part + static_cast<int64_t>(i1) * C + j1) =
+          make_float4(acc1[0], acc1[1], acc1[2], acc1[3]);
+    if (in2)
+      *reinterpret_cast<float4*>(part + static_cast<int64_t>(i2) * C + j2) =
+          make_float4(acc2[0], acc2[1], acc2[2], acc2[3]);
+  }
+}
+
+// out[k] = sum over p of part[p][k], p in order: the warps of a block take
+// interleaved p (as many warps as parts, up to 32), then combine in warp
+// order: deterministic.
 constexpr int kBwdReduceThreads = 1024;
 template <typename T, typename A>
 __global__ void __launch_bounds__(kBwdReduceThreads) bwd_reduce(const A* part, int nparts,
                                                                 int64_t n, T* out) {
-  constexpr int kBwdThreads = kBwdReduceThreads;
-  __shared__ A red[kBwdThreads / 32][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ A red[kBwdReduceThreads / 32][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int64_t k = static_cast<int64_t>(blockIdx.x) * 32 + lane;
   A t = 0;
   if (k < n)
-    for (int p = warp; p < nparts; p += kBwdThreads / 32) t += part[static_cast<int64_t>(p) * n + k];
+    for (int p = warp; p < nparts; p += nw) t += part[static_cast<int64_t>(p) * n + k];
   red[warp][lane] = t;
   __syncthreads();
   if (warp == 0 && k < n) {
     A s = 0;
-#pragma unroll
-    for (int w = 0; w < kBwdThreads / 32; ++w) s += red[w][lane];
+    for (int w = 0; w < nw; ++w) s += red[w][lane];
     st_as<T>(out + k, s);
   }
 }
