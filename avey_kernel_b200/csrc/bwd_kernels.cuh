@@ -492,8 +492,8 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_prep_v8(const BwdArgs a) {
   const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
   const int nv = a.feat / 8;
-  const T* z = static_cast<const T*>(a.z_tr);
-  G* zm = static_cast<G*>(a.zm);
+  const T* __restrict__ z = static_cast<const T*>(a.z_tr);
+  G* __restrict__ zm = static_cast<G*>(a.zm);
   for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
        r += nwarps) {
     const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
@@ -524,10 +524,10 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_scores_v8(const BwdArgs a) {
   const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
   const int C = a.ctx;
-  const float* gr = static_cast<const float*>(a.g);
-  const float* norms = static_cast<const float*>(a.norms);
-  G* s = static_cast<G*>(a.s);
-  const T* v = static_cast<const T*>(a.v);
+  const float* __restrict__ gr = static_cast<const float*>(a.g);
+  const float* __restrict__ norms = static_cast<const float*>(a.norms);
+  G* __restrict__ s = static_cast<G*>(a.s);
+  const T* __restrict__ v = static_cast<const T*>(a.v);
   const float ne = static_cast<float>(a.norm_eps);
   for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
        r += nwarps) {
@@ -590,14 +590,14 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_epilogue_v8(const BwdArgs a) 
   const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
   const int d = a.feat, C = a.ctx, nv = d / 8;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kBwdEpiRowsV8 + warp * kRows;
-  const float* num = static_cast<const float*>(a.num);
-  const float* den = static_cast<const float*>(a.den);
-  float* dden = static_cast<float*>(a.dden);
-  const T* bias = static_cast<const T*>(a.bias);
-  const T* zl = static_cast<const T*>(a.z_tl);
-  const T* go = static_cast<const T*>(a.gout);
-  G* dnum = static_cast<G*>(a.dnum);
-  T* gzl = static_cast<T*>(a.gz_tl);
+  const float* __restrict__ num = static_cast<const float*>(a.num);
+  const float* __restrict__ den = static_cast<const float*>(a.den);
+  float* __restrict__ dden = static_cast<float*>(a.dden);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  const T* __restrict__ zl = static_cast<const T*>(a.z_tl);
+  const T* __restrict__ go = static_cast<const T*>(a.gout);
+  G* __restrict__ dnum = static_cast<G*>(a.dnum);
+  T* __restrict__ gzl = static_cast<T*>(a.gz_tl);
   for (int w0 = 0; w0 < nv; w0 += 32 * kBwdEpiSlots) {
     float db[kBwdEpiSlots][8];
 #pragma unroll
@@ -687,10 +687,10 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
   const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
   const int d = a.feat, nv = d / 8;
-  const G* zm = static_cast<const G*>(a.zm);
-  const float* dzh = static_cast<const float*>(a.dzh);
-  const float* dzd = static_cast<const float*>(a.dzd);
-  T* gz = static_cast<T*>(a.gz_tr);
+  const G* __restrict__ zm = static_cast<const G*>(a.zm);
+  const float* __restrict__ dzh = static_cast<const float*>(a.dzh);
+  const float* __restrict__ dzd = static_cast<const float*>(a.dzd);
+  T* __restrict__ gz = static_cast<T*>(a.gz_tr);
   const float ne = static_cast<float>(a.norm_eps);
   for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
        r += nwarps) {
