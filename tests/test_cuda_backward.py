@@ -230,3 +230,42 @@ def test_packed_head_tail_views_take_one_gradient(op):
     gzt, gzl, gb2 = torch.autograd.grad(out2, (zt, zl, b2), go)
     assert torch.equal(gx[..., d:], gzt) and torch.equal(gx[..., :d], gzl)
     assert torch.equal(gb, gb2)
+
+
+def test_packed_custom_ops_pass_opcheck():
+    from avey_kernel_b200 import backward, ops
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(2, 24, 32, generator=g).to(DEV).requires_grad_(True)
+    w = torch.randn(24, 24, generator=g).to(DEV).requires_grad_(True)
+    torch.library.opcheck(ops.contextualize_packed, (x, w, None, None, 1e-6, 1e-12, True, False, 4))
+    go = torch.randn(2, 24, 16, generator=g).to(DEV)
+    torch.library.opcheck(backward.contextualize_packed_backward,
+                          (x.detach(), w.detach(), None, None, go, 1e-6, 1e-12, True, False, 4,
+                           [True, True, False]))
+
+
+def test_training_step_replays_from_a_cuda_graph():
+    # Forward + backward captured once and replayed: the same gradients as eager.
+    g = torch.Generator().manual_seed(8)
+    b, n, d = 2, 128, 64
+    x = torch.randn(b, n, 2 * d, generator=g).to(torch.bfloat16).to(DEV).requires_grad_(True)
+    w = (torch.randn(n, n, generator=g) * 0.05).to(torch.bfloat16).to(DEV).requires_grad_(True)
+    go = torch.randn(b, n, d, generator=g).to(torch.bfloat16).to(DEV)
+
+    def step():
+        out = avey(x[..., d:], w, z_tl=x[..., :d], activation='gelu')
+        return torch.autograd.grad(out, (x, w), go)
+
+    eager = step()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = step()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, c in zip(eager, captured):
+        assert torch.equal(a, c)

@@ -154,3 +154,55 @@ def test_workspace_size_is_four_bytes_per_row_on_the_tcgen05_path():
     p = ops.build_params(z32, None, None, None, None, z32.clone(), eps=1e-6, norm_eps=1e-12,
                          causal=False, normalize=True, activation_id=0)
     assert _native.workspace_size(p) == 0
+
+
+def _bwd_params(b=2, c=64, d=128, dtype=_native.AVEY_BF16, gemm=_native.AVEY_BF16, with_v=True):
+    p = _native.new_bwd_params()
+    p.dtype, p.gemm_dtype = dtype, gemm
+    p.batch, p.context, p.features = b, c, d
+    p.eps, p.norm_eps = 1e-6, 1e-12
+    p.causal = 1
+    p.z_tr = 0x1000  # host-side checks only: nothing is dereferenced or launched
+    p.z_tr_batch_stride, p.z_tr_row_stride = c * d, d
+    if with_v:
+        p.v, p.v_row_stride = 0x2000, c
+    return p
+
+
+def test_backward_workspace_size_covers_dbias_and_dv_partial_sums():
+    # Vector form (rows of multiples of 8, aligned): 32 rows per epilogue block,
+    # one fp32 partial row of d' per block; dV: one [C, C] partial per batch group.
+    p = _bwd_params(b=2, c=64, d=128)
+    epi = (2 * 64 // 32) * 128
+    pairs = 2 * 3 // 2  # 64 tokens = 2 tiles of 32: (0,0), (0,1), (1,1)
+    groups = min(2, -(-1184 // pairs), 16)
+    assert _native.bwd_workspace_size(p) == max(epi, groups * 64 * 64) * 4
+    p64 = _bwd_params(dtype=_native.AVEY_F64, gemm=_native.AVEY_F64, with_v=False)
+    assert _native.bwd_workspace_size(p64) == (2 * 64 // 64) * 128 * 8  # scalar form, fp64
+
+
+@pytest.mark.parametrize('field,value,match', [
+    ('gemm_dtype', _native.AVEY_F32, 'gemm_dtype'),
+    ('batch', 0, 'out of range'),
+    ('activation', 5, 'activation'),
+    ('eps', -1.0, 'finite and positive'),
+    ('z_tr_row_stride', 4, 'strides'),
+    ('grad_row_stride', 8, 'strides'),
+    ('struct_size', 12, 'struct_size'),
+])
+def test_backward_rejects_invalid_arguments_before_any_launch(field, value, match):
+    p = _bwd_params()
+    setattr(p, field, value)
+    before = _native.launch_count()
+    with pytest.raises(_native.NativeError, match=match):
+        _native.bwd_step(p, _native.BWD_PREP, 0)
+    assert _native.launch_count() == before
+
+
+def test_backward_steps_check_their_buffers_and_step_ids():
+    p = _bwd_params()
+    for step, match in ((_native.BWD_PREP, 'prep needs'), (_native.BWD_SCORES, 'scores needs'),
+                        (_native.BWD_EPILOGUE, 'epilogue needs'), (_native.BWD_DSCORES, 'dscores needs'),
+                        (_native.BWD_FINAL, 'final needs'), (9, 'unknown backward step')):
+        with pytest.raises(_native.NativeError, match=match):
+            _native.bwd_step(p, step, 0)
