@@ -201,6 +201,8 @@ __device__ __forceinline__ void bulk_commit_group() {
 __device__ __forceinline__ void bulk_wait_read_1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
+// At the end of a kernel this is enough: the stores' global writes complete
+// before the grid does, so only the shared-memory source must outlive them.
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }

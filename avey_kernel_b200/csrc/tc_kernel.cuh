@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int k = cw; k < nbf * nbr; k += 8)
           tma_store_3d(&map_o, stage_z, (k % nbf) * 32, q_lo + (k / nbf) * 32, b, stream);
         bulk_commit_group();
-        bulk_wait_all();
+        bulk_wait_read_all();
       }
       (void)out;
     } else {
@@ -776,7 +776,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         load_raw32<T>(zrow + ch_lo * 32, D - ch_lo * 32, zl_vec, gn, stream);
       if (!fix || h == 0) {
         for (int s = 0; s < nslices; ++s) drain(s);
-        if (lane == 0) bulk_wait_all();
+        if (lane == 0) bulk_wait_read_all();
       } else {
         // Fix mode: zero every padded key row of each mix unit before the MMA
         // reads it (warpgroup 1), while warpgroup 0 drains all slices.

@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kLgThreads, 2)
       if (norm && i < C)
         geom.den_part[(static_cast<int64_t>(b) * geom.n_groups + kg) * C + i] =
             (den4[0] + den4[1]) + (den4[2] + den4[3]);
-      if (lane == 0) bulk_wait_all();
+      if (lane == 0) bulk_wait_read_all();
     }
   }
 
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(kPvThreads, 2)
           warp_tile_store(stage0, pk, &map_o, f_lo + c0, q_lo + wq * 32,
                           b, stream, lane);
       }
-      if (lane == 0) bulk_wait_all();
+      if (lane == 0) bulk_wait_read_all();
     }
   }
 
