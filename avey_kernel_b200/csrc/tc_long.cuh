@@ -465,12 +465,24 @@ __global__ void __launch_bounds__(kPvThreads, 2)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     T* out = static_cast<T*>(args.out) + static_cast<int64_t>(b) * args.o_bs;
     if (skip) {
-      // No valid query row in this tile: its output rows are zero.
-      const int rows = min(128, C - q_lo);
-      for (int e = cw * 32 + lane; e < rows * width; e += 32 * (kPvThreads / 32 - 4)) {
-        const int r = e / width, f = e % width;
-        out[static_cast<int64_t>(q_lo + r) * args.o_rs + f_lo + f] = store_cast<T, float>(0.f);
+      // No valid query row in this tile: its output rows are zero. Each warp
+      // zeroes its 32 x 32 staging tile and stores it with TMA over its share
+      // of the tile's boxes (the tensor map clips rows past the context and
+      // columns past d').
+      const uint32_t stage_z = staging + cw * kPvStageTiles * kTcOutTileBytes;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) st_shared_v4(stage_z + lane * 64 + q * 16, 0u, 0u, 0u, 0u);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const uint64_t stream = l2_policy_evict_normal();
+        const int nbf = (width + 31) / 32, nbr = (min(128, C - q_lo) + 31) / 32;
+        for (int k = cw; k < nbf * nbr; k += kPvThreads / 32 - 4)
+          tma_store_3d(&map_o, stage_z, f_lo + (k % nbf) * 32, q_lo + (k / nbf) * 32, b, stream);
+        bulk_commit_group();
+        bulk_wait_read_all();
       }
+      (void)out;
     } else {
       griddep_wait();  // P, the partial sums and the sums of squares come from earlier launches
       const bool row_ok = i < C && pos_valid(args, b, i);

@@ -357,3 +357,31 @@ def test_autograd_inputs_run_the_native_backward():
     z.grad = None
     avey_b(z, backend='cuda').sum().backward()
     assert z.grad is not None
+
+
+@pytest.mark.parametrize('n', [512, 900], ids=['fused', 'long'])
+def test_fully_padded_query_tiles_overwrite_their_output_rows_with_zeros(n):
+    # The output buffer starts as NaN: every padded row must come back exactly
+    # zero, every valid row must match the oracle.
+    g = torch.Generator(device='cpu').manual_seed(n)
+    b, d = 3, 128
+    x = torch.randn(b, n, 2 * d, generator=g).to(torch.bfloat16).to(DEV)
+    head, tail = x[..., :d], x[..., d:]
+    lengths = torch.tensor([n, 130, 40])
+    valid = (torch.arange(n)[None, :] < lengths[:, None]).to(DEV)
+    out = torch.full(tail.shape, float('nan'), dtype=tail.dtype, device=DEV)
+    params = ops.build_params(tail, None, head, None, valid, out, eps=1e-6, norm_eps=1e-12,
+                              causal=False, normalize=True, activation_id=0)
+    nbytes = _native.workspace_size(params)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=DEV)
+    params.workspace, params.workspace_bytes = ws.data_ptr(), nbytes
+    assert _native.plan(params).kernel == _native.KERNEL_TCGEN05
+    _native.forward(params, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    y = to_numpy(out)
+    ok = to_numpy(valid.float()) > 0
+    assert (y[~ok] == 0).all() and np.isfinite(y).all()
+    for r in range(b):
+        ref = oracle.avey_b(to_numpy(tail[r:r + 1]), z_tl=to_numpy(head[r:r + 1]),
+                            valid=ok[r:r + 1])
+        assert norm_rel_err(y[r:r + 1], ref) <= TOL['bfloat16']
