@@ -137,25 +137,31 @@ constexpr bool kRowScaleInP = !std::is_same<T, __nv_bfloat16>::value;
 // gives 0); otherwise keys outside the allowed set already carry rk = 0. NORM
 // accumulates the row sums of P; HAS_V multiplies by the weight row.
 template <typename T, bool MASKED, bool NORM, bool HAS_V>
-__device__ __forceinline__ void p_chunk(const uint32_t (&g)[32], const float4* rk4, float rqi,
+__device__ __forceinline__ void p_chunk(const uint32_t (&g)[32], const float (&rk)[32], float rqi,
                                         const uint32_t (&vw)[16], uint32_t okb, uint32_t (&pk)[16],
                                         float (&den)[4]);
 
+// 32 consecutive fp32 values from shared memory, all loaded before any is
+// used: shared-memory loads interleaved with arithmetic stall behind the
+// tensor core's and TMA's shared-memory traffic (measured on the bias of the
+// epilogue: 1.5 us per config-2 forward).
+__device__ __forceinline__ void load_f32x32(const float* src, float (&v)[32]) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 x = s4[q];
+    v[4 * q] = x.x;
+    v[4 * q + 1] = x.y;
+    v[4 * q + 2] = x.z;
+    v[4 * q + 3] = x.w;
+  }
+}
+
 // The 32 bias values of one 32-feature output chunk (fp32, staged in shared
-// memory), all loaded before any is used: loads interleaved with the epilogue
-// arithmetic stall on shared memory, which the tensor core and TMA keep busy
-// during the mix phase (measured: 1.5 us per config-2 forward).
+// memory), or zeros.
 __device__ __forceinline__ void load_bias32(const float* bias, bool has_bias, float (&bv)[32]) {
   if (has_bias) {
-    const float4* b4 = reinterpret_cast<const float4*>(bias);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 bb = b4[q];
-      bv[4 * q] = bb.x;
-      bv[4 * q + 1] = bb.y;
-      bv[4 * q + 2] = bb.z;
-      bv[4 * q + 3] = bb.w;
-    }
+    load_f32x32(bias, bv);
   } else {
 #pragma unroll
     for (int q = 0; q < 32; ++q) bv[q] = 0.f;
@@ -171,18 +177,16 @@ __device__ __forceinline__ float raw_at(const uint32_t (&w)[16], int e) {
 }
 
 template <typename T, bool MASKED, bool NORM, bool HAS_V>
-__device__ __forceinline__ void p_chunk(const uint32_t (&g)[32], const float4* rk4, float rqi,
+__device__ __forceinline__ void p_chunk(const uint32_t (&g)[32], const float (&rk)[32], float rqi,
                                         const uint32_t (&vw)[16], uint32_t okb, uint32_t (&pk)[16],
                                         float (&den)[4]) {
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
-    const float4 rk = rk4[q];
-    const float r[4] = {rk.x, rk.y, rk.z, rk.w};
     float pv[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int idx = 4 * q + e;
-      float p = __uint_as_float(g[idx]) * r[e];
+      float p = __uint_as_float(g[idx]) * rk[idx];
       if (kRowScaleInP<T>) p *= rqi;
       if (HAS_V) p *= raw_at<T>(vw, idx);
       if (MASKED) p = ((okb >> idx) & 1u) ? p : 0.f;
@@ -624,24 +628,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               okb &= lim >= 32 ? 0xFFFFFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
             }
           }
+          // The chunk's 32 inverse key norms, loaded while the TMEM load is in flight.
+          float rk[32];
+          load_f32x32(&ctrl->rinv[c0], rk);
           tmem_wait_ld(g);
-          const float4* rk4 = reinterpret_cast<const float4*>(&ctrl->rinv[c0]);
           uint32_t pk[16];
           if (args.has_v) {  // uniform; rows past the context multiply by ones
             if (masked) {
-              if (norm) p_chunk<T, true, true, true>(g, rk4, rqi, vw, okb, pk, den4);
-              else p_chunk<T, true, false, true>(g, rk4, rqi, vw, okb, pk, den4);
+              if (norm) p_chunk<T, true, true, true>(g, rk, rqi, vw, okb, pk, den4);
+              else p_chunk<T, true, false, true>(g, rk, rqi, vw, okb, pk, den4);
             } else {
-              if (norm) p_chunk<T, false, true, true>(g, rk4, rqi, vw, okb, pk, den4);
-              else p_chunk<T, false, false, true>(g, rk4, rqi, vw, okb, pk, den4);
+              if (norm) p_chunk<T, false, true, true>(g, rk, rqi, vw, okb, pk, den4);
+              else p_chunk<T, false, false, true>(g, rk, rqi, vw, okb, pk, den4);
             }
           } else {
             if (masked) {
-              if (norm) p_chunk<T, true, true, false>(g, rk4, rqi, vw, okb, pk, den4);
-              else p_chunk<T, true, false, false>(g, rk4, rqi, vw, okb, pk, den4);
+              if (norm) p_chunk<T, true, true, false>(g, rk, rqi, vw, okb, pk, den4);
+              else p_chunk<T, true, false, false>(g, rk, rqi, vw, okb, pk, den4);
             } else {
-              if (norm) p_chunk<T, false, true, false>(g, rk4, rqi, vw, okb, pk, den4);
-              else p_chunk<T, false, false, false>(g, rk4, rqi, vw, okb, pk, den4);
+              if (norm) p_chunk<T, false, true, false>(g, rk, rqi, vw, okb, pk, den4);
+              else p_chunk<T, false, false, false>(g, rk, rqi, vw, okb, pk, den4);
             }
           }
           // Packed pairs into TMEM columns this thread has already read.

@@ -305,24 +305,25 @@ __global__ void __launch_bounds__(kLgThreads, 2)
             okb &= lim >= 32 ? 0xFFFFFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
           }
         }
+        float rk[32];  // the chunk's inverse key norms, loaded while the TMEM load is in flight
+        load_f32x32(&ctrl->rinv[c0], rk);
         tmem_wait_ld(g);
-        const float4* rk4 = reinterpret_cast<const float4*>(&ctrl->rinv[c0]);
         uint32_t pk[16];
         if (args.has_v) {
           if (masked) {
-            if (norm) p_chunk<T, true, true, true>(g, rk4, rqi, vw, okb, pk, den4);
-            else p_chunk<T, true, false, true>(g, rk4, rqi, vw, okb, pk, den4);
+            if (norm) p_chunk<T, true, true, true>(g, rk, rqi, vw, okb, pk, den4);
+            else p_chunk<T, true, false, true>(g, rk, rqi, vw, okb, pk, den4);
           } else {
-            if (norm) p_chunk<T, false, true, true>(g, rk4, rqi, vw, okb, pk, den4);
-            else p_chunk<T, false, false, true>(g, rk4, rqi, vw, okb, pk, den4);
+            if (norm) p_chunk<T, false, true, true>(g, rk, rqi, vw, okb, pk, den4);
+            else p_chunk<T, false, false, true>(g, rk, rqi, vw, okb, pk, den4);
           }
         } else {
           if (masked) {
-            if (norm) p_chunk<T, true, true, false>(g, rk4, rqi, vw, okb, pk, den4);
-            else p_chunk<T, true, false, false>(g, rk4, rqi, vw, okb, pk, den4);
+            if (norm) p_chunk<T, true, true, false>(g, rk, rqi, vw, okb, pk, den4);
+            else p_chunk<T, true, false, false>(g, rk, rqi, vw, okb, pk, den4);
           } else {
-            if (norm) p_chunk<T, false, true, false>(g, rk4, rqi, vw, okb, pk, den4);
-            else p_chunk<T, false, false, false>(g, rk4, rqi, vw, okb, pk, den4);
+            if (norm) p_chunk<T, false, true, false>(g, rk, rqi, vw, okb, pk, den4);
+            else p_chunk<T, false, false, false>(g, rk, rqi, vw, okb, pk, den4);
           }
         }
         // The previous store from this warp's staging tile must have read it.
