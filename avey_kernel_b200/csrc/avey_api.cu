@@ -182,8 +182,7 @@ LongLayout long_layout(const AveyFwdParams* p) {
   l.total = l.off_p + static_cast<uint64_t>(B * C * cp) * 2u;
   l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes +
               4 * avey::kLgWG * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kLgCtrlBytes;
-  l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes +
-              4 * avey::kPvStageTiles * avey::kTcOutTileBytes + avey::kPvCtrlBytes;
+  l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes + avey::kPvCtrlBytes;
   return l;
 }
 

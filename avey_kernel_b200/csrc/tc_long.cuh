@@ -35,11 +35,11 @@ constexpr int kLgStageTiles = 1;             // output staging tiles per compute
 constexpr int kLgCtrlBytes = 2048;
 constexpr int kLongMaxContext = 8192;
 
-// tc_pv: 256 threads (producer warp, MMA warp, two idle warps, one compute
-// warpgroup) and ~107 KB of shared memory, so two CTAs share an SM and one's
-// epilogue overlaps the other's main loop.
+// tc_pv: 256 threads (producer warp, MMA warp, two idle warps, one warpgroup
+// that waits for the accumulator; all eight warps then drain it) and ~99 KB of
+// shared memory, so two CTAs share an SM and one's epilogue overlaps the
+// other's main loop.
 constexpr int kPvThreads = 256;
-constexpr int kPvStageTiles = 1;             // output staging tiles per compute warp
 constexpr int kPvGroupCols = 256;            // output features per tc_pv item (TMEM columns)
 constexpr int kPvChunkKeys = 64;             // keys per pipeline stage
 constexpr int kPvABytes = 128 * kPvChunkKeys * 2;  // P box {64 keys, 128 rows}: 16 KB
@@ -366,10 +366,8 @@ __global__ void __launch_bounds__(kPvThreads, 2)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw);
-  const uint32_t ring = base;
-  const uint32_t staging = base + kPvStages * kPvStageBytes;
-  PvCtrl* ctrl = reinterpret_cast<PvCtrl*>(base_ptr + kPvStages * kPvStageBytes +
-                                           4 * kPvStageTiles * kTcOutTileBytes);
+  const uint32_t ring = base;  // TMA stages; output staging tiles in the epilogue
+  PvCtrl* ctrl = reinterpret_cast<PvCtrl*>(base_ptr + kPvStages * kPvStageBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = args.ctx, D = args.feat;
@@ -460,30 +458,36 @@ __global__ void __launch_bounds__(kPvThreads, 2)
       }
       tc_commit(smem_u32(&ctrl->o_full));
     }
-  } else if (warp >= 4) {
-    const int cw = warp - 4, wq = warp & 3;
+  }
+  __syncwarp();  // lanes 1-31 of the producer and MMA warps rejoin lane 0
+
+  // Epilogue: after the last MMA the stage ring is idle, so it holds the
+  // output staging tiles (two per warp), and all eight warps drain the
+  // accumulator: the warps of one TMEM lane quarter (w and w + 4) take one
+  // half of the columns each.
+  if (!skip || (warp != 2 && warp != 3)) {  // padded tiles: warps 0, 1, 4-7 write the zeros
+    const int wq = warp & 3, half = warp >> 2;
     const int row = wq * 32 + lane, i = q_lo + row;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    T* out = static_cast<T*>(args.out) + static_cast<int64_t>(b) * args.o_bs;
+    const uint32_t stage_w = ring + warp * 2 * kTcOutTileBytes;
     if (skip) {
       // No valid query row in this tile: its output rows are zero. Each warp
-      // zeroes its 32 x 32 staging tile and stores it with TMA over its share
-      // of the tile's boxes (the tensor map clips rows past the context and
+      // zeroes a staging tile and stores it with TMA over its share of the
+      // tile's 32 x 32 boxes (the tensor map clips rows past the context and
       // columns past d').
-      const uint32_t stage_z = staging + cw * kPvStageTiles * kTcOutTileBytes;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) st_shared_v4(stage_z + lane * 64 + q * 16, 0u, 0u, 0u, 0u);
+      for (int q = 0; q < 4; ++q) st_shared_v4(stage_w + lane * 64 + q * 16, 0u, 0u, 0u, 0u);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         const uint64_t stream = l2_policy_evict_normal();
         const int nbf = (width + 31) / 32, nbr = (min(128, C - q_lo) + 31) / 32;
-        for (int k = cw; k < nbf * nbr; k += kPvThreads / 32 - 4)
-          tma_store_3d(&map_o, stage_z, f_lo + (k % nbf) * 32, q_lo + (k / nbf) * 32, b, stream);
+        const int me = warp < 2 ? warp : warp - 2;  // warps 0, 1, 4..7
+        for (int k = me; k < nbf * nbr; k += 6)
+          tma_store_3d(&map_o, stage_w, f_lo + (k % nbf) * 32, q_lo + (k / nbf) * 32, b, stream);
         bulk_commit_group();
         bulk_wait_read_all();
       }
-      (void)out;
     } else {
       griddep_wait();  // P, the partial sums and the sums of squares come from earlier launches
       const bool row_ok = i < C && pos_valid(args, b, i);
@@ -505,13 +509,13 @@ __global__ void __launch_bounds__(kPvThreads, 2)
                           (args.zl_rs & 7) == 0 && (args.zl_bs & 7) == 0;
       const uint64_t stream = l2_policy_evict_normal();
       const bool has_bias = args.has_bias;
-      // The one compute warpgroup drains every column of the group.
-      const int c_lo = 0, c_hi = width;
+      // This warp's half of the group's 32-column chunks.
+      const int nch = (width + 31) / 32, ch_mid = (nch + 1) / 2;
+      const int c_lo = half ? ch_mid * 32 : 0, c_hi = half ? width : min(width, ch_mid * 32);
       uint32_t gn[16];
       if (zrow && c_lo < c_hi) load_raw32<T>(zrow + f_lo + c_lo, D - f_lo - c_lo, zl_vec, gn, stream);
       mbar_wait(smem_u32(&ctrl->o_full), 0);
       tc_fence_after();
-      const uint32_t stage0 = staging + cw * kPvStageTiles * kTcOutTileBytes;
 #pragma unroll 1
       for (int c0 = c_lo, n = 0; c0 < c_hi; c0 += 32, ++n) {
         uint32_t o[32], gw[16];
@@ -519,9 +523,9 @@ __global__ void __launch_bounds__(kPvThreads, 2)
 #pragma unroll
         for (int q = 0; q < 16; ++q) gw[q] = gn[q];
         if (zrow && c0 + 32 < c_hi) load_raw32<T>(zrow + f_lo + c0 + 32, D - f_lo - c0 - 32, zl_vec, gn, stream);
-        tmem_wait_ld(o);
         float bv[32];
         load_bias32(&ctrl->bias[c0], has_bias, bv);
+        tmem_wait_ld(o);
         uint32_t pk[16];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -536,11 +540,12 @@ __global__ void __launch_bounds__(kPvThreads, 2)
           pk[2 * q] = pack2<T>(yv[0], yv[1]);
           pk[2 * q + 1] = pack2<T>(yv[2], yv[3]);
         }
-        if (lane == 0) bulk_wait_read_all();  // one staging tile per warp
+        // Two staging tiles: the store two chunks back must have read its tile.
+        if (lane == 0) bulk_wait_read_1();
         __syncwarp();
         if (q_lo + wq * 32 < C)
-          warp_tile_store(stage0, pk, &map_o, f_lo + c0, q_lo + wq * 32,
-                          b, stream, lane);
+          warp_tile_store(stage_w + (n & 1) * kTcOutTileBytes, pk, &map_o, f_lo + c0,
+                          q_lo + wq * 32, b, stream, lane);
       }
       if (lane == 0) bulk_wait_read_all();
     }
