@@ -180,8 +180,7 @@ LongLayout long_layout(const AveyFwdParams* p) {
   l.off_den = align256(static_cast<uint64_t>(B * C) * sizeof(float));
   l.off_p = l.off_den + align256(static_cast<uint64_t>(B * l.geom.n_groups * C) * sizeof(float));
   l.total = l.off_p + static_cast<uint64_t>(B * C * cp) * 2u;
-  l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes +
-              4 * avey::kLgWG * avey::kLgStageTiles * avey::kTcOutTileBytes + avey::kLgCtrlBytes;
+  l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes + avey::kLgCtrlBytes;
   l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes + avey::kPvCtrlBytes;
   return l;
 }

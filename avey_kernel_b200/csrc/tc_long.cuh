@@ -31,7 +31,6 @@ constexpr int kLgGroupKeys = 256;            // keys per tc_gram_p item (TMEM co
 constexpr int kLgGroupTiles = kLgGroupKeys / 128;
 constexpr int kLgStageBytes = (1 + kLgGroupTiles) * kTcTileBytesA;  // query + key tiles, one chunk
 constexpr int kLgStages = 2;
-constexpr int kLgStageTiles = 1;             // output staging tiles per compute warp
 constexpr int kLgCtrlBytes = 2048;
 constexpr int kLongMaxContext = 8192;
 
@@ -130,10 +129,8 @@ __global__ void __launch_bounds__(kLgThreads, 2)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw);
-  const uint32_t stage_addr = base;
-  const uint32_t staging = base + kLgStages * kLgStageBytes;
-  LgCtrl* ctrl = reinterpret_cast<LgCtrl*>(base_ptr + kLgStages * kLgStageBytes +
-                                           4 * kLgWG * kLgStageTiles * kTcOutTileBytes);
+  const uint32_t stage_addr = base;  // TMA stages; P staging tiles once the Gram is complete
+  LgCtrl* ctrl = reinterpret_cast<LgCtrl*>(base_ptr + kLgStages * kLgStageBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = args.ctx, D = args.feat;
@@ -288,8 +285,8 @@ __global__ void __launch_bounds__(kLgThreads, 2)
       const int i0 = q_lo + wq * 32;
       const bool norm = args.normalize;
       float den4[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t stage0 = staging + cw * kLgStageTiles * kTcOutTileBytes;
-      static_assert(kLgStageTiles == 1, "one staging tile per warp: stores wait for the previous read");
+      // The stage ring is idle once the Gram is complete: two staging tiles per warp.
+      const uint32_t stage0 = stage_addr + cw * 2 * kTcOutTileBytes;
 #pragma unroll 1
       for (int ch = 0; ch < nch; ++ch) {
         const int c0 = c_begin + ch * 32;
@@ -326,11 +323,12 @@ __global__ void __launch_bounds__(kLgThreads, 2)
             else p_chunk<T, false, false, false>(g, rk, rqi, vw, okb, pk, den4);
           }
         }
-        // The previous store from this warp's staging tile must have read it.
-        if (lane == 0) bulk_wait_read_all();
+        // The store two chunks back must have read its staging tile.
+        if (lane == 0) bulk_wait_read_1();
         __syncwarp();
         if (key0 + c0 < C && i0 < C)  // the box holds some of the tensor
-          warp_tile_store(stage0, pk, &map_pst, key0 + c0, i0, b, stream, lane);
+          warp_tile_store(stage0 + (ch & 1) * kTcOutTileBytes, pk, &map_pst, key0 + c0, i0, b,
+                          stream, lane);
         if (vrow) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
