@@ -27,7 +27,7 @@ EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_fwd_workspace_size', 'avey_fwd_
            'avey_last_error', 'avey_device_status', 'avey_launch_count', 'avey_abi_version')
 BWD_PREP, BWD_SCORES, BWD_EPILOGUE, BWD_DSCORES, BWD_FINAL = range(5)
 NOALLOC_MAX_ROWS = 1 << 20
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 class AveyFwdParams(ctypes.Structure):
@@ -60,6 +60,7 @@ class AveyFwdParams(ctypes.Structure):
         ('kernel', ctypes.c_int32),
         ('workspace', ctypes.c_void_p),
         ('workspace_bytes', ctypes.c_uint64),
+        ('lengths', ctypes.c_void_p),
     ]
 
 

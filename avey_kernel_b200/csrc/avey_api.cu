@@ -85,6 +85,8 @@ int validate(const AveyFwdParams* p) {
   if (p->z_tr_row_stride < p->features || p->out_row_stride < p->features ||
       (p->z_tl && p->z_tl_row_stride < p->features) || (p->v && p->v_row_stride < p->context))
     return fail(AVEY_ERR_ARGUMENT, "row strides must be at least the row length");
+  if (p->valid && p->lengths)
+    return fail(AVEY_ERR_ARGUMENT, "pass the mask as valid or as lengths, not both");
   if (p->z_tr_batch_stride < 0 || p->out_batch_stride < 0 || p->z_tl_batch_stride < 0 ||
       p->valid_batch_stride < 0 || p->valid_row_stride < 0)
     return fail(AVEY_ERR_ARGUMENT, "negative strides are not supported");
@@ -215,8 +217,9 @@ avey::FwdArgs make_args(const AveyFwdParams* p) {
   a.has_v = p->v != nullptr;
   a.has_zl = p->z_tl != nullptr;
   a.has_bias = p->bias != nullptr;
-  a.has_valid = p->valid != nullptr;
+  a.has_valid = p->valid != nullptr || p->lengths != nullptr;
   a.sumsq = static_cast<float*>(p->workspace);
+  a.lengths = p->lengths;
   return a;
 }
 

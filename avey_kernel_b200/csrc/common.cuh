@@ -25,9 +25,19 @@ struct FwdArgs {
   float eps_f, norm_eps_f;
   double eps_d, norm_eps_d;
   int causal, normalize, act;
-  int has_v, has_zl, has_bias, has_valid;
+  int has_v, has_zl, has_bias, has_valid;  // has_valid: a byte mask or prefix lengths
   float* sumsq;  // workspace: per-row sums of squares of z_tr [batch][ctx] (tcgen05 path)
+  const int32_t* lengths;  // [batch] prefix lengths (instead of valid), or null
 };
+
+// Position j of batch row b is valid (not padding): j < lengths[b] with the
+// prefix-length form of the mask, valid[b][j] != 0 with the byte mask, always
+// without either. Callers keep j < ctx.
+__device__ __forceinline__ bool mask_ok(const FwdArgs& a, int b, int j) {
+  if (a.lengths) return j < __ldg(a.lengths + b);
+  return !a.valid ||
+         a.valid[static_cast<int64_t>(b) * a.va_bs + static_cast<int64_t>(j) * a.va_rs] != 0;
+}
 
 template <typename T>
 struct Elem;

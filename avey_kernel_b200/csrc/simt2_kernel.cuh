@@ -73,14 +73,13 @@ __global__ void __launch_bounds__(kS2Threads, 2) simt2_contextualize(const FwdAr
   const int qt = args.causal ? nqt - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
   const int q0 = qt * kS2Rows;
   const T* zr = static_cast<const T*>(args.z_tr) + static_cast<int64_t>(b) * args.zr_bs;
-  const uint8_t* va = args.has_valid ? args.valid + static_cast<int64_t>(b) * args.va_bs : nullptr;
   const bool vec = std::is_same<T, float>::value &&
                    (reinterpret_cast<uintptr_t>(args.z_tr) & 15u) == 0 && (args.zr_rs & 3) == 0 &&
                    (args.zr_bs & 3) == 0;
 
   // Position j < C is a valid (non-padding) row.
   auto kv = [&](int j) -> bool {
-    if constexpr (LONG) return !va || va[static_cast<int64_t>(j) * args.va_rs] != 0;
+    if constexpr (LONG) return mask_ok(args, b, j);
     else return kv_s[j] != 0;
   };
   if (tid == 0) last_valid_s = -1;
@@ -88,7 +87,7 @@ __global__ void __launch_bounds__(kS2Threads, 2) simt2_contextualize(const FwdAr
   {
     int last = -1;
     for (int j = tid; j < C; j += kS2Threads) {
-      const uint8_t ok = (!va || va[static_cast<int64_t>(j) * args.va_rs] != 0) ? 1 : 0;
+      const uint8_t ok = mask_ok(args, b, j) ? 1 : 0;
       if constexpr (!LONG) kv_s[j] = ok;  // C <= 512 here (the host's choice)
       if (ok) last = j;
     }

@@ -41,7 +41,6 @@ __global__ void __launch_bounds__(kSimtFeat) simt_contextualize(const FwdArgs ar
       sizeof(A) == 8 ? static_cast<A>(args.norm_eps_d) : static_cast<A>(args.norm_eps_f);
 
   const T* zr = static_cast<const T*>(args.z_tr) + static_cast<int64_t>(b) * args.zr_bs;
-  const uint8_t* va = args.has_valid ? args.valid + static_cast<int64_t>(b) * args.va_bs : nullptr;
 
   __shared__ A q_s[kSimtRows][kSimtChunk + 1];
   __shared__ A k_s[kSimtKeys][kSimtChunk + 1];
@@ -56,19 +55,19 @@ __global__ void __launch_bounds__(kSimtFeat) simt_contextualize(const FwdArgs ar
   // Last valid position of this batch row: keys past it contribute nothing.
   if (tid == 0) last_valid_s = -1;
   __syncthreads();
-  if (va) {
+  if (args.has_valid) {
     int last = -1;
     for (int j = tid; j < C; j += kSimtFeat)
-      if (va[static_cast<int64_t>(j) * args.va_rs]) last = j;
+      if (mask_ok(args, b, j)) last = j;
     if (last >= 0) atomicMax(&last_valid_s, last);
   }
   if (tid < kSimtRows) {
     const int i = q0 + tid;
-    qvalid_s[tid] = (i < C) && (!va || va[static_cast<int64_t>(i) * args.va_rs]);
+    qvalid_s[tid] = (i < C) && mask_ok(args, b, i);
     den_s[tid] = A(0);
   }
   __syncthreads();
-  const int key_end0 = va ? last_valid_s + 1 : C;
+  const int key_end0 = args.has_valid ? last_valid_s + 1 : C;
   const int key_end = args.causal ? min(key_end0, min(C, q0 + kSimtRows)) : key_end0;
 
   // Inverse L2 norms of the query rows (invalid rows are masked anyway).
@@ -126,7 +125,7 @@ __global__ void __launch_bounds__(kSimtFeat) simt_contextualize(const FwdArgs ar
     }
     if (tid < kSimtKeys) {
       const int j = k0 + tid;
-      kvalid_s[tid] = (j < key_end) && (!va || va[static_cast<int64_t>(j) * args.va_rs]);
+      kvalid_s[tid] = (j < key_end) && mask_ok(args, b, j);
     }
     __syncthreads();
     // P = G * rinv_q * rinv_k * V, masked by select so NaN padding cannot leak.

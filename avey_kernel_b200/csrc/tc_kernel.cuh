@@ -281,7 +281,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 #endif
 
-  const uint8_t* va = args.has_valid ? args.valid + static_cast<int64_t>(b) * args.va_bs : nullptr;
 
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
@@ -319,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   {
     int last = -1;
     for (int j = tid; j < kTcMaxKeys; j += kTcThreads) {
-      const int ok = j < C && (!va || va[static_cast<int64_t>(j) * args.va_rs] != 0);
+      const int ok = j < C && mask_ok(args, b, j);
       ctrl->kvalid[j] = static_cast<uint8_t>(ok);
       if (ok) last = j;
     }

@@ -80,17 +80,14 @@ static_assert(sizeof(PvCtrl) <= kPvCtrlBytes, "control block too large");
 
 // Last valid position of batch row b (-1 if none), computed by the whole CTA.
 __device__ __forceinline__ void find_last_valid(const FwdArgs& args, int b, int* slot) {
-  const uint8_t* va = args.has_valid ? args.valid + static_cast<int64_t>(b) * args.va_bs : nullptr;
   int last = -1;
   for (int j = threadIdx.x; j < args.ctx; j += blockDim.x)
-    if (!va || va[static_cast<int64_t>(j) * args.va_rs] != 0) last = j;
+    if (mask_ok(args, b, j)) last = j;
   if (last >= 0) atomicMax(slot, last);
 }
 
 __device__ __forceinline__ bool pos_valid(const FwdArgs& args, int b, int j) {
-  if (j >= args.ctx) return false;
-  if (!args.has_valid) return true;
-  return args.valid[static_cast<int64_t>(b) * args.va_bs + static_cast<int64_t>(j) * args.va_rs] != 0;
+  return j < args.ctx && mask_ok(args, b, j);
 }
 
 // Key groups of query tile qt: keys [0, nkeys) in groups of 512.

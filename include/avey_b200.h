@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define AVEY_ABI_VERSION 3
+#define AVEY_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define AVEY_API __attribute__((visibility("default")))
@@ -104,6 +104,14 @@ typedef struct AveyFwdParams {
   int32_t kernel;     /* AveyKernel */
   void* workspace;          /* device scratch, >= avey_fwd_workspace_size() bytes */
   uint64_t workspace_bytes; /* size of `workspace` in bytes */
+
+  /* Prefix form of the padding mask, instead of `valid` (passing both is an
+   * error): a device array of B int32 lengths, positions [0, lengths[b]) of
+   * batch row b are valid and the rest is padding (values above the context
+   * act as the context, values below 1 leave the row all padding). No mask
+   * bytes are read. The reference takes only the byte mask (ops.py:28-51);
+   * this is the C-ABI fast path for callers that hold lengths. */
+  const int32_t* lengths;
 } AveyFwdParams;
 
 /* What avey_fwd_v1 would launch for these parameters. */

@@ -385,3 +385,37 @@ def test_fully_padded_query_tiles_overwrite_their_output_rows_with_zeros(n):
         ref = oracle.avey_b(to_numpy(tail[r:r + 1]), z_tl=to_numpy(head[r:r + 1]),
                             valid=ok[r:r + 1])
         assert norm_rel_err(y[r:r + 1], ref) <= TOL['bfloat16']
+
+
+@pytest.mark.parametrize('dtype,n,op', [(torch.bfloat16, 300, 'avey_b'), (torch.bfloat16, 300, 'avey'),
+                                        (torch.bfloat16, 640, 'avey_b'), (torch.float32, 200, 'avey'),
+                                        (torch.float64, 70, 'avey_b')],
+                         ids=['fused-b', 'fused-a', 'long-b', 'fp32-a', 'fp64-b'])
+def test_prefix_lengths_match_the_byte_mask(dtype, n, op):
+    # The C ABI's lengths form of the padding mask gives bitwise the output of
+    # the equivalent byte mask (lengths above the context act as the context,
+    # 0 leaves a row all padding).
+    g = torch.Generator(device='cpu').manual_seed(n)
+    b, d = 4, 64
+    x = torch.randn(b, n, 2 * d, generator=g).to(dtype).to(DEV)
+    head, tail = x[..., :d], x[..., d:]
+    w = (torch.randn(n, n, generator=g) * 0.05).to(dtype).to(DEV) if op == 'avey' else None
+    lengths = torch.tensor([n, n // 3, 0, n + 7], dtype=torch.int32, device=DEV)
+    valid = torch.arange(n, device=DEV)[None, :] < lengths[:, None].long()
+    outs = []
+    for form in ('valid', 'lengths'):
+        out = torch.empty(tail.shape, dtype=dtype, device=DEV)
+        params = ops.build_params(tail, w, head, None, valid if form == 'valid' else None, out,
+                                  eps=0.5, norm_eps=1e-12, causal=op == 'avey',
+                                  normalize=op == 'avey_b', activation_id=0)
+        if form == 'lengths':
+            params.lengths = lengths.data_ptr()
+        nbytes = _native.workspace_size(params)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=DEV)
+        params.workspace, params.workspace_bytes = ws.data_ptr(), nbytes
+        _native.forward(params, torch.cuda.current_stream().cuda_stream)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    y = to_numpy(outs[1])
+    assert (y[2] == 0).all() and np.isfinite(y).all()

@@ -22,7 +22,7 @@ def header_functions():
 
 def test_library_loads_and_reports_abi_version():
     dll = _native.lib()
-    assert dll.avey_abi_version() == _native.ABI_VERSION == 3
+    assert dll.avey_abi_version() == _native.ABI_VERSION == 4
 
 
 def test_every_header_function_is_exported():
@@ -141,7 +141,7 @@ def test_ctypes_struct_matches_header_field_order():
     names = [n for n in names if n not in ('AveyFwdParams',)]
     assert names == [f for f, _ in _native.AveyFwdParams._fields_]
     # The library rejects any other size (test_struct_size_guard); 200 bytes on LP64.
-    assert ctypes.sizeof(_native.AveyFwdParams) == 200
+    assert ctypes.sizeof(_native.AveyFwdParams) == 208
 
 
 def test_workspace_size_is_four_bytes_per_row_on_the_tcgen05_path():
@@ -206,3 +206,12 @@ def test_backward_steps_check_their_buffers_and_step_ids():
                         (_native.BWD_FINAL, 'final needs'), (9, 'unknown backward step')):
         with pytest.raises(_native.NativeError, match=match):
             _native.bwd_step(p, step, 0)
+
+
+def test_mask_as_valid_and_lengths_together_is_rejected():
+    p, _keep = _params()
+    valid = torch.ones(2, 64, dtype=torch.bool)
+    lengths = torch.full((2,), 64, dtype=torch.int32)
+    p.valid, p.lengths = valid.data_ptr(), lengths.data_ptr()
+    with pytest.raises(_native.NativeError, match='not both'):
+        _native.plan(p)
