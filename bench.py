@@ -533,6 +533,16 @@ def run_ours(args, cfg):
         cpu = {'value': cpu_value, 'unit': UNIT, 'cores': cpu_cores, 'kind': 'port',
                'sample': f'{cpu_steps} runs of 1 batch row ({cfg["n"]} tokens) of {args.config}, '
                          f'{cpu_busy:.1f} s, fp32 NumPy port of avey_kernels/ops.py::_reference'}
+        # The same port on one thread, for reference (a shorter sample).
+        try:
+            from threadpoolctl import threadpool_limits
+            with threadpool_limits(limits=1):
+                one_value, one_steps, one_busy = time_cpu_port(
+                    cfg, seconds=max(1.0, args.cpu_seconds / 4), rows=1)
+            cpu['single_thread'] = {'value': one_value, 'unit': UNIT, 'cores': 1,
+                                    'sample': f'{one_steps} runs, {one_busy:.1f} s'}
+        except Exception as exc:  # pragma: no cover - reported, not fatal
+            cpu['single_thread'] = {'error': repr(exc)[:200]}
 
     if rank == 0:
         line = {
