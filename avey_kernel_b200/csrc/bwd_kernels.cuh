@@ -48,7 +48,7 @@ struct BwdArgs {
   double eps, norm_eps;
   int causal, normalize, act;
   void* zm;     // [B, C, d]  GEMM type: Z (padded rows zeroed)
-  void* norms;  // [B, C]     acc: ||Z||
+  void* norms;  // [B, C]     acc: ||Z||, -1 on padded rows
   void* g;      // [B, C, C]  acc: Z Z^T
   void* s;      // [B, C, C]  GEMM type: S
   void* den;    // [B, C]     acc: rowsum(S) + eps
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_prep(const BwdArgs a) {
       }
     ss = warp_sum(ss);
     for (int f = lane; f < d; f += 32) st_as<G>(zm + r * d + f, ok ? ld_as<A>(zr + f) : A(0));
-    if (lane == 0) static_cast<A*>(a.norms)[r] = sqrt(ss);
+    if (lane == 0) static_cast<A*>(a.norms)[r] = ok ? sqrt(ss) : A(-1);  // -1 marks padding
   }
 }
 
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_prep_v8(const BwdArgs a) {
       st8<G>(zm + r * a.feat + 8 * v, x);
     }
     ss = warp_sum(ss);
-    if (lane == 0) static_cast<float*>(a.norms)[r] = sqrtf(ss);
+    if (lane == 0) static_cast<float*>(a.norms)[r] = ok ? sqrtf(ss) : -1.f;  // -1 marks padding
   }
 }
 
@@ -543,7 +543,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_scores_v8(const BwdArgs a) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int j = j0 + e;
-        const bool allowed = (!a.causal || j <= i) && row_valid(a, b, j);
+        const bool allowed = (!a.causal || j <= i) && nk[e] >= 0.f;  // padding has norm -1
         float y = x[e] * ri * (1.f / fmaxf(nk[e], ne));
         if (v) y *= vv[e];
         x[e] = allowed ? y : 0.f;
@@ -695,8 +695,8 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
   for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
        r += nwarps) {
     const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
-    const bool ok = row_valid(a, b, n);
     const float norm = static_cast<const float*>(a.norms)[r];
+    const bool ok = norm >= 0.f;  // padding has norm -1
     const bool scaled = norm >= ne;
     const float rinv = 1.f / (scaled ? norm : ne);
     float dot = 0.f;
@@ -781,7 +781,7 @@ __device__ __forceinline__ void ds_compute(const BwdArgs& a, const DsIn& x, int 
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     rk[e] = in ? 1.f / fmaxf(ns[e], ne) : 0.f;
-    const bool ok = in && (!a.causal || j + e <= i) && row_valid(a, b, j + e);
+    const bool ok = in && (!a.causal || j + e <= i) && ns[e] >= 0.f;  // padding has norm -1
     const float dsm = ok ? xs[e] + x.dd : 0.f;
     acc[e] = fmaf(dsm, gs[e] * rq * rk[e], acc[e]);
     dg[e] = dsm * v[e];

@@ -183,7 +183,7 @@ AVEY_API int avey_fwd_noalloc_v1(const AveyFwdParams* params, void* stream);
  * five batched GEMMs, which the caller runs with a library GEMM, and five
  * fused steps that run here between them:
  *
- *   AVEY_BWD_PREP      zm = z_tr (padded rows 0), norms = ||zm||
+ *   AVEY_BWD_PREP      zm = z_tr (padded rows 0), norms = ||zm|| (-1: padding)
  *                                                          then  g = zm zm^T
  *   AVEY_BWD_SCORES    s = g r_i r_j (.) v (.) mask, den = rowsum(s) + eps,
  *                      r = 1 / max(norms, norm_eps)        then  num = s zm
@@ -233,7 +233,7 @@ typedef struct AveyBwdParams {
 
   /* Scratch written by one step and read by later ones or by the GEMMs. */
   void* zm;        /* [B, C, d'] gemm_dtype */
-  void* norms;     /* [B, C]     acc */
+  void* norms;     /* [B, C]     acc: ||zm||, -1 on padded positions */
   void* g;         /* [B, C, C]  acc (GEMM output) */
   void* s;         /* [B, C, C]  gemm_dtype */
   void* den;       /* [B, C]     acc */
