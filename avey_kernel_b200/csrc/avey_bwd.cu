@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 #include <type_traits>
 
 #include "avey_b200.h"
@@ -233,7 +234,19 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
       bool vdone = false;
       if constexpr (kHasVec) {
         if (vec) {
-          avey::bwd_dscores_v4<T, G><<<dim3(pairs, groups), kT, 0, st>>>(a, per);
+          // The cp.async operand ring: 2 tiles x kDsStages batch rows (84 KB).
+          constexpr int kRing = 2 * avey::kDsStages * static_cast<int>(sizeof(avey::DsStage));
+          int dev = 0;
+          cudaGetDevice(&dev);
+          static std::once_flag once[64];
+          static cudaError_t attr_err[64];
+          std::call_once(once[dev & 63], [&] {
+            attr_err[dev & 63] = cudaFuncSetAttribute(
+                avey::bwd_dscores_v4<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRing);
+          });
+          if (attr_err[dev & 63] != cudaSuccess)
+            return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute(bwd_dscores_v4) failed");
+          avey::bwd_dscores_v4<T, G><<<dim3(pairs, groups), kT, kRing, st>>>(a, per);
           vdone = true;
         }
       }

@@ -788,6 +788,62 @@ __device__ __forceinline__ void ds_compute(const BwdArgs& a, const DsIn& x, int 
   }
 }
 
+// cp.async copies of 16 / 4 bytes from global to shared memory (completion
+// tracked per thread by commit / wait groups).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// One batch row's operands of one dscores tile, field by field so that the
+// threads' 16-byte slots are contiguous (conflict-free float4 reads).
+struct DsStage {
+  float4 ds[kBwdThreads];
+  float4 g[kBwdThreads];
+  float4 nk[kBwdThreads];
+  float nq[kBwdThreads];
+  float dd[kBwdThreads];
+};
+constexpr int kDsStages = 3;
+
+// Issue the copies of this thread's operands of tile row i, columns j..j+3.
+__device__ __forceinline__ void ds_issue(const BwdArgs& a, DsStage& st, int64_t base, int64_t rb,
+                                         int i, int j, bool in, bool want_g) {
+  const int t = threadIdx.x;
+  if (!in) return;
+  const int64_t off = base + static_cast<int64_t>(i) * a.ctx + j;
+  cp_async16(&st.ds[t], static_cast<const float*>(a.ds0) + off);
+  if (want_g) cp_async16(&st.g[t], static_cast<const float*>(a.g) + off);
+  cp_async16(&st.nk[t], static_cast<const float*>(a.norms) + rb + j);
+  cp_async4(&st.nq[t], static_cast<const float*>(a.norms) + rb + i);
+  if (a.normalize) cp_async4(&st.dd[t], static_cast<const float*>(a.dden) + rb + i);
+}
+
+__device__ __forceinline__ DsIn ds_read(const BwdArgs& a, const DsStage& st, bool in, bool want_g) {
+  const int t = threadIdx.x;
+  DsIn x;
+  x.ds = x.g = x.nk = make_float4(0.f, 0.f, 0.f, 0.f);
+  x.nq = 1.f;
+  x.dd = 0.f;
+  if (in) {
+    x.ds = st.ds[t];
+    if (want_g) x.g = st.g[t];
+    x.nk = st.nk[t];
+    x.nq = st.nq[t];
+    if (a.normalize) x.dd = st.dd[t];
+  }
+  return x;
+}
+
 template <typename T, typename G>
 __global__ void __launch_bounds__(kBwdThreads) bwd_dscores_v4(const BwdArgs a, int bpg) {
   __shared__ float tr[2][kBwdTile][kBwdTile + 1];
@@ -818,21 +874,43 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dscores_v4(const BwdArgs a, i
     v1[e] = (v && in1) ? ld_as<float>(v + static_cast<int64_t>(i1) * a.v_rs + j1 + e) : 1.f;
     v2[e] = (v && in2) ? ld_as<float>(v + static_cast<int64_t>(i2) * a.v_rs + j2 + e) : 1.f;
   }
-  DsIn n1, n2;
-  if (b0 < b1) {
-    n1 = ds_load(a, static_cast<int64_t>(b0) * C * C, static_cast<int64_t>(b0) * C, i1, j1, in1, want_g);
-    n2 = ds_load(a, static_cast<int64_t>(b0) * C * C, static_cast<int64_t>(b0) * C, i2, j2, in2, want_g);
+  // Operands stream through a kDsStages-deep shared-memory ring filled with
+  // cp.async: each thread copies and later reads only its own slots, so the
+  // ring needs no block barrier, and the loads of later batch rows are in
+  // flight while this one is computed.
+  extern __shared__ __align__(16) uint8_t ds_smem[];
+  DsStage* ring1 = reinterpret_cast<DsStage*>(ds_smem);
+  DsStage* ring2 = ring1 + kDsStages;
+  const int nb = b1 - b0;
+#pragma unroll
+  for (int k = 0; k < kDsStages - 1; ++k) {
+    if (k < nb) {
+      const int bb = b0 + k;
+      ds_issue(a, ring1[k], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C, i1, j1,
+               in1, want_g);
+      ds_issue(a, ring2[k], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C, i2, j2,
+               in2, want_g);
+    }
+    cp_async_commit();
   }
   int buf = 0;
-  for (int b = b0; b < b1; ++b, buf ^= 1) {
+  for (int it = 0; it < nb; ++it, buf ^= 1) {
+    const int b = b0 + it;
     const int64_t base = static_cast<int64_t>(b) * C * C;
-    const DsIn x1 = n1, x2 = n2;
-    if (b + 1 < b1) {  // the next batch row's operands, in flight during this one
-      n1 = ds_load(a, base + static_cast<int64_t>(C) * C, static_cast<int64_t>(b + 1) * C, i1, j1,
-                   in1, want_g);
-      n2 = ds_load(a, base + static_cast<int64_t>(C) * C, static_cast<int64_t>(b + 1) * C, i2, j2,
-                   in2, want_g);
+    {
+      const int ahead = it + kDsStages - 1;
+      if (ahead < nb) {
+        const int bb = b0 + ahead, slot = ahead % kDsStages;
+        ds_issue(a, ring1[slot], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C,
+                 i1, j1, in1, want_g);
+        ds_issue(a, ring2[slot], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C,
+                 i2, j2, in2, want_g);
+      }
+      cp_async_commit();
     }
+    cp_async_wait<kDsStages - 1>();  // this batch row's group has landed
+    const DsIn x1 = ds_read(a, ring1[it % kDsStages], in1, want_g);
+    const DsIn x2 = ds_read(a, ring2[it % kDsStages], in2, want_g);
     float dg1[4], r1[4], dg2[4], r2[4];
     ds_compute(a, x1, b, i1, j1, in1, v1, acc1, dg1, r1);
     if (!diag) {
