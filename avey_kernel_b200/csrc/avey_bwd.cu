@@ -168,6 +168,27 @@ int row_grid(const AveyBwdParams* p) {
   return static_cast<int>(std::min<int64_t>((warps + 7) / 8, 148 * 16));
 }
 
+// Feature slots (256 features each) per epilogue pass: three when that takes
+// fewer passes over the rows than two (d' = 768: one pass instead of two),
+// else two (d' = 384 would leave most of a third slot idle).
+int epi_slots(const AveyBwdParams* p) {
+  const int64_t nv = p->features / 8;
+  const int64_t p2 = (nv + 63) / 64, p3 = (nv + 95) / 96;
+  return p3 < p2 ? 3 : 2;
+}
+
+template <typename T, typename G, int S>
+void launch_epilogue_v8(int activation, unsigned grid, cudaStream_t st, const avey::BwdArgs& a) {
+  constexpr int kT = avey::kBwdThreads;
+  switch (activation) {
+    case 1: avey::bwd_epilogue_v8<T, G, 1, S><<<grid, kT, 0, st>>>(a); break;
+    case 2: avey::bwd_epilogue_v8<T, G, 2, S><<<grid, kT, 0, st>>>(a); break;
+    case 3: avey::bwd_epilogue_v8<T, G, 3, S><<<grid, kT, 0, st>>>(a); break;
+    case 4: avey::bwd_epilogue_v8<T, G, 4, S><<<grid, kT, 0, st>>>(a); break;
+    default: avey::bwd_epilogue_v8<T, G, 0, S><<<grid, kT, 0, st>>>(a); break;
+  }
+}
+
 template <typename T, typename G, typename A>
 int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
   const avey::BwdArgs a = make_args(p);
@@ -204,14 +225,10 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
       bool done = false;
       if constexpr (kHasVec) {
         if (vec) {
-          const unsigned grid = static_cast<unsigned>(nb);
-          switch (p->activation) {
-            case 1: avey::bwd_epilogue_v8<T, G, 1><<<grid, kT, 0, st>>>(a); break;
-            case 2: avey::bwd_epilogue_v8<T, G, 2><<<grid, kT, 0, st>>>(a); break;
-            case 3: avey::bwd_epilogue_v8<T, G, 3><<<grid, kT, 0, st>>>(a); break;
-            case 4: avey::bwd_epilogue_v8<T, G, 4><<<grid, kT, 0, st>>>(a); break;
-            default: avey::bwd_epilogue_v8<T, G, 0><<<grid, kT, 0, st>>>(a); break;
-          }
+          if (epi_slots(p) == 3)
+            launch_epilogue_v8<T, G, 3>(p->activation, static_cast<unsigned>(nb), st, a);
+          else
+            launch_epilogue_v8<T, G, 2>(p->activation, static_cast<unsigned>(nb), st, a);
           done = true;
         }
       }

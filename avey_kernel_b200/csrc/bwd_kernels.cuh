@@ -563,11 +563,12 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_scores_v8(const BwdArgs a) {
 }
 
 // Step 3, vector form: a warp takes kBwdEpiRowsV8 rows, a lane 8 consecutive
-// features of up to 2 slots (512 features) per pass, keeping its dbias
+// features of up to S slots (256 S features) per pass, keeping its dbias
 // partial sums in registers across the rows; the block sums its 8 warps in
-// order. The activation is a template parameter. dden is accumulated in place
-// (one warp owns a row) and finished after the last pass.
-constexpr int kBwdEpiSlots = 2;
+// order. The activation and S (2 or 3, the host picks the fewest passes) are
+// template parameters. dden is accumulated in place (one warp owns a row) and
+// finished after the last pass.
+constexpr int kBwdEpiMaxSlots = 3;
 constexpr int kBwdEpiRowsV8 = 32;  // rows per block (4 per warp)
 
 template <int ACT>
@@ -591,9 +592,10 @@ __device__ __forceinline__ float act_grad_fn(float x) {
 // Three blocks per SM (at most 85 registers a thread): each warp has one row's
 // loads in flight at a time, so the kernel needs the warps to cover HBM latency
 // (96 registers and two blocks per SM measured ~9 us slower on config 2).
-template <typename T, typename G, int ACT>
+template <typename T, typename G, int ACT, int S>
 __global__ void __launch_bounds__(kBwdThreads, 3) bwd_epilogue_v8(const BwdArgs a) {
-  __shared__ float red[kBwdThreads / 32][kBwdEpiSlots * 256];
+  static_assert(S >= 1 && S <= kBwdEpiMaxSlots, "feature slots per pass");
+  __shared__ float red[kBwdThreads / 32][S * 256];
   constexpr int kRows = kBwdEpiRowsV8 / (kBwdThreads / 32);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
@@ -607,10 +609,10 @@ __global__ void __launch_bounds__(kBwdThreads, 3) bwd_epilogue_v8(const BwdArgs 
   const T* __restrict__ go = static_cast<const T*>(a.gout);
   G* __restrict__ dnum = static_cast<G*>(a.dnum);
   T* __restrict__ gzl = static_cast<T*>(a.gz_tl);
-  for (int w0 = 0; w0 < nv; w0 += 32 * kBwdEpiSlots) {
-    float db[kBwdEpiSlots][8];
+  for (int w0 = 0; w0 < nv; w0 += 32 * S) {
+    float db[S][8];
 #pragma unroll
-    for (int q = 0; q < kBwdEpiSlots; ++q)
+    for (int q = 0; q < S; ++q)
 #pragma unroll
       for (int e = 0; e < 8; ++e) db[q][e] = 0.f;
 #pragma unroll 1
@@ -626,7 +628,7 @@ __global__ void __launch_bounds__(kBwdThreads, 3) bwd_epilogue_v8(const BwdArgs 
                         : nullptr;
       float dsum = 0.f;
 #pragma unroll
-      for (int q = 0; q < kBwdEpiSlots; ++q) {
+      for (int q = 0; q < S; ++q) {
         const int v = w0 + 32 * q + lane;
         if (v >= nv) break;
         const int f0 = 8 * v;
@@ -667,11 +669,11 @@ __global__ void __launch_bounds__(kBwdThreads, 3) bwd_epilogue_v8(const BwdArgs 
       if (lane == 0) dden[r] = (w0 == 0 ? 0.f : dden[r]) + dsum;
     }
 #pragma unroll
-    for (int q = 0; q < kBwdEpiSlots; ++q)
+    for (int q = 0; q < S; ++q)
 #pragma unroll
       for (int e = 0; e < 8; ++e) red[warp][(32 * q + lane) * 8 + e] = db[q][e];
     __syncthreads();
-    for (int t = threadIdx.x; t < kBwdEpiSlots * 256; t += kBwdThreads) {
+    for (int t = threadIdx.x; t < S * 256; t += kBwdThreads) {
       const int f = 8 * w0 + t;
       if (f < d) {
         float acc = 0.f;

@@ -116,7 +116,9 @@ def test_nan_padding_cannot_contaminate_gradients():
 
 
 @pytest.mark.parametrize('op,b,n,d', [('avey', 2, 256, 192), ('avey_b', 3, 384, 128),
-                                      ('avey', 1, 640, 96)])
+                                      ('avey', 1, 640, 96),
+                                      # three feature slots per epilogue pass: one pass, two passes
+                                      ('avey', 1, 256, 520), ('avey_b', 2, 128, 1040)])
 def test_tensor_core_sizes_bf16(op, b, n, d):
     g = torch.Generator().manual_seed(n)
     x = torch.randn(b, n, 2 * d, generator=g).to(torch.bfloat16)
@@ -177,12 +179,13 @@ def test_custom_ops_pass_opcheck():
                            [True, True, True, False]))
 
 
+@pytest.mark.parametrize('d', [48, 520])  # two and three feature slots per epilogue pass
 @pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16, torch.float16])
-def test_vector_and_scalar_steps_agree(dtype):
+def test_vector_and_scalar_steps_agree(dtype, d):
     # The same values once in 16-byte aligned rows (vector steps) and once
     # shifted by one element (scalar steps).
     g = torch.Generator().manual_seed(9)
-    b, n, d = 2, 64, 48
+    b, n = 2, 64
     base = torch.randn(b, n, 2 * d + 1, generator=g).to(dtype).to(DEV)
     w = (torch.randn(n, n, generator=g) * 0.1).to(dtype).to(DEV)
     go = torch.randn(b, n, d, generator=g).to(dtype).to(DEV)
