@@ -271,8 +271,16 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
       int n = 1;
       if (a.gv) {
         const int64_t cc = p->context * p->context;
-        avey::bwd_reduce<T, A><<<static_cast<unsigned>((cc + 31) / 32), reduce_threads(groups), 0, st>>>(
-            static_cast<const A*>(p->workspace), groups, cc, static_cast<T*>(p->grad_v));
+        const A* part = static_cast<const A*>(p->workspace);
+        if (groups <= 32) {
+          constexpr int kRt = avey::kBwdReduceColThreads;
+          const int64_t blocks = std::min<int64_t>((cc + kRt - 1) / kRt, 148 * 8);
+          avey::bwd_reduce_cols<T, A><<<static_cast<unsigned>(blocks), kRt, 0, st>>>(
+              part, groups, cc, static_cast<T*>(p->grad_v));
+        } else {
+          avey::bwd_reduce<T, A><<<static_cast<unsigned>((cc + 31) / 32), reduce_threads(groups), 0, st>>>(
+              part, groups, cc, static_cast<T*>(p->grad_v));
+        }
         ++n;
       }
       return launched(n);

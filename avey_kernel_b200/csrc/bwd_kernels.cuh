@@ -978,14 +978,48 @@ __global__ void __launch_bounds__(kBwdReduceThreads) bwd_reduce(const A* part, i
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int64_t k = static_cast<int64_t>(blockIdx.x) * 32 + lane;
   A t = 0;
-  if (k < n)
-    for (int p = warp; p < nparts; p += nw) t += part[static_cast<int64_t>(p) * n + k];
+  if (k < n) {
+    int p = warp;
+    for (; p + 3 * nw < nparts; p += 4 * nw) {  // four loads in flight, added in order
+      A v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = part[static_cast<int64_t>(p + u * nw) * n + k];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) t += v[u];
+    }
+    for (; p < nparts; p += nw) t += part[static_cast<int64_t>(p) * n + k];
+  }
   red[warp][lane] = t;
   __syncthreads();
   if (warp == 0 && k < n) {
     A s = 0;
     for (int w = 0; w < nw; ++w) s += red[w][lane];
     st_as<T>(out + k, s);
+  }
+}
+
+// The same sums for many columns of at most 32 parts (dV: C x C columns, one
+// part per batch group): one thread per column adds the parts in order, eight
+// loads in flight. For nparts <= 32 bwd_reduce adds in the same order (one part
+// per warp, warps combined in order), so the two forms give the same bits.
+constexpr int kBwdReduceColThreads = 256;
+template <typename T, typename A>
+__global__ void __launch_bounds__(kBwdReduceColThreads) bwd_reduce_cols(const A* part, int nparts,
+                                                                        int64_t n, T* out) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kBwdReduceColThreads;
+  for (int64_t k = static_cast<int64_t>(blockIdx.x) * kBwdReduceColThreads + threadIdx.x; k < n;
+       k += stride) {
+    A t = 0;
+    int p = 0;
+    for (; p + 8 <= nparts; p += 8) {
+      A v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = part[static_cast<int64_t>(p + u) * n + k];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t += v[u];
+    }
+    for (; p < nparts; ++p) t += part[static_cast<int64_t>(p) * n + k];
+    st_as<T>(out + k, t);
   }
 }
 
