@@ -251,7 +251,7 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
       bool vdone = false;
       if constexpr (kHasVec) {
         if (vec) {
-          // The cp.async operand ring: 2 tiles x kDsStages batch rows (84 KB).
+          // The cp.async operand ring: 2 tiles x kDsStages batch rows (48 KB).
           constexpr int kRing = 2 * avey::kDsStages * static_cast<int>(sizeof(avey::DsStage));
           int dev = 0;
           cudaGetDevice(&dev);

@@ -762,23 +762,6 @@ struct DsIn {
   float nq, dd;      // norm of the row's query, its dden
 };
 
-__device__ __forceinline__ DsIn ds_load(const BwdArgs& a, int64_t base, int64_t rb, int i, int j,
-                                        bool in, bool want_g) {
-  DsIn x;
-  x.ds = x.g = x.nk = make_float4(0.f, 0.f, 0.f, 0.f);
-  x.nq = 1.f;
-  x.dd = 0.f;
-  if (in) {
-    const int64_t off = base + static_cast<int64_t>(i) * a.ctx + j;
-    x.ds = *reinterpret_cast<const float4*>(static_cast<const float*>(a.ds0) + off);
-    if (want_g) x.g = *reinterpret_cast<const float4*>(static_cast<const float*>(a.g) + off);
-    x.nk = *reinterpret_cast<const float4*>(static_cast<const float*>(a.norms) + rb + j);
-    x.nq = static_cast<const float*>(a.norms)[rb + i];
-    if (a.normalize) x.dd = static_cast<const float*>(a.dden)[rb + i];
-  }
-  return x;
-}
-
 // dG of 4 columns (j .. j+3) of query row i, the dV partial sums, and r of
 // the 4 keys.
 __device__ __forceinline__ void ds_compute(const BwdArgs& a, const DsIn& x, int b, int i, int j,
@@ -815,48 +798,61 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// One batch row's operands of one dscores tile, field by field so that the
-// threads' 16-byte slots are contiguous (conflict-free float4 reads).
+// One batch row's two large operands of one dscores tile (ds0 and Gr, 4 KB
+// each), field by field so that the threads' 16-byte slots are contiguous
+// (conflict-free float4 reads). The small per-row operands (key norms, query
+// norm, dden) go through registers, loaded one batch row ahead.
 struct DsStage {
   float4 ds[kBwdThreads];
   float4 g[kBwdThreads];
-  float4 nk[kBwdThreads];
-  float nq[kBwdThreads];
-  float dd[kBwdThreads];
 };
 constexpr int kDsStages = 3;
 
+struct DsSmall {
+  float4 nk;      // norms of the 4 keys
+  float nq, dd;   // norm of the query, its dden
+};
+
+__device__ __forceinline__ DsSmall ds_small(const BwdArgs& a, int64_t rb, int i, int j, bool in) {
+  DsSmall x;
+  x.nk = make_float4(0.f, 0.f, 0.f, 0.f);
+  x.nq = 1.f;
+  x.dd = 0.f;
+  if (in) {
+    const float* nrm = static_cast<const float*>(a.norms);
+    x.nk = __ldg(reinterpret_cast<const float4*>(nrm + rb + j));
+    x.nq = __ldg(nrm + rb + i);
+    if (a.normalize) x.dd = __ldg(static_cast<const float*>(a.dden) + rb + i);
+  }
+  return x;
+}
+
 // Issue the copies of this thread's operands of tile row i, columns j..j+3.
-__device__ __forceinline__ void ds_issue(const BwdArgs& a, DsStage& st, int64_t base, int64_t rb,
-                                         int i, int j, bool in, bool want_g) {
+__device__ __forceinline__ void ds_issue(const BwdArgs& a, DsStage& st, int64_t base, int i, int j,
+                                         bool in, bool want_g) {
   const int t = threadIdx.x;
   if (!in) return;
   const int64_t off = base + static_cast<int64_t>(i) * a.ctx + j;
   cp_async16(&st.ds[t], static_cast<const float*>(a.ds0) + off);
   if (want_g) cp_async16(&st.g[t], static_cast<const float*>(a.g) + off);
-  cp_async16(&st.nk[t], static_cast<const float*>(a.norms) + rb + j);
-  cp_async4(&st.nq[t], static_cast<const float*>(a.norms) + rb + i);
-  if (a.normalize) cp_async4(&st.dd[t], static_cast<const float*>(a.dden) + rb + i);
 }
 
-__device__ __forceinline__ DsIn ds_read(const BwdArgs& a, const DsStage& st, bool in, bool want_g) {
+__device__ __forceinline__ DsIn ds_read(const DsStage& st, const DsSmall& sm, bool in, bool want_g) {
   const int t = threadIdx.x;
   DsIn x;
-  x.ds = x.g = x.nk = make_float4(0.f, 0.f, 0.f, 0.f);
-  x.nq = 1.f;
-  x.dd = 0.f;
+  x.ds = x.g = make_float4(0.f, 0.f, 0.f, 0.f);
+  x.nk = sm.nk;
+  x.nq = sm.nq;
+  x.dd = sm.dd;
   if (in) {
     x.ds = st.ds[t];
     if (want_g) x.g = st.g[t];
-    x.nk = st.nk[t];
-    x.nq = st.nq[t];
-    if (a.normalize) x.dd = st.dd[t];
   }
   return x;
 }
 
 template <typename T, typename G>
-__global__ void __launch_bounds__(kBwdThreads) bwd_dscores_v4(const BwdArgs a, int bpg) {
+__global__ void __launch_bounds__(kBwdThreads, 3) bwd_dscores_v4(const BwdArgs a, int bpg) {
   __shared__ float tr[2][kBwdTile][kBwdTile + 1];
   __shared__ float ts[2][kBwdTile][kBwdTile + 1];
   const int row = threadIdx.x >> 3, c4 = (threadIdx.x & 7) * 4;
@@ -896,14 +892,14 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dscores_v4(const BwdArgs a, i
 #pragma unroll
   for (int k = 0; k < kDsStages - 1; ++k) {
     if (k < nb) {
-      const int bb = b0 + k;
-      ds_issue(a, ring1[k], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C, i1, j1,
-               in1, want_g);
-      ds_issue(a, ring2[k], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C, i2, j2,
-               in2, want_g);
+      const int64_t base = static_cast<int64_t>(b0 + k) * C * C;
+      ds_issue(a, ring1[k], base, i1, j1, in1, want_g);
+      ds_issue(a, ring2[k], base, i2, j2, in2, want_g);
     }
     cp_async_commit();
   }
+  DsSmall s1 = ds_small(a, static_cast<int64_t>(b0) * C, i1, j1, in1 && nb > 0);
+  DsSmall s2 = ds_small(a, static_cast<int64_t>(b0) * C, i2, j2, in2 && nb > 0);
   int buf = 0;
   for (int it = 0; it < nb; ++it, buf ^= 1) {
     const int b = b0 + it;
@@ -911,17 +907,21 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dscores_v4(const BwdArgs a, i
     {
       const int ahead = it + kDsStages - 1;
       if (ahead < nb) {
-        const int bb = b0 + ahead, slot = ahead % kDsStages;
-        ds_issue(a, ring1[slot], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C,
-                 i1, j1, in1, want_g);
-        ds_issue(a, ring2[slot], static_cast<int64_t>(bb) * C * C, static_cast<int64_t>(bb) * C,
-                 i2, j2, in2, want_g);
+        const int64_t abase = static_cast<int64_t>(b0 + ahead) * C * C;
+        ds_issue(a, ring1[ahead % kDsStages], abase, i1, j1, in1, want_g);
+        ds_issue(a, ring2[ahead % kDsStages], abase, i2, j2, in2, want_g);
       }
       cp_async_commit();
     }
+    // The next batch row's small operands, in flight while this row is computed.
+    const bool more = it + 1 < nb;
+    const DsSmall n1 = ds_small(a, static_cast<int64_t>(b + 1) * C, i1, j1, in1 && more);
+    const DsSmall n2 = ds_small(a, static_cast<int64_t>(b + 1) * C, i2, j2, in2 && more);
     cp_async_wait<kDsStages - 1>();  // this batch row's group has landed
-    const DsIn x1 = ds_read(a, ring1[it % kDsStages], in1, want_g);
-    const DsIn x2 = ds_read(a, ring2[it % kDsStages], in2, want_g);
+    const DsIn x1 = ds_read(ring1[it % kDsStages], s1, in1, want_g);
+    const DsIn x2 = ds_read(ring2[it % kDsStages], s2, in2, want_g);
+    s1 = n1;
+    s2 = n2;
     float dg1[4], r1[4], dg2[4], r2[4];
     ds_compute(a, x1, b, i1, j1, in1, v1, acc1, dg1, r1);
     if (!diag) {
