@@ -980,12 +980,12 @@ __global__ void __launch_bounds__(kBwdReduceThreads) bwd_reduce(const A* part, i
   A t = 0;
   if (k < n) {
     int p = warp;
-    for (; p + 3 * nw < nparts; p += 4 * nw) {  // four loads in flight, added in order
-      A v[4];
+    for (; p + 7 * nw < nparts; p += 8 * nw) {  // eight loads in flight, added in order
+      A v[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = part[static_cast<int64_t>(p + u * nw) * n + k];
+      for (int u = 0; u < 8; ++u) v[u] = part[static_cast<int64_t>(p + u * nw) * n + k];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) t += v[u];
+      for (int u = 0; u < 8; ++u) t += v[u];
     }
     for (; p < nparts; p += nw) t += part[static_cast<int64_t>(p) * n + k];
   }
