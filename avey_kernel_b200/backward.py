@@ -100,8 +100,13 @@ def contextualize_backward_impl(z_tr, v, z_tl, bias, valid, grad_out, eps, norm_
 
     stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
-        zm, norms = empty(B, C, d, dtype=gdt), empty(B, C, dtype=acc)
-        p.zm, p.norms = zm.data_ptr(), norms.data_ptr()
+        norms = empty(B, C, dtype=acc)
+        if valid is None and gdt == dt:
+            zm = z_tr  # nothing to zero: the GEMMs read z_tr in place (strided)
+        else:
+            zm = empty(B, C, d, dtype=gdt)
+            p.zm = zm.data_ptr()
+        p.norms = norms.data_ptr()
         _native.bwd_step(p, _native.BWD_PREP, stream)
         g = _bmm(zm, zm.transpose(1, 2), acc)
         s, den = empty(B, C, C, dtype=gdt), empty(B, C, dtype=acc)

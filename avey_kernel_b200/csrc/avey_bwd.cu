@@ -168,6 +168,10 @@ int row_grid(const AveyBwdParams* p) {
   return static_cast<int>(std::min<int64_t>((warps + 7) / 8, 148 * 16));
 }
 
+// zm equals z_tr when nothing is padded and the GEMM type is the input type;
+// the caller may then pass no zm and give z_tr (strided) to the GEMMs.
+bool zm_optional(const AveyBwdParams* p) { return !p->valid && p->gemm_dtype == p->dtype; }
+
 // Feature slots (256 features each) per epilogue pass: three when that takes
 // fewer passes over the rows than two (d' = 768: one pass instead of two),
 // else two (d' = 384 would leave most of a third slot idle).
@@ -197,7 +201,9 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
   const bool vec = kHasVec && vec_ok(p);
   switch (step) {
     case AVEY_BWD_PREP:
-      if (!p->zm || !p->norms) return fail(AVEY_ERR_ARGUMENT, "prep needs zm, norms");
+      if (!p->norms) return fail(AVEY_ERR_ARGUMENT, "prep needs norms");
+      if (!p->zm && !zm_optional(p))
+        return fail(AVEY_ERR_ARGUMENT, "zm may be NULL only without valid and with gemm_dtype == dtype");
       if constexpr (kHasVec) {
         if (vec) {
           avey::bwd_prep_v8<T, G><<<row_grid(p), kT, 0, st>>>(a);
@@ -286,8 +292,10 @@ int run_step(const AveyBwdParams* p, int step, cudaStream_t st) {
       return launched(n);
     }
     case AVEY_BWD_FINAL:
-      if (!p->zm || !p->norms || !p->dzh || !p->dzd || !p->grad_z_tr)
-        return fail(AVEY_ERR_ARGUMENT, "final needs zm, norms, dzh, dzd, grad_z_tr");
+      if (!p->norms || !p->dzh || !p->dzd || !p->grad_z_tr)
+        return fail(AVEY_ERR_ARGUMENT, "final needs norms, dzh, dzd, grad_z_tr");
+      if (!p->zm && !zm_optional(p))
+        return fail(AVEY_ERR_ARGUMENT, "zm may be NULL only without valid and with gemm_dtype == dtype");
       if constexpr (kHasVec) {
         if (vec) {
           avey::bwd_final_v8<T, G><<<row_grid(p), kT, 0, st>>>(a);

@@ -102,6 +102,16 @@ __device__ __forceinline__ bool row_valid(const BwdArgs& a, int b, int n) {
   return !a.valid || a.valid[static_cast<int64_t>(b) * a.va_bs + static_cast<int64_t>(n) * a.va_rs] != 0;
 }
 
+// Row (b, n) = flat row r of zm. A caller without a padding mask whose GEMM
+// type is the input type may pass no zm (it equals z_tr then): the row is
+// read from z_tr through its strides.
+template <typename G>
+__device__ __forceinline__ const G* zm_row(const BwdArgs& a, int64_t r, int b, int n) {
+  if (a.zm) return static_cast<const G*>(a.zm) + r * a.feat;
+  return static_cast<const G*>(a.z_tr) + static_cast<int64_t>(b) * a.zr_bs +
+         static_cast<int64_t>(n) * a.zr_rs;
+}
+
 template <typename A>
 __device__ __forceinline__ A warp_sum(A x) {
 #pragma unroll
@@ -156,7 +166,8 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_prep(const BwdArgs a) {
         ss += x * x;
       }
     ss = warp_sum(ss);
-    for (int f = lane; f < d; f += 32) st_as<G>(zm + r * d + f, ok ? ld_as<A>(zr + f) : A(0));
+    if (zm)
+      for (int f = lane; f < d; f += 32) st_as<G>(zm + r * d + f, ok ? ld_as<A>(zr + f) : A(0));
     if (lane == 0) static_cast<A*>(a.norms)[r] = ok ? sqrt(ss) : A(-1);  // -1 marks padding
   }
 }
@@ -393,13 +404,13 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final(const BwdArgs a) {
   const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
   const int d = a.feat;
-  const G* zm = static_cast<const G*>(a.zm);
   const A* dzh = static_cast<const A*>(a.dzh);
   const A* dzd = static_cast<const A*>(a.dzd);
   T* gz = static_cast<T*>(a.gz_tr);
   for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
        r += nwarps) {
     const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
+    const G* zr = zm_row<G>(a, r, b, n);
     const bool ok = row_valid(a, b, n);
     const A norm = static_cast<const A*>(a.norms)[r];
     const A ne = static_cast<A>(a.norm_eps);
@@ -407,12 +418,12 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final(const BwdArgs a) {
     const A rinv = A(1) / (scaled ? norm : ne);
     A dot = 0;
     if (ok && scaled)
-      for (int f = lane; f < d; f += 32) dot += ld_as<A>(zm + r * d + f) * rinv * dzh[r * d + f];
+      for (int f = lane; f < d; f += 32) dot += ld_as<A>(zr + f) * rinv * dzh[r * d + f];
     dot = warp_sum(dot);
     for (int f = lane; f < d; f += 32) {
       A g = 0;
       if (ok) {
-        const A zhat = ld_as<A>(zm + r * d + f) * rinv;
+        const A zhat = ld_as<A>(zr + f) * rinv;
         g = (dzh[r * d + f] - (scaled ? zhat * dot : A(0))) * rinv + dzd[r * d + f];
       }
       st_as<T>(gz + grad_off(a, b, n) + f, g);
@@ -510,7 +521,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_prep_v8(const BwdArgs a) {
       }
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
-      st8<G>(zm + r * a.feat + 8 * v, x);
+      if (zm) st8<G>(zm + r * a.feat + 8 * v, x);
     }
     ss = warp_sum(ss);
     if (lane == 0) static_cast<float*>(a.norms)[r] = ok ? sqrtf(ss) : -1.f;  // -1 marks padding
@@ -698,7 +709,6 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
   const int64_t rows = static_cast<int64_t>(a.batch) * a.ctx;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kBwdThreads / 32);
   const int d = a.feat, nv = d / 8;
-  const G* __restrict__ zm = static_cast<const G*>(a.zm);
   const float* __restrict__ dzh = static_cast<const float*>(a.dzh);
   const float* __restrict__ dzd = static_cast<const float*>(a.dzd);
   T* __restrict__ gz = static_cast<T*>(a.gz_tr);
@@ -706,6 +716,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
   for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kBwdThreads + threadIdx.x) >> 5; r < rows;
        r += nwarps) {
     const int b = static_cast<int>(r / a.ctx), n = static_cast<int>(r % a.ctx);
+    const G* __restrict__ zr = zm_row<G>(a, r, b, n);
     const float norm = static_cast<const float*>(a.norms)[r];
     const bool ok = norm >= 0.f;  // padding has norm -1
     const bool scaled = norm >= ne;
@@ -714,7 +725,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
     if (ok && scaled)
       for (int v = lane; v < nv; v += 32) {
         float z[8], h[8];
-        ld8<G>(zm + r * d + 8 * v, z);
+        ld8<G>(zr + 8 * v, z);
         ld8<float>(dzh + r * d + 8 * v, h);
 #pragma unroll
         for (int e = 0; e < 8; ++e) dot = fmaf(z[e] * rinv, h[e], dot);
@@ -724,7 +735,7 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_final_v8(const BwdArgs a) {
       float o[8];
       if (ok) {
         float z[8], h[8], dd[8];
-        ld8<G>(zm + r * d + 8 * v, z);
+        ld8<G>(zr + 8 * v, z);
         ld8<float>(dzh + r * d + 8 * v, h);
         ld8<float>(dzd + r * d + 8 * v, dd);
 #pragma unroll

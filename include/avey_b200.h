@@ -232,7 +232,10 @@ typedef struct AveyBwdParams {
   int64_t grad_out_batch_stride, grad_out_row_stride;
 
   /* Scratch written by one step and read by later ones or by the GEMMs. */
-  void* zm;        /* [B, C, d'] gemm_dtype */
+  void* zm;        /* [B, C, d'] gemm_dtype; may be NULL when valid is NULL and
+                      gemm_dtype == dtype (zm would equal z_tr): PREP then writes
+                      only the norms, FINAL reads z_tr, and the caller's GEMMs
+                      take z_tr (strided) in place of zm */
   void* norms;     /* [B, C]     acc: ||zm||, -1 on padded positions */
   void* g;         /* [B, C, C]  acc (GEMM output) */
   void* s;         /* [B, C, C]  gemm_dtype */

@@ -208,6 +208,21 @@ def test_backward_steps_check_their_buffers_and_step_ids():
             _native.bwd_step(p, step, 0)
 
 
+@pytest.mark.parametrize('step', [_native.BWD_PREP, _native.BWD_FINAL])
+def test_backward_omits_zm_only_without_padding_and_with_the_input_gemm_type(step):
+    # zm may be NULL (the steps then read z_tr) only when it would equal z_tr.
+    for dtype, gemm, padded in ((_native.AVEY_BF16, _native.AVEY_BF16, True),
+                                (_native.AVEY_F16, _native.AVEY_F32, False)):
+        p = _bwd_params(dtype=dtype, gemm=gemm)
+        p.norms, p.dzh, p.dzd, p.grad_z_tr = 0x3000, 0x4000, 0x5000, 0x6000
+        if padded:
+            p.valid, p.valid_batch_stride, p.valid_row_stride = 0x7000, 64, 1
+        before = _native.launch_count()
+        with pytest.raises(_native.NativeError, match='zm may be NULL only'):
+            _native.bwd_step(p, step, 0)
+        assert _native.launch_count() == before
+
+
 def test_mask_as_valid_and_lengths_together_is_rejected():
     p, _keep = _params()
     valid = torch.ones(2, 64, dtype=torch.bool)
