@@ -1,8 +1,8 @@
 """Backward of the contextualizer on the GPU, and its autograd registration.
 
 The reference differentiates only through its PyTorch path
-(avey_kernels/ops.py:99-111 route inputs that require grad to _reference,
-ops.py:66-96). Here ``avey_b200::contextualize`` (the native forward) gets a
+(avey_kernels/ops.py:94-106 route inputs that require grad to _reference,
+ops.py:61-91). Here ``avey_b200::contextualize`` (the native forward) gets a
 native backward: five library GEMMs (``torch.bmm``, i.e. cuBLAS) with the
 fused elementwise / reduction steps of ``csrc/bwd_kernels.cuh`` between them,
 called through the C ABI (``avey_bwd_step_v1``):

@@ -22,10 +22,10 @@
 // that streams its operands once; reductions (dbias, dV, dden) use fixed
 // orders, so gradients are bitwise reproducible.
 //
-// Reference: torch autograd through avey_kernels/ops.py:66-96 (_reference):
-// masked_fill before the arithmetic (ops.py:69-72), F.normalize (73), the
-// masks (74-82), numerator / denominator (83-85), bias (86-87), activation
-// (ops.py:54-63), gate and final row mask (89-94).
+// Reference: torch autograd through avey_kernels/ops.py:61-91 (_reference):
+// masked_fill before the arithmetic (ops.py:64-67), F.normalize (68), the
+// masks (69-77), numerator / denominator (78-80), bias (81-82), activation
+// (ops.py:49-58), gate and final row mask (84-90).
 #pragma once
 
 #include <type_traits>
@@ -119,7 +119,7 @@ __device__ __forceinline__ A warp_sum(A x) {
   return x;
 }
 
-// Derivative of the activations of the reference (ops.py:54-63) at x, with
+// Derivative of the activations of the reference (ops.py:49-58) at x, with
 // torch's conventions: relu' = [x > 0]; relu2' = 2 max(x, 0); silu' =
 // s (1 + x (1 - s)); tanh-gelu' = 0.5 (1 + t) + 0.5 x (1 - t^2) k (1 + 3 c x^2),
 // t = tanh(k (x + c x^3)), k = sqrt(2 / pi), c = 0.044715.

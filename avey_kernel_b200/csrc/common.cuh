@@ -85,7 +85,7 @@ __device__ __forceinline__ double sigmoid_stable(double x) {
   return x >= 0.0 ? 1.0 / (1.0 + e) : e / (1.0 + e);
 }
 
-// Activations of the reference (ops.py:54-63); ids as in _triton.py:169.
+// Activations of the reference (ops.py:49-58); ids as in _triton.py:169.
 // relu keeps NaN (x < 0 is false for NaN), as torch.relu does.
 template <typename A>
 __device__ __forceinline__ A activate(A x, int act) {

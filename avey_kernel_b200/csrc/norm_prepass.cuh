@@ -4,8 +4,8 @@
 // kernel that follows start at once (programmatic dependent launch); that
 // kernel waits for these sums only before its P phase.
 //
-// Reference: the row L2 norm inside F.normalize (avey_kernels/ops.py:73 and
-// :113); only the sum of squares is produced here, the division by
+// Reference: the row L2 norm inside F.normalize (avey_kernels/ops.py:68 and
+// :108); only the sum of squares is produced here, the division by
 // max(sqrt(.), norm_eps) is applied to the Gram tile in the fused kernel.
 #pragma once
 

@@ -13,9 +13,9 @@
 //   phase 2  O = P Z in passes of 256 output features: 8 x 4 register tiles,
 //            Z streamed in chunks of 32 keys; then the epilogue (divide,
 //            bias, activation, gate, row mask).
-// Rows that are padding are zeroed as they are loaded (ops.py:69-72), so a
+// Rows that are padding are zeroed as they are loaded (ops.py:64-67), so a
 // NaN in them cannot reach any product. Arithmetic is fp32 like the
-// reference's (ops.py:68); S is computed once per query tile instead of once
+// reference's (ops.py:63); S is computed once per query tile instead of once
 // per output-feature tile as in simt_contextualize and the reference's Triton
 // kernel (_triton.py:78-105).
 #pragma once

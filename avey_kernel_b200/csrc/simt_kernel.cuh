@@ -8,7 +8,7 @@
 // feature chunks staged in shared memory, scaled by both inverse row norms, V
 // and the masks into P, and then P Z_k is accumulated into registers (one
 // output feature per thread, 16 rows). Arithmetic is in A (fp32, or fp64 for
-// fp64 inputs), like the reference's fp32 accumulation (ops.py:68).
+// fp64 inputs), like the reference's fp32 accumulation (ops.py:63).
 #pragma once
 
 #include "common.cuh"

@@ -37,7 +37,7 @@
 // Reference: the fused loop of avey_kernels/_triton.py:53-128 (S tile 83-92,
 // V 93-96, masks 97-100, row sum 101-102, S.Z 103-105, divide 106-107, bias
 // 108-110, activation 111-121, gate 122-125, masked store 126-128), plus the
-// normalisation pre-pass it relies on (ops.py:112-113), fused here.
+// normalisation pre-pass it relies on (ops.py:107-108), fused here.
 #pragma once
 
 #include <cuda.h>

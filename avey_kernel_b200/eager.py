@@ -1,11 +1,11 @@
 """Differentiable PyTorch path (``backend='torch'``).
 
 This is the path the reference takes for autograd and CPU tensors
-(avey_kernels/ops.py:99-111): plain tensor ops with fp32 accumulation (fp64
+(avey_kernels/ops.py:94-106): plain tensor ops with fp32 accumulation (fp64
 kept for gradcheck). It is not the inference hot path -- CUDA inference inputs
 go to the native kernels -- and it is not the test oracle (``oracle/``).
 
-Math per ops.py:66-96: padded rows are replaced by zeros before any
+Math per ops.py:61-91: padded rows are replaced by zeros before any
 arithmetic (so NaN padding cannot reach values or gradients), rows are
 L2-normalised with ``x / max(||x||, norm_eps)``, S = N N^T is weighted by V,
 masked (causal keeps the diagonal; padded keys zero whole columns), mixed into

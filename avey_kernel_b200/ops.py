@@ -1,12 +1,12 @@
 """Public operations: drop-in for ``avey_kernels.ops`` (``avey``, ``avey_b``).
 
 Same signatures, tensor conventions and errors as the reference
-(avey_kernels/ops.py:28-152). Backends:
+(avey_kernels/ops.py:23-147). Backends:
 
 * ``'cuda'``  the native sm_100a kernels through the C ABI (``libavey_b200.so``)
   for CUDA tensors, otherwise ``ValueError``. Inputs that require grad get the
   native backward (``backward.py``); the reference has none and sends them to
-  its PyTorch path (ops.py:99-111).
+  its PyTorch path (ops.py:94-106).
 * ``'triton'`` accepted for source compatibility: it names the fused GPU
   kernel, which here is the native CUDA one (same rules as ``'cuda'``).
 * ``'torch'`` the differentiable PyTorch path (``eager.py``).
@@ -38,7 +38,7 @@ _DTYPE_IDS = {torch.float32: _native.AVEY_F32, torch.float16: _native.AVEY_F16,
 
 def _validate(z_tr, v, z_tl, bias, valid, eps, norm_eps, activation, backend, output_tile,
               autotune):
-    """Input contract of the reference (ops.py:28-51); violations raise ValueError."""
+    """Input contract of the reference (ops.py:23-46); violations raise ValueError."""
     if not isinstance(z_tr, torch.Tensor) or z_tr.ndim != 3 or 0 in z_tr.shape:
         raise ValueError('z_tr must have nonempty shape [batch, context, features]')
     if z_tr.dtype not in _DTYPE_IDS:
@@ -126,7 +126,7 @@ def contextualize(z_tr: torch.Tensor, v: Optional[torch.Tensor], z_tl: Optional[
                   variant: int = 0) -> torch.Tensor:
     """Native contextualizer forward: one launch of the sm_100a library on the
     current stream. Replaces the reference's ``avey_kernels::mix`` custom op
-    (_triton.py:153-188) plus its normalisation pre-pass (ops.py:112-113).
+    (_triton.py:153-188) plus its normalisation pre-pass (ops.py:107-108).
     ``variant`` selects the kernel (0 auto, 1 CUDA-core, 2 tcgen05)."""
     if not z_tr.is_cuda:
         raise ValueError('avey_b200::contextualize needs CUDA tensors')
@@ -258,7 +258,7 @@ def avey(z_tr: torch.Tensor, v: torch.Tensor, *, z_tl=None, bias=None, valid=Non
     Causal masking keeps the diagonal. ``valid`` masks both query and key
     positions; invalid output rows are zero, including after bias and gating.
     ``bias`` has shape [features]; ``z_tl``, if present, has the shape of z_tr.
-    Mirrors avey_kernels/ops.py:122-138.
+    Mirrors avey_kernels/ops.py:117-133.
     """
     if v is None:
         raise ValueError('Avey requires the learned V matrix (v)')
@@ -272,7 +272,7 @@ def avey_b(z_tr: torch.Tensor, *, z_tl=None, bias=None, valid=None, eps=1e-6, no
 
     S is the cosine similarity with invalid keys zeroed; signed similarities are
     kept and the denominator is neither clamped nor a softmax. GELU uses the
-    tanh approximation. Mirrors avey_kernels/ops.py:141-152.
+    tanh approximation. Mirrors avey_kernels/ops.py:136-147.
     """
     return _dispatch(z_tr, None, z_tl, bias, valid, eps, norm_eps, False, True, activation,
                      backend, output_tile, autotune)

@@ -7,7 +7,7 @@
  *
  * with S_b the cosine similarity of the rows of z_tr[b], M_b the causal and
  * padding mask and den_b the signed row sum (Avey-B) or 1 (Avey): the math of
- * the reference's avey_kernels/ops.py:66-96 (_reference).
+ * the reference's avey_kernels/ops.py:61-91 (_reference).
  *
  * The library is plain C at this boundary: raw device pointers, element
  * strides and sizes, no framework types. It never throws; every entry point
@@ -109,7 +109,7 @@ typedef struct AveyFwdParams {
    * error): a device array of B int32 lengths, positions [0, lengths[b]) of
    * batch row b are valid and the rest is padding (values above the context
    * act as the context, values below 1 leave the row all padding). No mask
-   * bytes are read. The reference takes only the byte mask (ops.py:28-51);
+   * bytes are read. The reference takes only the byte mask (ops.py:23-46);
    * this is the C-ABI fast path for callers that hold lengths. */
   const int32_t* lengths;
 } AveyFwdParams;
@@ -129,7 +129,7 @@ typedef struct AveyPlan {
 /*
  * Run the contextualizer forward on `stream` (a cudaStream_t; NULL is the
  * legacy default stream). Replaces, in the reference, the normalisation
- * pre-pass plus the fused mixing launch: avey_kernels/ops.py:112-119
+ * pre-pass plus the fused mixing launch: avey_kernels/ops.py:107-114
  * (F.normalize into a temporary fp32 buffer, then mix) and
  * avey_kernels/_triton.py:153-188 (the avey_kernels::mix custom op that
  * launches _mix_kernel). Normalisation is fused into the kernel here.
@@ -147,7 +147,7 @@ AVEY_API int avey_fwd_plan(const AveyFwdParams* params, AveyPlan* plan);
  * row sums, 4 bytes per row per group of 256 keys (partial row sums) and P
  * itself (2 bytes per (query, key) pair, rows padded to 64 keys): 134 MB for
  * batch 16 x 2048 tokens. The workspace must be 256-byte aligned. The
- * reference allocates its normalisation buffer itself (ops.py:113); this
+ * reference allocates its normalisation buffer itself (ops.py:108); this
  * library leaves allocation to the caller. Launches nothing. */
 AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* bytes);
 
@@ -178,8 +178,8 @@ AVEY_API int avey_fwd_noalloc_v1(const AveyFwdParams* params, void* stream);
 
 /*
  * Backward pass. The reference has no fused backward: autograd runs through
- * its PyTorch path (avey_kernels/ops.py:99-111 send any input that requires
- * grad to _reference, ops.py:66-96). This library splits the gradient into
+ * its PyTorch path (avey_kernels/ops.py:94-106 send any input that requires
+ * grad to _reference, ops.py:61-91). This library splits the gradient into
  * five batched GEMMs, which the caller runs with a library GEMM, and five
  * fused steps that run here between them:
  *

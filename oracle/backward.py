@@ -4,25 +4,25 @@ TEST INFRASTRUCTURE ONLY, like ``contextualizer.py``: the checker for the
 native backward (``avey_kernel_b200/backward.py``), never called by it.
 
 The reference has no hand-written backward: its gradients are torch autograd
-through ``avey_kernels/ops.py::_reference`` (ops.py:66-96; the reference's
+through ``avey_kernels/ops.py::_reference`` (ops.py:61-91; the reference's
 tests/test_contextualizer.py:41-62 gradcheck it and check NaN padding). This
 module restates that chain rule in NumPy, step by step against the forward
 lines it differentiates:
 
-* ops.py:94-96   rows of padded queries get no gradient (masked_fill).
-* ops.py:89-93   d gate = dout * act(Ypre); dA = dout * gate (padded rows 0).
-* ops.py:86-88   dYpre = dA * act'(Ypre) with torch's derivative conventions
+* ops.py:89-91   rows of padded queries get no gradient (masked_fill).
+* ops.py:84-88   d gate = dout * act(Ypre); dA = dout * gate (padded rows 0).
+* ops.py:81-83   dYpre = dA * act'(Ypre) with torch's derivative conventions
                  (relu' = [x > 0], relu2' = 2 max(x, 0), silu' = s (1 + x (1 - s)),
                  tanh-gelu' = 0.5 (1 + t) + 0.5 x (1 - t^2) k (1 + 3 c x^2));
                  d bias = sum over rows of dYpre.
-* ops.py:84-85   Avey-B: dnum = dYpre / den, dden_i = -sum_f dYpre_if Y0_if / den_i.
-* ops.py:83      dS = dnum Z^T (+ dden along the row), dZ += S^T dnum.
-* ops.py:74-82   masked entries of S pass no gradient; dV = sum_b dS (.) G,
+* ops.py:79-80   Avey-B: dnum = dYpre / den, dden_i = -sum_f dYpre_if Y0_if / den_i.
+* ops.py:78      dS = dnum Z^T (+ dden along the row), dZ += S^T dnum.
+* ops.py:69-77   masked entries of S pass no gradient; dV = sum_b dS (.) G,
                  dG = dS (.) V, dZhat = (dG + dG^T) Zhat.
-* ops.py:73      F.normalize: dZ += (dZhat - Zhat (Zhat . dZhat)) / ||Z|| where
+* ops.py:68      F.normalize: dZ += (dZhat - Zhat (Zhat . dZhat)) / ||Z|| where
                  ||Z|| >= norm_eps, dZhat / norm_eps below (clamp_min passes no
                  gradient to the norm there).
-* ops.py:69-72   padded rows of z_tr get no gradient (masked_fill before use).
+* ops.py:64-67   padded rows of z_tr get no gradient (masked_fill before use).
 
 Pinned by ``tests/test_oracle_backward.py`` against gradients of the reference
 itself (``tests/golden/make_grad_golden.py``) and against finite differences.

@@ -10,26 +10,26 @@ It restates, in NumPy, the reference implementation
 ``avey_kernels/ops.py::_reference`` (HusamettinYilmazz/avey_kernel), step by
 step; the line numbers below are those of that file:
 
-* ops.py:68      accumulate in fp32 (fp64 kept for fp64 input).  The oracle
+* ops.py:63      accumulate in fp32 (fp64 kept for fp64 input).  The oracle
                  accumulates in ``accum`` (fp64 by default: a tighter truth
                  than the reference's own fp32 arithmetic).
-* ops.py:69-72   zero invalid rows *before* any arithmetic (NaN padding).
-* ops.py:73      ``F.normalize(x, p=2, dim=-1, eps)`` = x / max(||x||, eps).
-* ops.py:74      cosine similarity S = N N^T.
-* ops.py:75-76   S *= V (Avey only), V indexed [query, key].
-* ops.py:77-80   causal mask keeps j <= i (the diagonal is kept).
-* ops.py:81-82   invalid keys zero whole columns of S.
-* ops.py:83      numerator = S @ z_tr (the *un-normalised* tail).
-* ops.py:84-85   Avey-B: divide by the signed row sum plus eps.
-* ops.py:86-88   + bias, then the activation (ops.py:54-63).
-* ops.py:89-93   multiply by the gate z_tl with invalid rows zeroed.
-* ops.py:94-96   zero invalid output rows; cast back to the input dtype
+* ops.py:64-67   zero invalid rows *before* any arithmetic (NaN padding).
+* ops.py:68      ``F.normalize(x, p=2, dim=-1, eps)`` = x / max(||x||, eps).
+* ops.py:69      cosine similarity S = N N^T.
+* ops.py:70-71   S *= V (Avey only), V indexed [query, key].
+* ops.py:72-75   causal mask keeps j <= i (the diagonal is kept).
+* ops.py:76-77   invalid keys zero whole columns of S.
+* ops.py:78      numerator = S @ z_tr (the *un-normalised* tail).
+* ops.py:79-80   Avey-B: divide by the signed row sum plus eps.
+* ops.py:81-83   + bias, then the activation (ops.py:49-58).
+* ops.py:84-88   multiply by the gate z_tl with invalid rows zeroed.
+* ops.py:89-91   zero invalid output rows; cast back to the input dtype
                  (the caller does the cast: the oracle returns ``accum``).
 
 Parity pin: ``tests/test_oracle.py`` checks this oracle against the
 hand-computed fixtures of the reference's own tests
 (tests/test_contextualizer.py:13-39, tests/test_profiling.py:46-61,
-tests/test_triton.py:251-258) and against golden vectors produced by running
+tests/test_triton.py:162-169) and against golden vectors produced by running
 the reference's ``_reference`` (``tests/golden/make_golden.py``).
 """
 
@@ -43,7 +43,7 @@ ACTIVATIONS = ('identity', 'relu', 'relu2', 'silu', 'gelu')
 
 
 def activate(x: np.ndarray, activation: str) -> np.ndarray:
-    """ops.py:54-63: identity, relu, relu^2, silu and tanh-approximate gelu."""
+    """ops.py:49-58: identity, relu, relu^2, silu and tanh-approximate gelu."""
     if activation == 'identity':
         return x
     if activation == 'relu':
@@ -109,7 +109,7 @@ def contextualize(z_tr, v=None, z_tl=None, bias=None, valid=None, *,
 
 def avey(z_tr, v, *, z_tl=None, bias=None, valid=None, causal=True,
          norm_eps=1e-12, activation='identity', accum=np.float64):
-    """ops.py:122-138: Avey (learned V, eps fixed at 1e-6, no row-sum divide)."""
+    """ops.py:117-133: Avey (learned V, eps fixed at 1e-6, no row-sum divide)."""
     if v is None:
         raise ValueError('Avey requires the learned V matrix (v)')
     return contextualize(z_tr, v, z_tl, bias, valid, eps=1e-6, norm_eps=norm_eps,
@@ -119,7 +119,7 @@ def avey(z_tr, v, *, z_tl=None, bias=None, valid=None, causal=True,
 
 def avey_b(z_tr, *, z_tl=None, bias=None, valid=None, eps=1e-6, norm_eps=1e-12,
            activation='identity', accum=np.float64):
-    """ops.py:141-152: Avey-B (no V, bidirectional, signed row-sum divide)."""
+    """ops.py:136-147: Avey-B (no V, bidirectional, signed row-sum divide)."""
     return contextualize(z_tr, None, z_tl, bias, valid, eps=eps, norm_eps=norm_eps,
                          causal=False, normalize=True, activation=activation,
                          accum=accum)

@@ -9,10 +9,10 @@ regenerate the fixtures, never to run the tests.
 
 Case families follow the reference's own tests:
 
-* ``tiled_*``     tests/test_triton.py:215-249  (tails, zero row, NaN padding,
+* ``tiled_*``     tests/test_triton.py:126-160  (tails, zero row, NaN padding,
                   every activation, eps 0.25 for signed Avey-B inputs)
-* ``lowprec_*``   tests/test_triton.py:186-213  (fp16/bf16 inputs, fp32 math)
-* ``tiles_*``     tests/test_triton.py:159-184  (35x133 tails, gate, bias, mask)
+* ``lowprec_*``   tests/test_triton.py:97-124  (fp16/bf16 inputs, fp32 math)
+* ``tiles_*``     tests/test_triton.py:70-95  (35x133 tails, gate, bias, mask)
 * ``skip_*``      tests/test_causal_skip.py:80-105 (causal, NaN rows, silu)
 * ``cfg1``        BASELINE config 1 (B=2, N=256, head/tail 128, fp32, seed 0)
 * ``mini_*``      scaled-down bf16 versions of BASELINE configs 2-4
@@ -44,7 +44,7 @@ def _case(name, op, z_tr, *, v=None, z_tl=None, bias=None, valid=None, causal=Tr
 
 def build_cases():
     cases = []
-    # tests/test_triton.py:215-249 -- fp32, randn, tails, NaN padding, all activations.
+    # tests/test_triton.py:126-160 -- fp32, randn, tails, NaN padding, all activations.
     torch.manual_seed(17)
     for c, d in ((1, 1), (5, 7), (35, 37), (67, 65)):
         z_tr = torch.randn(2, c, d)
@@ -67,14 +67,14 @@ def build_cases():
             else:
                 cases.append(_case(name, 'avey', z_tr, v=v, z_tl=z_tl, bias=bias, valid=valid,
                                    causal=causal, activation=act))
-    # tests/test_triton.py:186-213 -- low-precision inputs, no gate/bias/mask.
+    # tests/test_triton.py:97-124 -- low-precision inputs, no gate/bias/mask.
     torch.manual_seed(9)
     for dt in ('float16', 'bfloat16'):
         z_tr = torch.rand(2, 35, 37, dtype=DTYPES[dt])
         v = torch.randn(35, 35, dtype=DTYPES[dt])
         cases.append(_case(f'lowprec_{dt}_a', 'avey', z_tr, v=v))
         cases.append(_case(f'lowprec_{dt}_b', 'avey_b', z_tr))
-    # tests/test_triton.py:159-184 -- 35 x 133 tails with gate, bias and mask.
+    # tests/test_triton.py:70-95 -- 35 x 133 tails with gate, bias and mask.
     torch.manual_seed(29)
     for dt in ('float32', 'float16', 'bfloat16'):
         z_tr = torch.rand(2, 35, 133, dtype=DTYPES[dt])

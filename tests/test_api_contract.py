@@ -1,7 +1,7 @@
 """The drop-in API: signatures, validation errors, the differentiable PyTorch
 path, and custom-op tracing without a GPU (mirrors the reference's
 tests/test_contextualizer.py, tests/test_symbolic_tile.py and
-tests/test_autotune.py:25-42)."""
+tests/test_autotune.py:25-45)."""
 
 import subprocess
 import sys

@@ -64,13 +64,13 @@ def test_zero_rows_and_padding_do_not_leak_bias():
 
 
 def test_signed_denominator_not_softmax_or_abs():
-    # reference tests/test_contextualizer.py:36-39 and tests/test_triton.py:251-258
+    # reference tests/test_contextualizer.py:36-39 and tests/test_triton.py:162-169
     z = np.array([[[1., 0.], [-2., 0.]]])
     np.testing.assert_allclose(oracle.avey_b(z, eps=0.5), [[[6., 0.], [-6., 0.]]], **TOL)
 
 
 def test_full_call_values():
-    # reference tests/test_profiling.py:151-166
+    # reference tests/test_profiling.py:46-61
     z = np.array([[[1., 0.], [3., 0.]]])
     v = np.array([[2., 1.], [4., 3.]])
     gate = np.array([[[2., 3.], [4., 5.]]])
