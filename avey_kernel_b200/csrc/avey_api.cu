@@ -139,12 +139,9 @@ TcLayout tc_layout(const AveyFwdParams* p) {
   int nslot = room / avey::kTcUnitBytes;
   if (nslot > avey::kTcMaxSlots) nslot = avey::kTcMaxSlots;
   l.geom.nslot = nslot;
-  // Phase-A stages use the space of the phase-C ring.
-  l.geom.a_stage_bytes = nk_max * avey::kTcTileBytesA;
-  int nst = (nslot * avey::kTcUnitBytes) / l.geom.a_stage_bytes;
-  if (nst > avey::kTcMaxStages) nst = avey::kTcMaxStages;
-  l.geom.a_nstage = nst;
   l.geom.n_qtiles = nk_max;
+  // V tiles by TMA need a 16-byte aligned base and rows of multiples of 8 elements.
+  l.geom.v_tma = p->v && aligned16(p->v) && (p->v_row_stride % 8 == 0);
   l.smem = 1024 + nslot * avey::kTcUnitBytes + avey::kTcOutStageBytes + avey::kTcCtrlBytes;
   return l;
 }
@@ -367,7 +364,8 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
   });
   if (attr_err != cudaSuccess)
     return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
-  CUtensorMap map_q, map_z, map_o;
+  CUtensorMap map_q, map_z, map_o, map_v;
+  std::memset(&map_v, 0, sizeof(map_v));
   int rc = encode_map(p, p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride, avey::kTcChunk, 128,
                       &map_q);
   if (rc != AVEY_OK) return rc;
@@ -377,6 +375,14 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
   rc = encode_map(p, p->out, p->out_batch_stride, p->out_row_stride, 32, 32, &map_o);
   if (rc != AVEY_OK) return rc;
   const TcLayout l = tc_layout(p);
+  if (l.geom.v_tma) {
+    // V [query, key] as a 2-D map (one "batch"): {64 keys, 128 query rows} boxes.
+    rc = encode_map_dims(p->dtype, p->v, static_cast<uint64_t>(p->context),
+                         static_cast<uint64_t>(p->context), 1,
+                         static_cast<uint64_t>(p->v_row_stride) * elem_size(p->dtype), 0, 64, 128,
+                         &map_v);
+    if (rc != AVEY_OK) return rc;
+  }
   const avey::FwdArgs args = make_args(p);
   const uint64_t need = static_cast<uint64_t>(p->batch) * p->context * sizeof(float);
   if (!p->workspace || p->workspace_bytes < need || (reinterpret_cast<uintptr_t>(p->workspace) & 3u))
@@ -401,7 +407,7 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, avey::tc_contextualize<T, ACT>, args, map_q, map_z, map_o, l.geom);
+  e = cudaLaunchKernelEx(&cfg, avey::tc_contextualize<T, ACT>, args, map_q, map_z, map_o, map_v, l.geom);
   if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tcgen05 kernel launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return ok();

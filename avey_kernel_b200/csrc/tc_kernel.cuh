@@ -58,17 +58,16 @@ constexpr int kTcOutTileBytes = 2048; // one warp's 32 x 32 output staging tile
 constexpr int kTcOutStageBytes = 8 * kTcOutTileBytes;
 constexpr int kTcZBoxBytes = 16384;  // one {64 features x 128 keys} box of a unit
 constexpr int kTcMaxSlots = 6;
-constexpr int kTcMaxStages = 8;
+constexpr int kTcMaxStages = 12;  // 192 KB of ring / 16 KB stages (one key tile)
 constexpr int kTcChunk = 64;                      // phase-A feature chunk (128-byte rows)
 constexpr int kTcTileBytesA = 128 * kTcChunk * 2; // one 128-row tile of a chunk (16 KB)
 constexpr int kTcMaxFeatures = 2048;  // bias staged in shared memory
 constexpr int kTcCtrlBytes = 13312;
 
 struct TcGeom {
-  int nslot;          // phase-C ring slots
-  int n_qtiles;       // query tiles per batch row
-  int a_nstage;       // phase-A stages inside the phase-C ring space
-  int a_stage_bytes;  // key tiles x 16 KB
+  int nslot;     // phase-C ring slots
+  int n_qtiles;  // query tiles per batch row
+  int v_tma;     // V tiles reach shared memory by TMA (aligned V), else per-thread loads
 };
 
 // TMEM column of the packed P pair holding key j (two keys per 32-bit column).
@@ -219,6 +218,24 @@ __device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
   return v;
 }
 
+// The 32 weights V[row, c0 .. c0 + 31] of the TMA-staged V tiles: key tile
+// c0 / 128 sits in ring slot c0 / 128 as two {64 keys, 128 rows} boxes with
+// the 128-byte swizzle (16-byte chunk q of row r at position q ^ (r % 8)).
+__device__ __forceinline__ void load_v_tile32(uint32_t ring_addr, int c0, int row, uint32_t (&w)[16]) {
+  const int kk = c0 & 127;
+  const uint32_t base = ring_addr + static_cast<uint32_t>((c0 >> 7) * kTcUnitBytes + (kk >> 6) * kTcZBoxBytes +
+                                                          row * 128);
+  const uint32_t j0 = static_cast<uint32_t>((kk & 63) >> 3);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 v = ld_shared_v4(base + (((j0 + q) ^ static_cast<uint32_t>(row & 7)) << 4));
+    w[4 * q] = v.x;
+    w[4 * q + 1] = v.y;
+    w[4 * q + 2] = v.z;
+    w[4 * q + 3] = v.w;
+  }
+}
+
 // 32 consecutive 16-bit elements starting at p into w[16] (p 16-byte aligned
 // when vec); elements at or past n_ok read as zero.
 template <typename T>
@@ -248,7 +265,8 @@ template <typename T, int ACT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_contextualize(const FwdArgs args, const __grid_constant__ CUtensorMap map_q,
                      const __grid_constant__ CUtensorMap map_z,
-                     const __grid_constant__ CUtensorMap map_o, const TcGeom geom) {
+                     const __grid_constant__ CUtensorMap map_o,
+                     const __grid_constant__ CUtensorMap map_v, const TcGeom geom) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -264,7 +282,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = tid >> 5, lane = tid & 31;
   if (tid == 0) AVEY_STAMP(0);
   const int nslot = geom.nslot;
-  const int nst = geom.a_nstage;
   const int C = args.ctx, D = args.feat, B = args.batch;
 
   // Work item: causal items with more key tiles come first (longest first).
@@ -308,6 +325,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_z);
     tma_prefetch_desc(&map_o);
+    if (geom.v_tma) tma_prefetch_desc(&map_v);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctrl->tmem_base), 512);
@@ -340,6 +358,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nunits = skip ? 0 : (nkeys + kTcUnitKeys - 1) / kTcUnitKeys;  // units per slice
   const int units_c = nslices * nunits;
   const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  // Phase-A stages of this item: one 16 KB tile per key tile, as many stages
+  // as the ring holds (up to 12 with one key tile).
+  const int a_stage_bytes = max(nk, 1) * kTcTileBytesA;
+  const int nst = min(kTcMaxStages, (nslot * kTcUnitBytes) / a_stage_bytes);
+  // With an aligned V, its tiles (128 query rows x 128 keys, 32 KB each) take
+  // the first nk ring slots after the Gram; the mix units follow them.
+  const int nvt = (geom.v_tma && args.has_v && !skip) ? nk : 0;
+  // Phase-C ring entries in order: the V tiles, then the units slice by slice.
+  auto e_unit = [&](int s, int u) { return nvt + s * nunits + u; };
 
   if (warp == 0) {
     // ============================================================ TMA producer
@@ -350,15 +377,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint64_t keep = l2_policy_evict_last();  // z_tr is read again (phase C, other CTAs)
       // Phase-A stage state.
       int a_st = 0, a_use = 0, c = 0;
-      // Phase-C ring state.
-      int c_slot = 0, c_use = 0, u = 0, sl = 0, uu = 0;
-      int nbox = (min(kTcSliceCols, D) + 63) / 64;
+      // Phase-A stages (bit per stage) released for the last time so far.
+      uint32_t released = 0u;
+      // Phase-C ring entry e goes to slot e % nslot once the slot's previous
+      // entry (e - nslot) has been released on empty[] (its phase
+      // (e / nslot) - 1); a slot's first entry waits only for the last use of
+      // the phase-A stages that overlap its bytes, so V tiles and early units
+      // load while the Gram's last chunks still run.
+      auto claim = [&](int e) -> int {
+        const int slot = e % nslot;
+        if (e >= nslot) {
+          mbar_wait(smem_u32(&ctrl->empty[slot]), ((e / nslot) - 1) & 1);
+        } else {
+          const int lo = (slot * kTcUnitBytes) / a_stage_bytes;
+          const int hi = min(((slot + 1) * kTcUnitBytes - 1) / a_stage_bytes, min(nst, nchunk) - 1);
+          for (int st_i = lo; st_i <= hi; ++st_i) {
+            if ((released >> st_i) & 1u) continue;
+            const int uses = (nchunk - st_i + nst - 1) / nst;  // chunks that went to stage st_i
+            mbar_wait(smem_u32(&ctrl->a_empty[st_i]), (uses - 1) & 1);
+            released |= 1u << st_i;
+          }
+        }
+        return slot;
+      };
       auto load_stage = [&]() {
         if (a_use > 0) mbar_wait(smem_u32(&ctrl->a_empty[a_st]), (a_use - 1) & 1);
         AVEY_STAMP_UNIT(c, 0);
         {
           const uint32_t full = smem_u32(&ctrl->a_full[a_st]);
-          const uint32_t st = stage_addr + a_st * geom.a_stage_bytes;
+          const uint32_t st = stage_addr + a_st * a_stage_bytes;
           // Key tiles 0 .. nk-1; the query tile is key tile qt (qt < nk in
           // both modes), so it is not loaded a second time.
           mbar_arrive_expect_tx(full, nk * kTcTileBytesA);
@@ -371,41 +418,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ++a_use;
         }
       };
-      auto load_unit = [&]() {
-        if (c_use > 0) mbar_wait(smem_u32(&ctrl->empty[c_slot]), (c_use - 1) & 1);
-        AVEY_STAMP_UNIT(128 + u, 0);
-        {
-          const uint32_t full = smem_u32(&ctrl->full[c_slot]);
-          const uint32_t dst = ring_addr + c_slot * kTcUnitBytes;
+      // Phase-A stages occupy the ring space: each phase-C entry claims its
+      // slot only after the stages under it are released (claim above).
+      while (c < nchunk) load_stage();
+      // V tiles for the P phase: two {64 keys, 128 rows} boxes per key tile.
+      for (int t = 0; t < nvt; ++t) {
+        const int slot = claim(t);
+        const uint32_t full = smem_u32(&ctrl->full[slot]);
+        mbar_arrive_expect_tx(full, kTcUnitBytes);
+        for (int bx = 0; bx < 2; ++bx)
+          tma_load_3d_hint(ring_addr + slot * kTcUnitBytes + bx * kTcZBoxBytes, &map_v, full,
+                           t * kTcUnitKeys + bx * 64, q_lo, 0, keep);
+      }
+      for (int sl = 0; sl < nslices; ++sl) {
+        const int nbox = (min(kTcSliceCols, D - sl * kTcSliceCols) + 63) / 64;
+        for (int uu = 0; uu < nunits; ++uu) {
+          const int slot = claim(e_unit(sl, uu));
+          AVEY_STAMP_UNIT(128 + sl * nunits + uu, 0);
+          const uint32_t full = smem_u32(&ctrl->full[slot]);
+          const uint32_t dst = ring_addr + slot * kTcUnitBytes;
           mbar_arrive_expect_tx(full, nbox * kTcZBoxBytes);
           for (int i = 0; i < nbox; ++i)
             tma_load_3d_hint(dst + i * kTcZBoxBytes, &map_z, full, sl * kTcSliceCols + i * 64,
                              uu * kTcUnitKeys, b, keep);
         }
-        ++u;
-        if (++uu == nunits) {
-          uu = 0;
-          ++sl;
-          nbox = (min(kTcSliceCols, D - sl * kTcSliceCols) + 63) / 64;
-        }
-        if (++c_slot == nslot) {
-          c_slot = 0;
-          ++c_use;
-        }
-      };
-      // Phase-A stages occupy the ring space, so the ring is filled only once
-      // every stage has been released for the last time (the MMA warp is done
-      // with it); the first ring loads overlap phase B.
-      while (c < nchunk) load_stage();
-      {
-        // Final release of every stage slot s: its last use is use index
-        // (uses[s] - 1), where uses[s] = number of chunks that went to slot s.
-        for (int st_i = 0; st_i < min(nst, nchunk); ++st_i) {
-          const int uses = (nchunk - st_i + nst - 1) / nst;
-          mbar_wait(smem_u32(&ctrl->a_empty[st_i]), (uses - 1) & 1);
-        }
       }
-      while (u < units_c) load_unit();
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
@@ -414,7 +451,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // Descriptors are advanced by adding (byte offset >> 4) to the start
       // address field; every address stays below 2^18, so nothing carries out.
       const uint64_t dq0 = smem_desc_sw128(stage_addr, 16, 1024);
-      const uint32_t stage_adv = static_cast<uint32_t>(geom.a_stage_bytes) >> 4;
+      const uint32_t stage_adv = static_cast<uint32_t>(a_stage_bytes) >> 4;
       const uint32_t q_adv = static_cast<uint32_t>(qt * kTcTileBytesA) >> 4;
       const uint32_t idesc_g256 = idesc_f16(fmt, 128, 256, 0, 0);
       const uint32_t idesc_g128 = idesc_f16(fmt, 128, 128, 0, 0);
@@ -454,8 +491,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       AVEY_STAMP(3);  // P observed by the MMA warp
       const bool fix = ctrl->fix != 0;
       const uint64_t dz0 = smem_desc_sw128(ring_addr, kTcZBoxBytes, 1024);
-      int slot = 0;
-      ph = 0;
+      uint32_t fpar = 0u;  // per slot: parity of the units it has held (phases of fixed[])
       for (int s = 0; s < nslices; ++s) {
         const int buf = s & 1;
         if (s >= 2) {
@@ -466,7 +502,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t idesc_o = idesc_f16(fmt, 128, static_cast<uint32_t>((width + 15) & ~15), 0, 1);
         const uint32_t d_tmem = tmem + o_col(buf, nk);
         for (int uu = 0; uu < nunits; ++uu) {
-          mbar_wait(smem_u32(fix ? &ctrl->fixed[slot] : &ctrl->full[slot]), ph);
+          const int e = e_unit(s, uu);
+          const int slot = e % nslot;
+          if (fix) {
+            mbar_wait(smem_u32(&ctrl->fixed[slot]), (fpar >> slot) & 1u);
+            fpar ^= 1u << slot;
+          }
+          else mbar_wait(smem_u32(&ctrl->full[slot]), (e / nslot) & 1);
           tc_fence_after();
           AVEY_STAMP_UNIT(128 + s * nunits + uu, 1);
           {
@@ -480,10 +522,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             (uu != 0 || k != 0) ? 1u : 0u);
             tc_commit(smem_u32(&ctrl->empty[slot]));
             AVEY_STAMP_UNIT(128 + s * nunits + uu, 2);
-          }
-          if (++slot == nslot) {
-            slot = 0;
-            ph ^= 1u;
           }
         }
         tc_commit(smem_u32(&ctrl->o_full[buf]));
@@ -577,8 +615,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // ---------------- phase B: P = G * rinv_i * rinv_j * V, masked, into TMEM
       const bool row_ok = i < C && ctrl->kvalid[i];
       const float rqi = row_ok ? ctrl->rinv[i] : 0.f;
-      const T* vrow = (args.has_v && i < C) ? static_cast<const T*>(args.v) + static_cast<int64_t>(i) * args.v_rs
-                                            : nullptr;
+      // V rows by per-thread loads only when its tiles do not come by TMA.
+      const T* vrow = (args.has_v && i < C && nvt == 0)
+                          ? static_cast<const T*>(args.v) + static_cast<int64_t>(i) * args.v_rs
+                          : nullptr;
       const bool v_vec = (reinterpret_cast<uintptr_t>(args.v) & 15u) == 0 && (args.v_rs & 7) == 0;
       const uint64_t keep = l2_policy_evict_last();    // V: read by every batch row
       const uint64_t stream = l2_policy_evict_normal(); // gate and output: touched once
@@ -602,6 +642,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         mbar_wait(smem_u32(&ctrl->s_full), 0);
         tc_fence_after();
+        for (int t = 0; t < nvt; ++t) mbar_wait(smem_u32(&ctrl->full[t]), 0);
         if (cw == 0 && lane == 0) AVEY_STAMP(6);  // Gram complete
         // Chunks need per-key selects only where a mask bit can be 0 for a key
         // whose zero inverse norm does not already zero the product: keys above
@@ -617,6 +658,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           uint32_t g[32];
           tmem_ld32(tmem + lane_off + c0, g);
           if (vrow && ch + 2 < nch) load_raw32<T>(vrow + c0 + 64, C - c0 - 64, v_vec, vnn, keep);
+          if (nvt) load_v_tile32(ring_addr, c0, row, vw);
           const bool masked = exact || (args.causal && c0 + 31 > i0);
           uint32_t okb = 0u;
           if (masked) {
@@ -667,7 +709,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctrl->p_ready));
       named_bar_sync(1, 256);
-      if (cw == 0 && lane == 0) AVEY_STAMP(7);  // P written
+      if (cw == 0 && lane == 0) {
+        AVEY_STAMP(7);  // P written
+        // Every compute warp is done with the V tiles: their slots go to the mix units.
+        for (int t = 0; t < nvt; ++t) mbar_arrive(smem_u32(&ctrl->empty[t]));
+      }
       // O (and the row sums) carry rq only if it went into P.
       const float o_scale = kRowScaleInP<T> ? 1.f : rqi;
       const float inv_den =
@@ -785,11 +831,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else {
         // Fix mode: zero every padded key row of each mix unit before the MMA
         // reads it (warpgroup 1), while warpgroup 0 drains all slices.
-        int slot = 0, sl = 0, uu = 0;
-        uint32_t ph = 0;
+        int sl = 0, uu = 0;
         for (int u = 0; u < units_c; ++u) {
           const int nbox = (min(kTcSliceCols, D - sl * kTcSliceCols) + 63) / 64;
-          mbar_wait(smem_u32(&ctrl->full[slot]), ph);
+          const int e = e_unit(sl, uu);
+          const int slot = e % nslot;
+          mbar_wait(smem_u32(&ctrl->full[slot]), (e / nslot) & 1);
           // Warpgroup 1 (128 threads) covers the unit's nbox x 64 rows.
           for (int idx = wq * 32 + lane; idx < nbox * kTcUnitKeys; idx += 128) {
             const int r = idx & (kTcUnitKeys - 1), box = idx / kTcUnitKeys;
@@ -806,10 +853,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (++uu == nunits) {
             uu = 0;
             ++sl;
-          }
-          if (++slot == nslot) {
-            slot = 0;
-            ph ^= 1u;
           }
         }
       }
