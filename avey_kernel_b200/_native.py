@@ -24,7 +24,8 @@ STATUS_NAMES = {
 # Exported symbols, mirrored from include/avey_b200.h (tests check the header).
 EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_fwd_workspace_size', 'avey_fwd_noalloc_v1',
            'avey_bwd_step_v1', 'avey_bwd_workspace_size',
-           'avey_last_error', 'avey_device_status', 'avey_launch_count', 'avey_abi_version')
+           'avey_last_error', 'avey_device_status', 'avey_launch_count', 'avey_abi_version',
+           'avey_test_hooks_v1')
 BWD_PREP, BWD_SCORES, BWD_EPILOGUE, BWD_DSCORES, BWD_FINAL = range(5)
 NOALLOC_MAX_ROWS = 1 << 20
 ABI_VERSION = 4
@@ -180,6 +181,8 @@ def lib() -> ctypes.CDLL:
         dll.avey_launch_count.restype = ctypes.c_uint64
         dll.avey_abi_version.argtypes = []
         dll.avey_abi_version.restype = ctypes.c_int
+        dll.avey_test_hooks_v1.argtypes = [ctypes.c_longlong, ctypes.c_int]
+        dll.avey_test_hooks_v1.restype = ctypes.c_int
         if dll.avey_abi_version() != ABI_VERSION:
             raise RuntimeError(f'{path}: ABI version {dll.avey_abi_version()} != {ABI_VERSION}')
         _lib = dll
@@ -228,6 +231,13 @@ def device_status(clear: bool = False) -> int:
     flags = ctypes.c_uint32(0)
     _check(lib().avey_device_status(ctypes.byref(flags), int(clear)))
     return flags.value
+
+
+def test_hooks(wait_limit_cycles: int = 0, stall: bool = False) -> None:
+    """avey_test_hooks_v1 (tests only): lower the bounded-wait limit and make
+    the fused kernel's TMA and MMA warps idle so a wait runs out. Call with no
+    arguments to restore the defaults."""
+    _check(lib().avey_test_hooks_v1(int(wait_limit_cycles), 1 if stall else 0))
 
 
 def launch_count() -> int:

@@ -26,6 +26,8 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
+// Test hook (avey_test_hooks_v1): the fused kernel's TMA and MMA warps issue nothing.
+std::atomic<int> g_test_stall{0};
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -93,16 +95,41 @@ int validate(const AveyFwdParams* p) {
   return AVEY_OK;
 }
 
-int device_arch_ok(int* major_out) {
-  int dev = 0, major = 0, minor = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return fail(AVEY_ERR_CUDA, "cudaGetDevice failed");
-  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
-  if (major_out) *major_out = major;
-  if (major != 10 || minor != 0)
-    return fail(AVEY_ERR_ARCH, "device %d is sm_%d%d; this library is built for sm_100a", dev, major,
-                minor);
+constexpr int kMaxDevices = 64;
+
+// The current device, checked to be sm_100 once per device (the compute
+// capability is queried on the first call only).
+int device_arch_ok(int* dev_out) {
+  static std::once_flag once[kMaxDevices];
+  static int cc[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(AVEY_ERR_CUDA, "cannot determine the current device");
+  std::call_once(once[dev], [dev] {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cc[dev] = 10 * major + minor;
+  });
+  if (dev_out) *dev_out = dev;
+  if (cc[dev] != 100)
+    return fail(AVEY_ERR_ARCH, "device %d is sm_%d; this library is built for sm_100a", dev, cc[dev]);
   return AVEY_OK;
+}
+
+// Opt kernel K into `bytes` of dynamic shared memory, once per device. The
+// outcome is kept per device and returned on every call, so a failure is
+// reported as itself each time instead of as a later launch error.
+template <auto K>
+cudaError_t smem_opt_in(int bytes) {
+  static std::once_flag once[kMaxDevices];
+  static cudaError_t err[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::call_once(once[dev], [dev, bytes] {
+    err[dev] = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  return err[dev];
 }
 
 // Contexts up to 512 run the fused kernel; longer ones (up to 8192) the
@@ -142,6 +169,7 @@ TcLayout tc_layout(const AveyFwdParams* p) {
   l.geom.n_qtiles = nk_max;
   // V tiles by TMA need a 16-byte aligned base and rows of multiples of 8 elements.
   l.geom.v_tma = p->v && aligned16(p->v) && (p->v_row_stride % 8 == 0);
+  l.geom.test_stall = g_test_stall.load(std::memory_order_relaxed);
   l.smem = 1024 + nslot * avey::kTcUnitBytes + avey::kTcOutStageBytes + avey::kTcCtrlBytes;
   return l;
 }
@@ -234,68 +262,99 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 3-D map over z_tr viewed as [batch][context][features] with a box of
-// `box_rows` rows x `box_cols` features (64-byte swizzle for 32 columns,
-// 128-byte swizzle for 64), zero fill out of bounds.
-int encode_map(const AveyFwdParams* p, const void* base, int64_t batch_stride, int64_t row_stride,
-               int box_cols, int box_rows, CUtensorMap* map) {
-  auto fn = encode_fn();
-  if (!fn) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  const int es = elem_size(p->dtype);
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(p->features), static_cast<cuuint64_t>(p->context),
-                        static_cast<cuuint64_t>(p->batch)};
-  int64_t bs = batch_stride;
-  if (p->batch == 1) bs = row_stride * p->context;  // unused; any aligned value
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * es),
-                           static_cast<cuuint64_t>(((bs * es) + 15) / 16 * 16)};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
-  const CUtensorMapSwizzle swz =
-      box_cols * es == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
-  cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapDataType dt =
-      p->dtype == AVEY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return AVEY_OK;
+// Encoded tensor maps, cached per process: a map is a pure function of its
+// encode arguments (device, base address, shape, strides, box, element type),
+// so callers that reuse buffers (training loops, graph warm-ups, benchmarks)
+// skip the driver call. Small and mutex-guarded; the oldest entry is replaced.
+struct MapKey {
+  int dev, dtype, box_cols, box_rows;
+  const void* base;
+  uint64_t dims[3], strides[2];
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapCache {
+  static constexpr int kEntries = 64;
+  std::mutex mu;
+  MapKey keys[kEntries];
+  CUtensorMap maps[kEntries];
+  int used = 0, next = 0;
+};
+MapCache& map_cache() {
+  static MapCache c;
+  return c;
 }
 
-// 3-D map with explicit sizes: dims {inner, rows, batch}, strides in bytes.
-int encode_map_dims(int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
-                    uint64_t row_bytes, uint64_t batch_bytes, int box_cols, int box_rows,
-                    CUtensorMap* map) {
+// Encode (or fetch) a 3-D tiled map: dims {inner, rows, batch}, strides in bytes.
+int encode_cached(int dtype, const void* base, const cuuint64_t (&dims)[3], const cuuint64_t (&strides)[2],
+                  int box_cols, int box_rows, CUtensorMap* map) {
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));  // padding bytes take part in the comparison
+  cudaGetDevice(&k.dev);
+  k.dtype = dtype;
+  k.box_cols = box_cols;
+  k.box_rows = box_rows;
+  k.base = base;
+  for (int i = 0; i < 3; ++i) k.dims[i] = dims[i];
+  for (int i = 0; i < 2; ++i) k.strides[i] = strides[i];
+  MapCache& c = map_cache();
+  {
+    std::lock_guard<std::mutex> lock(c.mu);
+    for (int i = 0; i < c.used; ++i)
+      if (c.keys[i] == k) {
+        *map = c.maps[i];
+        return AVEY_OK;
+      }
+  }
   auto fn = encode_fn();
   if (!fn) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const int es = elem_size(dtype);
-  cuuint64_t dims[3] = {inner, rows, batch};
-  cuuint64_t strides[2] = {row_bytes, batch > 1 ? batch_bytes : row_bytes * rows};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
   const CUtensorMapSwizzle swz =
       box_cols * es == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt =
       dtype == AVEY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides[0], strides[1]};
+  const CUresult r = fn(map, dt, 3, const_cast<void*>(base), d, st, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(AVEY_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  std::lock_guard<std::mutex> lock(c.mu);
+  const int slot = c.used < MapCache::kEntries ? c.used++ : (c.next++ % MapCache::kEntries);
+  c.keys[slot] = k;
+  c.maps[slot] = *map;
   return AVEY_OK;
+}
+
+// 3-D map over z_tr viewed as [batch][context][features] with a box of
+// `box_rows` rows x `box_cols` features (64-byte swizzle for 32 columns,
+// 128-byte swizzle for 64), zero fill out of bounds.
+int encode_map(const AveyFwdParams* p, const void* base, int64_t batch_stride, int64_t row_stride,
+               int box_cols, int box_rows, CUtensorMap* map) {
+  const int es = elem_size(p->dtype);
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p->features), static_cast<cuuint64_t>(p->context),
+                              static_cast<cuuint64_t>(p->batch)};
+  int64_t bs = batch_stride;
+  if (p->batch == 1) bs = row_stride * p->context;  // unused; any aligned value
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * es),
+                                 static_cast<cuuint64_t>(((bs * es) + 15) / 16 * 16)};
+  return encode_cached(p->dtype, base, dims, strides, box_cols, box_rows, map);
+}
+
+// 3-D map with explicit sizes: dims {inner, rows, batch}, strides in bytes.
+int encode_map_dims(int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
+                    uint64_t row_bytes, uint64_t batch_bytes, int box_cols, int box_rows,
+                    CUtensorMap* map) {
+  const cuuint64_t dims[3] = {inner, rows, batch};
+  const cuuint64_t strides[2] = {row_bytes, batch > 1 ? batch_bytes : row_bytes * rows};
+  return encode_cached(dtype, base, dims, strides, box_cols, box_rows, map);
 }
 
 template <typename T, int ACT>
 int launch_long(const AveyFwdParams* p, cudaStream_t stream) {
-  static std::once_flag attr_once[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(avey::tc_gram_p<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    kMaxDynSmem);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(avey::tc_pv<T, ACT>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-  });
+  cudaError_t attr_err = smem_opt_in<avey::tc_gram_p<T>>(kMaxDynSmem);
+  if (attr_err == cudaSuccess) attr_err = smem_opt_in<avey::tc_pv<T, ACT>>(kMaxDynSmem);
   if (attr_err != cudaSuccess)
     return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
   LongLayout l = long_layout(p);
@@ -354,14 +413,7 @@ int launch_long(const AveyFwdParams* p, cudaStream_t stream) {
 template <typename T, int ACT>
 int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
   if (is_long(p)) return launch_long<T, ACT>(p, stream);
-  static std::once_flag attr_once[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(avey::tc_contextualize<T, ACT>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-  });
+  const cudaError_t attr_err = smem_opt_in<avey::tc_contextualize<T, ACT>>(kMaxDynSmem);
   if (attr_err != cudaSuccess)
     return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
   CUtensorMap map_q, map_z, map_o, map_v;
@@ -430,14 +482,7 @@ bool use_simt2(const AveyFwdParams* p) { return p->dtype != AVEY_F64; }
 
 template <typename T, bool LONG>
 int launch_simt2(const AveyFwdParams* p, cudaStream_t stream) {
-  static std::once_flag attr_once[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(avey::simt2_contextualize<T, LONG>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, avey::kS2SmemBytes);
-  });
+  const cudaError_t attr_err = smem_opt_in<avey::simt2_contextualize<T, LONG>>(avey::kS2SmemBytes);
   if (attr_err != cudaSuccess)
     return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
   const avey::FwdArgs args = make_args(p);
@@ -568,7 +613,6 @@ namespace {
 // name as a device address; its address comes from cudaGetSymbolAddress.
 __device__ __align__(256) float g_noalloc_sumsq[AVEY_NOALLOC_MAX_ROWS];
 
-constexpr int kMaxDevices = 64;
 std::once_flag g_noalloc_once[kMaxDevices];
 void* g_noalloc_ptr[kMaxDevices];
 cudaError_t g_noalloc_err[kMaxDevices];
@@ -581,6 +625,18 @@ int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
   AveyPlan plan;
   int rc = avey_fwd_plan(p, &plan);
   if (rc != AVEY_OK) return rc;
+  AveyFwdParams q = *p;
+  // Contexts above 512 would take the long-context tensor-core path, whose P
+  // workspace this entry point does not have: they run the CUDA-core kernel.
+  if (is_long(p)) {
+    if (p->kernel == AVEY_KERNEL_TCGEN05)
+      return fail(AVEY_ERR_UNSUPPORTED,
+                  "the no-allocation entry point runs contexts above 512 on CUDA cores only");
+    q.kernel = AVEY_KERNEL_SIMT;
+  }
+  // Only the fused tensor-core path reads scratch (one float per row); the
+  // CUDA-core kernels need none and have no row limit here.
+  if (plan.kernel != AVEY_KERNEL_TCGEN05 || is_long(p)) return avey_fwd_v1(&q, stream);
   const uint64_t rows = static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context);
   if (rows > AVEY_NOALLOC_MAX_ROWS)
     return fail(AVEY_ERR_ARGUMENT,
@@ -598,15 +654,6 @@ int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
   if (g_noalloc_err[dev] != cudaSuccess || !g_noalloc_ptr[dev])
     return fail(AVEY_ERR_CUDA, "cudaGetSymbolAddress(no-allocation scratch): %s",
                 cudaGetErrorString(g_noalloc_err[dev]));
-  AveyFwdParams q = *p;
-  // Contexts above 512 would take the long-context tensor-core path, whose P
-  // workspace this entry point does not have: they run the CUDA-core kernel.
-  if (is_long(p)) {
-    if (p->kernel == AVEY_KERNEL_TCGEN05)
-      return fail(AVEY_ERR_UNSUPPORTED,
-                  "the no-allocation entry point runs contexts above 512 on CUDA cores only");
-    q.kernel = AVEY_KERNEL_SIMT;
-  }
   q.workspace = g_noalloc_ptr[dev];
   q.workspace_bytes = static_cast<uint64_t>(AVEY_NOALLOC_MAX_ROWS) * sizeof(float);
   return avey_fwd_v1(&q, stream);
@@ -632,18 +679,15 @@ int avey_device_status(uint32_t* flags, int clear) {
 
 uint64_t avey_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int avey_test_hooks_v1(long long wait_limit_cycles, int stall) {
+  if (wait_limit_cycles <= 0) wait_limit_cycles = avey::kWaitLimitCycles;
+  const cudaError_t e = cudaMemcpyToSymbol(avey::g_wait_limit, &wait_limit_cycles, sizeof(long long));
+  if (e != cudaSuccess) return fail(AVEY_ERR_CUDA, "setting the wait limit: %s", cudaGetErrorString(e));
+  g_test_stall.store(stall ? 1 : 0, std::memory_order_relaxed);
+  return ok();
+}
+
 int avey_abi_version(void) { return AVEY_ABI_VERSION; }
 
-#ifdef AVEY_TRACE
-// Trace builds only: copy the per-CTA phase timeline (kTraceCtas x 16 u64).
-AVEY_API int avey_trace_read(unsigned long long* dst) {
-  return cudaMemcpyFromSymbol(dst, avey::g_trace, sizeof(avey::g_trace)) == cudaSuccess ? 0 : -1;
-}
-AVEY_API int avey_trace_units_read(unsigned long long* dst) {
-  return cudaMemcpyFromSymbol(dst, avey::g_trace_units, sizeof(avey::g_trace_units)) == cudaSuccess
-             ? 0
-             : -1;
-}
-#endif
 
 }  // extern "C"

@@ -50,19 +50,13 @@ def needs_build() -> bool:
     return any(p.stat().st_mtime > mtime for p in deps)
 
 
-TRACE_LIB = LIB_DIR / 'libavey_b200_trace.so'
-
-
-def build(force: bool = False, verbose: bool = False, extra=(), trace: bool = False) -> Path:
-    """Build the library (or, with trace=True, the phase-timeline build that
-    records %globaltimer stamps per CTA; see ptx.cuh)."""
-    target = TRACE_LIB if trace else LIB
-    if not force and not trace and not needs_build():
+def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
+    """Build the library unless it is newer than every source."""
+    target = LIB
+    if not force and not needs_build():
         return LIB
     LIB_DIR.mkdir(exist_ok=True)
     tmp = target.with_suffix('.so.tmp')
-    if trace:
-        extra = (*extra, '-DAVEY_TRACE')
     cmd = [nvcc_path(), *NVCC_FLAGS, *extra, '-I', str(ROOT / 'include'), '-I', str(CSRC),
            *[str(CSRC / s) for s in SOURCES], '-o', str(tmp), '-lcudart']
     if verbose:
@@ -82,11 +76,10 @@ def main():
     ap.add_argument('--force', action='store_true')
     ap.add_argument('--verbose', action='store_true')
     ap.add_argument('--ptxas-info', action='store_true', help='print registers / spills / smem')
-    ap.add_argument('--trace', action='store_true', help='build lib/libavey_b200_trace.so')
     args = ap.parse_args()
     extra = ['-Xptxas', '-v'] if args.ptxas_info else []
     print(build(force=args.force or args.ptxas_info, verbose=args.verbose or args.ptxas_info,
-                extra=extra, trace=args.trace))
+                extra=extra))
 
 
 if __name__ == '__main__':

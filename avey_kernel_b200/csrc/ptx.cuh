@@ -11,36 +11,11 @@ namespace avey {
 // The library is a single translation unit, so the definition lives here.
 __device__ unsigned int g_devflags = 0u;
 
-// Optional phase timeline (trace builds only, -DAVEY_TRACE): per CTA, the
-// %globaltimer value (ns) at numbered points of the kernel.
-#ifdef AVEY_TRACE
-constexpr int kTraceCtas = 2048;
-constexpr int kTraceSlots = 16;
-__device__ unsigned long long g_trace[kTraceCtas][kTraceSlots];
-__device__ __forceinline__ void trace_stamp(int slot) {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  if (blockIdx.x < kTraceCtas) g_trace[blockIdx.x][slot] = t;
-}
-#define AVEY_STAMP(slot) ::avey::trace_stamp(slot)
-// Per-unit events of the first kTraceUnitCtas CTAs: [cta][unit][event].
-constexpr int kTraceUnitCtas = 4;
-constexpr int kTraceUnits = 256;
-__device__ unsigned long long g_trace_units[kTraceUnitCtas][kTraceUnits][4];
-__device__ __forceinline__ void trace_unit(int unit, int event) {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  if (blockIdx.x < kTraceUnitCtas && unit >= 0 && unit < kTraceUnits)
-    g_trace_units[blockIdx.x][unit][event] = t;
-}
-#define AVEY_STAMP_UNIT(unit, event) ::avey::trace_unit(unit, event)
-#else
-#define AVEY_STAMP(slot) ((void)0)
-#define AVEY_STAMP_UNIT(unit, event) ((void)0)
-#endif
-
 // ~2^31 SM cycles (about one second at 1.9 GHz) before a wait gives up.
 constexpr long long kWaitLimitCycles = 1ll << 31;
+// The limit in force: kWaitLimitCycles unless a test lowers it (test-only
+// entry point avey_test_hooks_v1). Read only on the slow path of a wait.
+__device__ long long g_wait_limit = kWaitLimitCycles;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -101,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 255u) == 0u) {
       if (*reinterpret_cast<volatile unsigned int*>(&g_devflags) != 0u) return false;
-      if (clock64() - start > kWaitLimitCycles) {
+      if (clock64() - start > *reinterpret_cast<volatile long long*>(&g_wait_limit)) {
         atomicOr(&g_devflags, 1u);
         return false;
       }

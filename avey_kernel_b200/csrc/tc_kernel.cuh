@@ -68,6 +68,7 @@ struct TcGeom {
   int nslot;     // phase-C ring slots
   int n_qtiles;  // query tiles per batch row
   int v_tma;     // V tiles reach shared memory by TMA (aligned V), else per-thread loads
+  int test_stall;  // test hook: the TMA and MMA warps issue nothing, so waits run out
 };
 
 // TMEM column of the packed P pair holding key j (two keys per 32-bit column).
@@ -280,7 +281,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) AVEY_STAMP(0);
   const int nslot = geom.nslot;
   const int C = args.ctx, D = args.feat, B = args.batch;
 
@@ -289,14 +289,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int qt = args.causal ? geom.n_qtiles - 1 - item / B : item / B;
   const int b = item % B;
   const int q_lo = qt * 128;
-#ifdef AVEY_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) {
-    g_trace[blockIdx.x][15] = qt * 100000ull + b;
-    uint32_t smid;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    g_trace[blockIdx.x][13] = smid;
-  }
-#endif
 
 
   // ---------------------------------------------------------------- setup
@@ -346,7 +338,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctrl->tmem_base;
-  if (tid == 0) AVEY_STAMP(1);
 
   // ---------------------------------------------------------------- geometry
   const int kv_end = ctrl->last_valid + 1;  // == C without a mask
@@ -373,7 +364,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // One lane walks the whole schedule (a per-step branch on the lane index
     // would cost a reconvergence every step). Slot indices and barrier
     // parities advance incrementally (no divisions in the hot loop).
-    if (!skip && lane == 0) {
+    if (!skip && lane == 0 && !geom.test_stall) {
       const uint64_t keep = l2_policy_evict_last();  // z_tr is read again (phase C, other CTAs)
       // Phase-A stage state.
       int a_st = 0, a_use = 0, c = 0;
@@ -402,7 +393,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       auto load_stage = [&]() {
         if (a_use > 0) mbar_wait(smem_u32(&ctrl->a_empty[a_st]), (a_use - 1) & 1);
-        AVEY_STAMP_UNIT(c, 0);
         {
           const uint32_t full = smem_u32(&ctrl->a_full[a_st]);
           const uint32_t st = stage_addr + a_st * a_stage_bytes;
@@ -434,7 +424,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int nbox = (min(kTcSliceCols, D - sl * kTcSliceCols) + 63) / 64;
         for (int uu = 0; uu < nunits; ++uu) {
           const int slot = claim(e_unit(sl, uu));
-          AVEY_STAMP_UNIT(128 + sl * nunits + uu, 0);
           const uint32_t full = smem_u32(&ctrl->full[slot]);
           const uint32_t dst = ring_addr + slot * kTcUnitBytes;
           mbar_arrive_expect_tx(full, nbox * kTcZBoxBytes);
@@ -447,7 +436,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ============================================================ MMA issuer
     // One lane issues everything (see the producer).
-    if (!skip && lane == 0) {
+    if (!skip && lane == 0 && !geom.test_stall) {
       // Descriptors are advanced by adding (byte offset >> 4) to the start
       // address field; every address stays below 2^18, so nothing carries out.
       const uint64_t dq0 = smem_desc_sw128(stage_addr, 16, 1024);
@@ -462,7 +451,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < nchunk; ++c) {
         mbar_wait(smem_u32(&ctrl->a_full[st]), ph);
         tc_fence_after();
-        AVEY_STAMP_UNIT(c, 1);
         {
           const uint64_t dk = dq0 + st * stage_adv;  // key tile 0 of this stage
           const uint64_t dq = dk + q_adv;              // the query tile (key tile qt)
@@ -477,7 +465,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                          acc);
           }
           tc_commit(smem_u32(&ctrl->a_empty[st]));
-          AVEY_STAMP_UNIT(c, 2);
         }
         if (++st == nst) {
           st = 0;
@@ -485,10 +472,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       tc_commit(smem_u32(&ctrl->s_full));
-      AVEY_STAMP(2);  // last Gram MMA issued
       mbar_wait(smem_u32(&ctrl->p_ready), 0);
       tc_fence_after();
-      AVEY_STAMP(3);  // P observed by the MMA warp
       const bool fix = ctrl->fix != 0;
       const uint64_t dz0 = smem_desc_sw128(ring_addr, kTcZBoxBytes, 1024);
       uint32_t fpar = 0u;  // per slot: parity of the units it has held (phases of fixed[])
@@ -510,7 +495,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           else mbar_wait(smem_u32(&ctrl->full[slot]), (e / nslot) & 1);
           tc_fence_after();
-          AVEY_STAMP_UNIT(128 + s * nunits + uu, 1);
           {
             // P keys 128 uu .. +127 start at TMEM column p_col(128 uu); K steps
             // of 16 keys advance 8 columns of P and 16 rows (2 KB) of the Z unit.
@@ -521,12 +505,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               tc_mma_f16_ts(d_tmem, a_tmem + 8 * k, dz + k * (2048 >> 4), idesc_o,
                             (uu != 0 || k != 0) ? 1u : 0u);
             tc_commit(smem_u32(&ctrl->empty[slot]));
-            AVEY_STAMP_UNIT(128 + s * nunits + uu, 2);
           }
         }
         tc_commit(smem_u32(&ctrl->o_full[buf]));
       }
-      AVEY_STAMP(4);  // last mix MMA issued
     }
   } else if (warp >= 4) {
     // ============================================================ compute warps
@@ -579,7 +561,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int j = cw * 32 + lane; j < nk * 128; j += 256) ctrl->rinv[j] = j < C ? ssq[j] : 0.f;
       }
       named_bar_sync(1, 256);
-      if (cw == 0 && lane == 0) AVEY_STAMP(5);  // norms read
       {
         const int tid_c = cw * 32 + lane;
         const float norm_eps = args.norm_eps_f;
@@ -643,7 +624,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_wait(smem_u32(&ctrl->s_full), 0);
         tc_fence_after();
         for (int t = 0; t < nvt; ++t) mbar_wait(smem_u32(&ctrl->full[t]), 0);
-        if (cw == 0 && lane == 0) AVEY_STAMP(6);  // Gram complete
         // Chunks need per-key selects only where a mask bit can be 0 for a key
         // whose zero inverse norm does not already zero the product: keys above
         // the causal diagonal, non-finite rows (0 * Inf), and padded keys when a
@@ -710,7 +690,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&ctrl->p_ready));
       named_bar_sync(1, 256);
       if (cw == 0 && lane == 0) {
-        AVEY_STAMP(7);  // P written
         // Every compute warp is done with the V tiles: their slots go to the mix units.
         for (int t = 0; t < nvt; ++t) mbar_arrive(smem_u32(&ctrl->empty[t]));
       }
@@ -821,7 +800,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cnt(smem_u32(&ctrl->o_empty[buf]), rel_cnt);
-        if (wq == 0 && lane == 0 && s < 4) AVEY_STAMP(8 + s);  // slice s drained
       };
       if (zrow && ch_lo * 32 < D)
         load_raw32<T>(zrow + ch_lo * 32, D - ch_lo * 32, zl_vec, gn, stream);
@@ -862,7 +840,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (tid == 0) AVEY_STAMP(14);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);

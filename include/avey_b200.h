@@ -165,9 +165,12 @@ AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* byte
  * for them needs a P workspace); forcing AVEY_KERNEL_TCGEN05 for them fails
  * with AVEY_ERR_UNSUPPORTED.
  *
- * Limit: batch * context <= AVEY_NOALLOC_MAX_ROWS (1,048,576 rows; the
- * array holds one float per row, 4 MiB per GPU); larger inputs are rejected
- * with AVEY_ERR_ARGUMENT. The first call on each device looks up the array's
+ * Limit: on the fused tensor-core path (bf16 / f16 up to 512 tokens, the only
+ * path that reads the scratch) batch * context <= AVEY_NOALLOC_MAX_ROWS
+ * (1,048,576 rows; the array holds one float per row, 4 MiB per GPU); larger
+ * inputs are rejected with AVEY_ERR_ARGUMENT. Inputs that run a CUDA-core
+ * kernel use no scratch and have no such limit. The first call on each device
+ * looks up the array's
  * device address (with that device current); make that first call before
  * any stream capture. All calls share the one array, so calls whose kernels
  * overlap on the GPU (for example on two streams) race; each call rewrites
@@ -279,6 +282,16 @@ AVEY_API int avey_device_status(uint32_t* flags, int clear);
 
 /* Number of kernels this library has launched in this process. */
 AVEY_API uint64_t avey_launch_count(void);
+
+/* Test-only hooks of the failure path (no counterpart in the reference).
+ * wait_limit_cycles: SM cycles after which a bounded wait on an mbarrier gives
+ * up (<= 0 restores the default of about one second). stall != 0: later
+ * launches of the fused tensor-core kernel start with their TMA and MMA warps
+ * issuing nothing, so its compute warps' first wait runs out, the kernel
+ * raises AVEY_DEVFLAG_TIMEOUT, unwinds and returns (no trap, the context stays
+ * usable). The wait limit applies to the current device; the stall flag to
+ * the process. Not for production use. */
+AVEY_API int avey_test_hooks_v1(long long wait_limit_cycles, int stall);
 
 /* AVEY_ABI_VERSION of the loaded library. */
 AVEY_API int avey_abi_version(void);

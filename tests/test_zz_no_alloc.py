@@ -78,9 +78,9 @@ def test_noalloc_entry_point_on_the_cuda_core_path():
 
 
 def test_noalloc_entry_point_rejects_inputs_beyond_its_limit():
-    # 2 x 524289 rows is one past the limit; rejected before anything launches.
-    rows = _native.NOALLOC_MAX_ROWS + 2
-    z = torch.empty(2, rows // 2, 8, dtype=torch.bfloat16)
+    # 2049 x 512 rows on the fused tensor-core path (the one that reads the
+    # scratch) is past the limit; rejected before anything launches.
+    z = torch.empty(_native.NOALLOC_MAX_ROWS // 512 + 1, 512, 8, dtype=torch.bfloat16)
     out = torch.empty_like(z)
     params = ops.build_params(z, None, None, None, None, out, eps=1e-6, norm_eps=1e-12,
                               causal=False, normalize=True, activation_id=0)
@@ -102,3 +102,46 @@ def test_noalloc_entry_point_runs_long_contexts_on_cuda_cores():
     assert _native.launch_count() == before + 1
     want = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=False)
     assert norm_rel_err(to_numpy(got), to_numpy(want)) <= TOL['bfloat16']
+
+
+@pytest.mark.gpu
+def test_noalloc_entry_point_runs_cuda_core_inputs_past_the_row_limit():
+    # The CUDA-core kernels read no scratch, so the row limit does not apply:
+    # fp32 input with more rows than the array holds.
+    z = torch.rand(_native.NOALLOC_MAX_ROWS // 64 + 1, 64, 8, device='cuda')
+    got = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=True)
+    want = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=False)
+    assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+def test_noalloc_entry_point_replays_from_a_cuda_graph():
+    # Graph capture is one of the situations with no allocator: warm up once
+    # (the first call on a device looks up the scratch address), capture one
+    # call into a CUDA graph, replay it, and compare with the workspace entry
+    # point bit for bit.
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4, 512, 2 * 256, generator=g).to(torch.bfloat16).cuda()
+    head, tail = x[..., :256], x[..., 256:]
+    v = (torch.randn(512, 512, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    want = _call(tail, v, head, None, None, causal=True, normalize=False, act=3, noalloc=False)
+    _call(tail, v, head, None, None, causal=True, normalize=False, act=3, noalloc=True)  # warm-up
+    out = torch.full(tail.shape, float('nan'), dtype=tail.dtype, device='cuda')
+    params = ops.build_params(tail, v, head, None, None, out, eps=1e-6, norm_eps=1e-12,
+                              causal=True, normalize=False, activation_id=3)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            _native.forward_noalloc(params, side.cuda_stream)
+    torch.cuda.current_stream().wait_stream(side)
+    out.fill_(float('nan'))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    out.fill_(float('nan'))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    del graph
