@@ -16,9 +16,14 @@ value  device time: K steps replayed from CUDA graphs between CUDA events on
 e2e    the same metric through the public API (avey / avey_b) with pinned
        host buffers: every step copies its inputs host->device and reads the
        output back, inside the timed region.
---impl reference  times the CPU implementation of the path (the NumPy port of
-       the reference's _reference in oracle/, fp32, all host threads) on a
-       bounded sample of the same workload; rank 0 only.
+--impl reference  times the reference's own CPU implementation of the path:
+       avey_kernels.ops.avey / avey_b with backend='torch' (its _reference,
+       fp32) from the unmodified install in baseline/_ref, on CPU tensors of
+       the whole per-GPU batch, every host thread, up to K steps within about
+       a minute; rank 0 only, the line stating the same global workload as
+       the GPU arm. Without baseline/_ref: the NumPy port in oracle/.
+cpu_baseline  (in the GPU arm's line, one GPU) the NumPy port of _reference
+       (oracle/, fp32, all host threads) on one batch row per run, ~10 s.
 --impl triton  (informational, one GPU) times the reference's own GPU kernel
        through its public API (avey_kernels.ops, backend='triton', from the
        unmodified install in baseline/_ref): normalisation pre-pass,
@@ -296,26 +301,77 @@ def time_cpu_port(cfg, seconds=10.0, max_steps=None, warmup=1, rows=1):
     return tokens / statistics.median(times), len(times), sum(times)
 
 
+def time_reference_torch(cfg, batch, steps, warmup, budget_s=60.0):
+    """Time the reference's own CPU path: avey_kernels.ops.avey / avey_b with
+    backend='torch' (its _reference: inputs upcast to fp32, dense S) from the
+    unmodified install in baseline/_ref, on CPU tensors of the whole per-GPU
+    batch, with every host core. Returns (tokens/s, steps timed, seconds,
+    threads), or None when baseline/_ref does not import."""
+    try:
+        sys.path.insert(0, str(ROOT / 'baseline' / '_ref'))
+        from avey_kernels import ops as ref_ops
+    except Exception:
+        return None
+    import torch
+    torch.set_num_threads(host_cores())
+    inp = make_inputs(cfg, batch, seed=0)
+    d = cfg['d']
+    # The reference's callers pass the head and tail halves as separate tensors.
+    head, tail = inp['x'][..., :d].contiguous(), inp['x'][..., d:].contiguous()
+
+    def step():
+        with torch.no_grad():
+            if cfg['op'] == 'avey':
+                return ref_ops.avey(tail, inp['w'], z_tl=head, bias=inp['bias'], valid=inp['valid'],
+                                    backend='torch')
+            return ref_ops.avey_b(tail, z_tl=head, bias=inp['bias'], valid=inp['valid'],
+                                  backend='torch')
+
+    for _ in range(max(1, min(warmup, 2))):
+        step()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < steps and (len(times) < 3 or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    return batch * cfg['n'] / statistics.median(times), len(times), sum(times), torch.get_num_threads()
+
+
 def run_reference(args, cfg):
     world, rank, _ = rank_env()
     if rank != 0:
         return 0  # the CPU reference arm runs once, on rank 0
     batch = shard_batch(cfg, world)
     t0 = time.perf_counter()
-    with all_host_threads():
-        value, steps, busy = time_cpu_port(cfg, max_steps=args.steps, warmup=args.warmup, rows=1)
-        cores = cpu_threads()
-    sample = (f'{steps} steps x 1 of {batch} batch rows ({cfg["n"]} tokens) of {args.config}, '
-              f'fp32 NumPy port of avey_kernels/ops.py::_reference (oracle/)')
+    ref = time_reference_torch(cfg, batch, steps=args.steps, warmup=args.warmup)
+    if ref is not None:
+        value, steps, busy, cores = ref
+        kind = 'reference'
+        sample = (f'{steps} timed steps of the whole per-GPU batch ({batch} x {cfg["n"]} tokens) of '
+                  f'{args.config}, {busy:.1f} s: avey_kernels.ops.{cfg["op"]}(..., backend="torch") '
+                  f'from baseline/_ref (the reference\'s _reference, fp32) on CPU tensors')
+        dtype = 'bf16 inputs, f32 arithmetic'
+    else:
+        with all_host_threads():
+            value, steps, busy = time_cpu_port(cfg, max_steps=args.steps, warmup=args.warmup, rows=1)
+            cores = cpu_threads()
+        kind = 'port'
+        sample = (f'{steps} steps x 1 of {batch} batch rows ({cfg["n"]} tokens) of {args.config}, '
+                  f'fp32 NumPy port of avey_kernels/ops.py::_reference (oracle/); baseline/_ref '
+                  f'was not importable')
+        dtype = 'f32'
     line = {
         'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world,
-        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': 1e3 * cfg['n'] / value,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': 1e3 * batch * cfg['n'] / value,
         'higher_is_better': True, 'scaling': cfg['scaling'], 'vs_baseline': None,
-        'dtype': 'f32', 'data': 'synthetic',
+        'dtype': dtype, 'data': 'synthetic',
+        # The same workload as the GPU arm's line: at N GPUs the job is N per-GPU
+        # batches; the host's cores process it at this rate whatever N is.
         'config': {'workload': f'{args.config}: {cfg["desc"]}', 'context': cfg['n'],
                    'features': cfg['d'], 'batch_per_gpu': batch,
-                   'global_batch': batch * world},
-        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                   'global_batch': batch * world, 'parallelism': f'host CPU, {cores} threads'},
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': kind,
                          'sample': sample},
         'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
         'wall_s': time.perf_counter() - t0,
@@ -381,9 +437,9 @@ def run_ours(args, cfg):
     verify_err = max_over_ranks(verify_err, device=dev)
     plan = ops.plan(sets[0]['x'][..., d:], sets[0]['w'], sets[0]['x'][..., :d], sets[0]['bias'],
                     sets[0]['valid'], causal=cfg['op'] == 'avey', normalize=cfg['op'] != 'avey')
-    kernel_name = {1: 'simt_contextualize', 2: 'tc_contextualize'}[plan.kernel]
+    kernel_name = {1: 'simt_contextualize', 2: 'norm_prepass + tc_contextualize (whole step)'}[plan.kernel]
     if plan.kernel == 2 and plan.launches == 3:  # contexts above 512: two tensor-core kernels
-        kernel_name = 'tc_gram_p + tc_pv (whole step)'
+        kernel_name = 'norm_prepass + tc_gram_p + tc_pv (whole step)'
 
     # Warm-up (untimed), then capture chunks of steps into CUDA graphs.
     for i in range(max(args.warmup, 3)):
@@ -499,6 +555,43 @@ def run_ours(args, cfg):
     assert torch.isfinite(out_host[(e2e_steps - 1) % 2].float()).all()
     e2e_value = tokens_per_step / (e2e_ms / 1e3)
 
+    # The copy ceiling of that pipeline: the same pinned copies with no
+    # compute, both directions at once on their streams, on every rank at once
+    # (ranks share the host's memory and PCIe); and each direction alone.
+    o_dev = [torch.empty(out_host[0].shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+
+    def copy_run(n, h2d_on=True, d2h_on=True):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(s_cmp)
+        s_in.wait_stream(s_cmp)
+        s_out.wait_stream(s_cmp)
+        for i in range(n):
+            k = i % 2
+            if h2d_on:
+                with torch.cuda.stream(s_in):
+                    for dst, src in zip(dev_bufs[k], hosts):
+                        if src is not None:
+                            dst.copy_(src, non_blocking=True)
+            if d2h_on:
+                with torch.cuda.stream(s_out):
+                    out_host[k].copy_(o_dev[k], non_blocking=True)
+        s_cmp.wait_stream(s_in)
+        s_cmp.wait_stream(s_out)
+        b.record(s_cmp)
+        return a, b
+
+    copy_ms = {}
+    for name, kw in (('both', {}), ('h2d', dict(d2h_on=False)), ('d2h', dict(h2d_on=False))):
+        copy_run(2, **kw)
+        torch.cuda.synchronize()
+        barrier()
+        a, b = copy_run(e2e_steps, **kw)
+        torch.cuda.synchronize()
+        barrier()
+        copy_ms[name] = max_over_ranks(a.elapsed_time(b) / e2e_steps, device=dev)
+    ceiling_ms = max(copy_ms['both'], ms_step)
+
     # Roofline of the dominant (only) kernel.
     nbytes, flops = algorithmic(cfg, batch, sets[0]['valid'])
     t_launch = ms_step / 1e3
@@ -519,7 +612,8 @@ def run_ours(args, cfg):
     else:
         roof = {'bound': 'tensor', 'achieved': tflops, 'peak': peaks['bf16_tflops'],
                 'unit': 'TFLOP/s', 'frac': tflops / peaks['bf16_tflops']}
-    roof.update({'traffic': traffic, 'kernel': kernel_name, 'peak_source': peaks['source'],
+    roof.update({'traffic': traffic, 'traffic_ratio': traffic / nbytes if traffic else None,
+                 'kernel': kernel_name, 'peak_source': peaks['source'],
                  'algorithmic_bytes': nbytes, 'useful_flops': flops,
                  'hbm_frac': gbs / peaks['hbm_gbs'], 'tensor_frac': tflops / peaks['bf16_tflops'],
                  'tensor_tflops': tflops, 'binding_floor_us': 1e6 * max(hbm_time, tc_time),
@@ -559,7 +653,17 @@ def run_ours(args, cfg):
             'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': h2d * world,
                     'd2h_bytes_per_step': d2h * world, 'ms_per_step': e2e_ms,
                     'pipelining': 'copy-in of step i+1, compute of step i and copy-out of step i-1 overlap (3 streams, 2 buffer sets)',
-                    'api': f'avey_kernel_b200.{cfg["op"]} (pinned host buffers)'},
+                    'api': f'avey_kernel_b200.{cfg["op"]} (pinned host buffers)',
+                    'copy_ceiling': {
+                        'how': 'the same pinned copies per step with no compute, max over ranks '
+                               '(all ranks copying at once); ceiling = max(both directions, '
+                               'device step)',
+                        'ms_per_step_both': copy_ms['both'], 'ms_per_step_h2d': copy_ms['h2d'],
+                        'ms_per_step_d2h': copy_ms['d2h'],
+                        'h2d_gbs_per_rank': h2d / (copy_ms['h2d'] / 1e3) / 1e9,
+                        'd2h_gbs_per_rank': d2h / (copy_ms['d2h'] / 1e3) / 1e9,
+                        'value': tokens_per_step / (ceiling_ms / 1e3),
+                        'e2e_frac_of_ceiling': ceiling_ms / e2e_ms}},
             'roofline': roof,
             'cpu_baseline': cpu,
             'clocks': clocks.summary(),

@@ -34,8 +34,13 @@ def test_reference_arm_prints_one_json_line_with_the_contract_keys():
         assert key in line, key
     assert line['impl'] == 'reference' and line['value'] > 0 and line['higher_is_better']
     assert line['e2e']['h2d_bytes_per_step'] == 0 and line['e2e']['value'] == line['value']
-    assert line['cpu_baseline']['kind'] == 'port' and line['cpu_baseline']['cores'] >= 1
+    # The reference's own CPU path when its unmodified install is importable,
+    # else the NumPy port of it.
+    ref_installed = (ROOT / 'baseline' / '_ref' / 'avey_kernels' / 'ops.py').exists()
+    assert line['cpu_baseline']['kind'] == ('reference' if ref_installed else 'port')
+    assert line['cpu_baseline']['cores'] >= 1
     assert line['config']['workload'].startswith('c2:')
+    assert line['config']['global_batch'] == 64
 
 
 def test_algorithmic_bytes_and_flops_of_config_2():
