@@ -179,9 +179,17 @@ bool is_long(const AveyFwdParams* p) { return p->context > avey::kTcMaxKeys; }
 // Long-context path: grid shapes, shared memory and the workspace layout
 // [row sums of squares | partial row sums of P | P (bf16/f16, rows padded to
 // 64 elements)], each part 256-byte aligned.
+// P workspace of one batch slice of the long path. Slices of 32 MB (P read
+// back from L2, DRAM traffic 367 -> 292 MB at config 4) measured slower (227
+// against 193 us: eight smaller launches with their tails), so a slice holds
+// up to 256 MB: config 4 runs as one slice, and only larger batches are cut
+// into slices, which also bounds the workspace.
+constexpr uint64_t kLongSliceBytes = 256ull << 20;
+
 struct LongLayout {
   avey::LongGeom geom;
   int gp_items;
+  int slice_rows;  // batch rows per G/P + P.Z launch pair
   int smem_gp, smem_pv;
   uint64_t off_den, off_p, total;
 };
@@ -204,9 +212,12 @@ LongLayout long_layout(const AveyFwdParams* p) {
   const int64_t cp = (C + 63) / 64 * 64;
   l.geom.p_rs = cp;
   l.geom.p_bs = C * cp;
+  const uint64_t p_row_bytes = static_cast<uint64_t>(C * cp) * 2u;
+  l.slice_rows = static_cast<int>(std::max<uint64_t>(
+      1, std::min<uint64_t>(static_cast<uint64_t>(B), kLongSliceBytes / p_row_bytes)));
   l.off_den = align256(static_cast<uint64_t>(B * C) * sizeof(float));
   l.off_p = l.off_den + align256(static_cast<uint64_t>(B * l.geom.n_groups * C) * sizeof(float));
-  l.total = l.off_p + static_cast<uint64_t>(B * C * cp) * 2u;
+  l.total = l.off_p + static_cast<uint64_t>(l.slice_rows) * p_row_bytes;
   l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes + avey::kLgCtrlBytes;
   l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes + avey::kPvCtrlBytes;
   return l;
@@ -364,49 +375,67 @@ int launch_long(const AveyFwdParams* p, cudaStream_t stream) {
                 "the long-context tcgen05 path needs a 256-byte aligned workspace of %llu bytes",
                 (unsigned long long)l.total);
   uint8_t* ws = static_cast<uint8_t*>(p->workspace);
-  l.geom.den_part = reinterpret_cast<float*>(ws + l.off_den);
+  float* den_base = reinterpret_cast<float*>(ws + l.off_den);
   void* pbuf = ws + l.off_p;
-  const uint64_t C = static_cast<uint64_t>(p->context), B = static_cast<uint64_t>(p->batch);
+  const uint64_t C = static_cast<uint64_t>(p->context);
   const uint64_t prow = static_cast<uint64_t>(l.geom.p_rs) * 2u, pbat = static_cast<uint64_t>(l.geom.p_bs) * 2u;
-  CUtensorMap map_k, map_pst, map_p, map_z, map_o;
-  int rc = encode_map(p, p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride, avey::kTcChunk, 128, &map_k);
-  if (rc == AVEY_OK) rc = encode_map_dims(p->dtype, pbuf, C, C, B, prow, pbat, 32, 32, &map_pst);
-  if (rc == AVEY_OK) rc = encode_map_dims(p->dtype, pbuf, C, C, B, prow, pbat, 64, 128, &map_p);
-  if (rc == AVEY_OK)
-    rc = encode_map(p, p->z_tr, p->z_tr_batch_stride, p->z_tr_row_stride, 64, avey::kPvChunkKeys, &map_z);
-  if (rc == AVEY_OK) rc = encode_map(p, p->out, p->out_batch_stride, p->out_row_stride, 32, 32, &map_o);
-  if (rc != AVEY_OK) return rc;
-  const avey::FwdArgs args = make_args(p);
-  // 1. Row sums of squares.
+  const avey::FwdArgs all = make_args(p);
+  // 1. Row sums of squares of every row.
   const int rows = static_cast<int>(p->batch * p->context);
   const int pre_blocks = std::min(148 * 8, (rows + 7) / 8);
-  avey::norm_prepass<T><<<pre_blocks, avey::kPrepassThreads, 0, stream>>>(args);
+  avey::norm_prepass<T><<<pre_blocks, avey::kPrepassThreads, 0, stream>>>(all);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "norm pre-pass launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
-  // 2. G and P per (query tile, key group), a programmatic dependent of the
-  //    pre-pass (it waits for the sums only before forming P).
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(l.gp_items), static_cast<unsigned>(p->batch));
-  cfg.blockDim = dim3(avey::kLgThreads);
-  cfg.dynamicSmemBytes = static_cast<size_t>(l.smem_gp);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, avey::tc_gram_p<T>, args, map_k, map_pst, l.geom);
-  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_gram_p launch: %s", cudaGetErrorString(e));
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  // 3. O = P Z and the epilogue, in plain stream order after tc_gram_p.
-  avey::tc_pv<T, ACT><<<dim3(static_cast<unsigned>(l.geom.n_qtiles * l.geom.n_fgroups),
-                             static_cast<unsigned>(p->batch)),
-                        avey::kPvThreads, static_cast<size_t>(l.smem_pv), stream>>>(
-      args, map_p, map_z, map_o, l.geom);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_pv launch: %s", cudaGetErrorString(e));
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+  // 2./3. Per batch slice: G and P per (query tile, key group) into the P
+  // workspace (written with an L2 evict-last hint), then O = P Z and the
+  // epilogue; a slice's P is small enough to be read back from L2.
+  const int es = elem_size(p->dtype);
+  for (int64_t b0 = 0; b0 < p->batch; b0 += l.slice_rows) {
+    AveyFwdParams q = *p;
+    q.batch = std::min<int64_t>(l.slice_rows, p->batch - b0);
+    q.z_tr = static_cast<const uint8_t*>(p->z_tr) + b0 * p->z_tr_batch_stride * es;
+    if (p->z_tl) q.z_tl = static_cast<const uint8_t*>(p->z_tl) + b0 * p->z_tl_batch_stride * es;
+    q.out = static_cast<uint8_t*>(p->out) + b0 * p->out_batch_stride * es;
+    if (p->valid) q.valid = p->valid + b0 * p->valid_batch_stride;
+    if (p->lengths) q.lengths = p->lengths + b0;
+    const uint64_t nb = static_cast<uint64_t>(q.batch);
+    CUtensorMap map_k, map_pst, map_p, map_z, map_o;
+    int rc = encode_map(&q, q.z_tr, q.z_tr_batch_stride, q.z_tr_row_stride, avey::kTcChunk, 128, &map_k);
+    if (rc == AVEY_OK) rc = encode_map_dims(q.dtype, pbuf, C, C, nb, prow, pbat, 32, 32, &map_pst);
+    if (rc == AVEY_OK) rc = encode_map_dims(q.dtype, pbuf, C, C, nb, prow, pbat, 64, 128, &map_p);
+    if (rc == AVEY_OK)
+      rc = encode_map(&q, q.z_tr, q.z_tr_batch_stride, q.z_tr_row_stride, 64, avey::kPvChunkKeys, &map_z);
+    if (rc == AVEY_OK) rc = encode_map(&q, q.out, q.out_batch_stride, q.out_row_stride, 32, 32, &map_o);
+    if (rc != AVEY_OK) return rc;
+    avey::FwdArgs args = make_args(&q);
+    args.sumsq = all.sumsq + b0 * static_cast<int64_t>(C);
+    avey::LongGeom geom = l.geom;
+    geom.den_part = den_base + b0 * geom.n_groups * static_cast<int64_t>(C);
+    // The first slice's G/P launch is a programmatic dependent of the pre-pass
+    // (it waits for the sums only before forming P); later ones follow in
+    // plain stream order.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(l.gp_items), static_cast<unsigned>(q.batch));
+    cfg.blockDim = dim3(avey::kLgThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(l.smem_gp);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = b0 == 0 ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, avey::tc_gram_p<T>, args, map_k, map_pst, geom);
+    if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_gram_p launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    avey::tc_pv<T, ACT><<<dim3(static_cast<unsigned>(geom.n_qtiles * geom.n_fgroups),
+                               static_cast<unsigned>(q.batch)),
+                          avey::kPvThreads, static_cast<size_t>(l.smem_pv), stream>>>(
+        args, map_p, map_z, map_o, geom);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_pv launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  }
   return ok();
 }
 
@@ -533,8 +562,9 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
   if (reason == kReasonNone && is_long(p)) {
     const LongLayout l = long_layout(p);
     plan->kernel = AVEY_KERNEL_TCGEN05;
-    plan->launches = 3;
-    plan->grid = static_cast<int32_t>(p->batch * l.gp_items);
+    // The pre-pass, then a G/P + P.Z launch pair per batch slice.
+    plan->launches = 1 + 2 * static_cast<int32_t>((p->batch + l.slice_rows - 1) / l.slice_rows);
+    plan->grid = static_cast<int32_t>(std::min<int64_t>(p->batch, l.slice_rows) * l.gp_items);
     plan->block = avey::kLgThreads;
     plan->smem_bytes = std::max(l.smem_gp, l.smem_pv);
   } else if (reason == kReasonNone) {

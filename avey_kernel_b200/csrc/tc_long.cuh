@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(kLgThreads, 2)
         __syncwarp();
         if (key0 + c0 < C && i0 < C)  // the box holds some of the tensor
           warp_tile_store(stage0 + (ch & 1) * kTcOutTileBytes, pk, &map_pst, key0 + c0, i0, b,
-                          stream, lane);
+                          keep, lane);  // P is read back by tc_pv soon: keep it in L2
         if (vrow) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) {

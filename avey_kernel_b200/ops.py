@@ -8,7 +8,10 @@ Same signatures, tensor conventions and errors as the reference
   native backward (``backward.py``); the reference has none and sends them to
   its PyTorch path (ops.py:94-106).
 * ``'triton'`` accepted for source compatibility: it names the fused GPU
-  kernel, which here is the native CUDA one (same rules as ``'cuda'``).
+  kernel, which here is the native CUDA one, under the reference's rules for
+  that backend (ops.py:98-103): CUDA fp16 / bf16 / fp32 inference inputs only,
+  so fp64 inputs, CPU tensors and inputs that require grad raise
+  ``ValueError`` as they do in the reference.
 * ``'torch'`` the differentiable PyTorch path (``eager.py``).
 * ``'auto'``  ``'cuda'`` for CUDA tensors, with or without autograd; the
   PyTorch path for CPU tensors.
@@ -236,7 +239,14 @@ def _dispatch(z_tr, v, z_tl, bias, valid, eps, norm_eps, causal, normalize, acti
     _validate(z_tr, v, z_tl, bias, valid, eps, norm_eps, activation, backend, output_tile,
               autotune)
     native_ok = z_tr.is_cuda and torch.version.hip is None
-    if backend in ('cuda', 'triton') and not native_ok:
+    if backend == 'triton':
+        # The reference's conditions for its fused-kernel backend (ops.py:96-103).
+        needs_grad = torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (z_tr, v, z_tl, bias))
+        if not native_ok or z_tr.dtype == torch.float64 or needs_grad:
+            raise ValueError('Triton requires Triton installed, NVIDIA SM80+, and CUDA '
+                             'FP16/BF16/FP32 inference inputs; use backend="torch" for autograd')
+    if backend == 'cuda' and not native_ok:
         raise ValueError('the CUDA backend needs CUDA tensors; use backend="torch" for CPU tensors')
     if backend == 'torch' or not native_ok:
         return eager.contextualize(z_tr, v, z_tl, bias, valid, eps=eps, norm_eps=norm_eps,

@@ -3,6 +3,7 @@ path, and custom-op tracing without a GPU (mirrors the reference's
 tests/test_contextualizer.py, tests/test_symbolic_tile.py and
 tests/test_autotune.py:25-45)."""
 
+import io
 import subprocess
 import sys
 from pathlib import Path
@@ -110,12 +111,54 @@ def test_auto_backend_preserves_autograd_on_cpu():
     torch.testing.assert_close(out, avey_b(x, backend='torch'))
 
 
-@pytest.mark.parametrize('backend', ['cuda', 'triton'])
-def test_native_backend_rejects_cpu_inputs(backend):
+def test_native_backend_rejects_cpu_inputs():
     with pytest.raises(ValueError, match='CUDA tensors'):
-        avey_b(torch.rand(1, 5, 8), backend=backend)
+        avey_b(torch.rand(1, 5, 8), backend='cuda')
     with pytest.raises(ValueError, match='CUDA tensors'):
-        avey_b(torch.rand(1, 5, 8, requires_grad=True), backend=backend)
+        avey_b(torch.rand(1, 5, 8, requires_grad=True), backend='cuda')
+
+
+def test_triton_backend_keeps_the_reference_rules_on_cpu():
+    # The reference's backend='triton' wants CUDA fp16/bf16/fp32 inference
+    # inputs (ops.py:96-103) and raises ValueError otherwise.
+    with pytest.raises(ValueError, match='inference inputs'):
+        avey_b(torch.rand(1, 5, 8), backend='triton')
+    with pytest.raises(ValueError, match='inference inputs'):
+        avey_b(torch.rand(1, 5, 8, requires_grad=True), backend='triton')
+
+
+REFERENCE_TESTS = Path('/root/reference/tests/test_contextualizer.py')
+
+
+@pytest.mark.skipif(not REFERENCE_TESTS.exists(), reason='the reference checkout is not mounted')
+def test_the_reference_contract_tests_pass_against_this_package():
+    # Runs the reference's own public-API tests (tests/test_contextualizer.py:
+    # orientation, ordering, padding, signed sums, gradients, NaN padding, the
+    # input contract, autograd under 'auto') with `avey_kernels` bound to this
+    # package, on CPU tensors.
+    import importlib.util
+    import types
+    import unittest
+
+    import avey_kernel_b200
+    shim = types.ModuleType('avey_kernels')
+    shim.avey, shim.avey_b = avey_kernel_b200.avey, avey_kernel_b200.avey_b
+    saved = sys.modules.get('avey_kernels')
+    sys.modules['avey_kernels'] = shim
+    try:
+        spec = importlib.util.spec_from_file_location('reference_test_contextualizer',
+                                                      REFERENCE_TESTS)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        suite = unittest.defaultTestLoader.loadTestsFromModule(mod)
+        result = unittest.TextTestRunner(stream=io.StringIO(), verbosity=0).run(suite)
+    finally:
+        if saved is None:
+            sys.modules.pop('avey_kernels', None)
+        else:
+            sys.modules['avey_kernels'] = saved
+    assert result.testsRun >= 8
+    assert result.wasSuccessful(), [str(f[1])[-400:] for f in result.failures + result.errors]
 
 
 @pytest.mark.parametrize('case', CASES, ids=[c['name'] for c in CASES])

@@ -2,9 +2,10 @@
 
 * every golden case (reference outputs) through the public API, with the
   kernel the library picks and with each kernel forced where it applies;
-* BASELINE-sized configs: sampled batch rows against the fp64 oracle, the
-  rest through size-independent properties (exact scaling, determinism,
-  batch-permutation equivariance, shard consistency);
+* BASELINE-sized configs (2, 3, a config-5 shard, 4): every batch row against
+  the oracle with the reference's fp32 accumulation, and size-independent
+  properties (exact scaling, determinism, batch-permutation equivariance,
+  shard consistency);
 * that CUDA inference calls really launch the native kernels.
 
 Tolerances (north-star spec, norm-wise max relative error vs the fp64
@@ -115,8 +116,19 @@ def _config(name, seed=0):
     return x[..., :d], x[..., d:], w, bias, lengths
 
 
+def _elementwise_ratio(y, ref, scale, rtol=2e-2, atol_frac=1e-2):
+    """max over elements of |y - r| / (atol + rtol |r|), atol = atol_frac * max |r|
+    of the row (the floor for elements near zero, where the signed Avey-B sums
+    cancel): <= 1 means every element is within the elementwise tolerance."""
+    return float(np.max(np.abs(y - ref) / (atol_frac * scale + rtol * np.abs(ref))))
+
+
 @pytest.mark.parametrize('name', ['c2', 'c3', 'c5shard'])
-def test_baseline_sized_config_rows_match_oracle(name):
+def test_baseline_sized_config_every_row_matches_oracle(name):
+    """Every batch row of the full-size config against the oracle with the
+    reference's own accumulation (fp32 for 16-bit inputs, ops.py:62-63),
+    norm-wise per row; c3 (signed Avey-B sums near zero) also elementwise
+    with an atol floor."""
     head, tail, w, bias, lengths = _config(name)
     b, n, _ = tail.shape
     if name == 'c3':
@@ -131,16 +143,23 @@ def test_baseline_sized_config_rows_match_oracle(name):
     torch.cuda.synchronize()
     y = to_numpy(out)
     assert np.isfinite(y).all()
-    rows = [0, 1, b // 2, b - 1]
-    for r in rows:
-        zt = to_numpy(tail[r:r + 1])
-        zl = to_numpy(head[r:r + 1])
-        if name == 'c3':
-            ref = oracle.avey_b(zt, z_tl=zl, valid=to_numpy(valid[r:r + 1].float()) > 0)
-        else:
-            ref = oracle.avey(zt, to_numpy(w), z_tl=zl, bias=to_numpy(bias))
-        err = norm_rel_err(y[r:r + 1], ref)
-        assert err <= TOL['bfloat16'], (name, r, err)
+    zt, zl = to_numpy(tail), to_numpy(head)
+    if name == 'c3':
+        ok = to_numpy(valid.float()) > 0
+        ref = oracle.avey_b(zt, z_tl=zl, valid=ok, accum=np.float32)
+        assert (y[~ok] == 0).all()  # padded rows are exactly zero
+    else:
+        ref = oracle.avey(zt, to_numpy(w), z_tl=zl, bias=to_numpy(bias), accum=np.float32)
+    errs = [norm_rel_err(y[r], ref[r]) for r in range(b)]
+    worst = int(np.argmax(errs))
+    print(f'{name}: {b} rows, norm-wise max {errs[worst]:.2e} (row {worst}), '
+          f'median {float(np.median(errs)):.2e}')
+    assert max(errs) <= TOL['bfloat16'], (name, worst, errs[worst])
+    if name == 'c3':
+        ratios = [_elementwise_ratio(y[r], ref[r], float(np.max(np.abs(ref[r]))) or 1.0)
+                  for r in range(b)]
+        print(f'c3 elementwise: max |y - r| / (1e-2 max|r| + 2e-2 |r|) = {max(ratios):.3f}')
+        assert max(ratios) <= 1.0
 
 
 def test_exact_properties_at_full_size():
@@ -158,11 +177,14 @@ def test_exact_properties_at_full_size():
 
 
 @pytest.mark.parametrize('name', ['c4', 'b1000', 'f16_1536'])
-def test_long_context_rows_match_oracle(name):
-    """Contexts above 512: pre-pass, G/P per key group into the workspace, O = P Z."""
+def test_long_context_every_row_matches_oracle(name):
+    """Contexts above 512: pre-pass, G/P per key group into the workspace, O = P Z.
+    c4 is BASELINE config 4 at its full batch of 16 (5% of rows scaled x50),
+    every row checked against the oracle (fp32 accumulation, as the reference
+    does for 16-bit inputs), four rows at a time."""
     g = torch.Generator(device='cpu').manual_seed(4)
-    if name == 'c4':  # BASELINE config 4 at two batch rows: 5% of rows scaled x50
-        b, n, d, dt = 2, 2048, 1024, torch.bfloat16
+    if name == 'c4':
+        b, n, d, dt = 16, 2048, 1024, torch.bfloat16
     elif name == 'b1000':
         b, n, d, dt = 3, 1000, 384, torch.bfloat16
     else:
@@ -185,20 +207,26 @@ def test_long_context_rows_match_oracle(name):
         out = avey(tail, w, z_tl=head, activation=act)
         plan = ops.plan(tail, w, z_tl=head)
     torch.cuda.synchronize()
-    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.launches == 3
+    # The pre-pass, then a G/P + P.Z launch pair per batch slice (one slice
+    # here: a slice's P workspace holds up to 256 MB).
+    slices = 1
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.launches == 1 + 2 * slices
     assert _native.launch_count() == before + plan.launches
     y = to_numpy(out)
     assert np.isfinite(y).all()
-    for r in sorted({0, b - 1}):
-        zt, zl = to_numpy(tail[r:r + 1]), to_numpy(head[r:r + 1])
+    errs = []
+    for r0 in range(0, b, 4):
+        sl = slice(r0, min(b, r0 + 4))
+        zt, zl = to_numpy(tail[sl]), to_numpy(head[sl])
         if name == 'b1000':
-            ok = to_numpy(valid[r:r + 1].float()) > 0
-            ref = oracle.avey_b(zt, z_tl=zl, valid=ok, activation='gelu')
-            assert (y[r:r + 1][~ok] == 0).all()
+            ok = to_numpy(valid[sl].float()) > 0
+            ref = oracle.avey_b(zt, z_tl=zl, valid=ok, activation='gelu', accum=np.float32)
+            assert (y[sl][~ok] == 0).all()
         else:
-            ref = oracle.avey(zt, to_numpy(w), z_tl=zl, activation=act)
-        err = norm_rel_err(y[r:r + 1], ref)
-        assert err <= TOL['bfloat16'], (name, r, err)
+            ref = oracle.avey(zt, to_numpy(w), z_tl=zl, activation=act, accum=np.float32)
+        errs += [norm_rel_err(y[sl][i], ref[i]) for i in range(ref.shape[0])]
+    print(f'{name}: {b} rows, norm-wise max {max(errs):.2e}')
+    assert max(errs) <= TOL['bfloat16'], (name, int(np.argmax(errs)), max(errs))
 
 
 def test_long_context_exact_properties():
@@ -300,6 +328,23 @@ def test_long_context_batch_slices_under_a_workspace_cap(monkeypatch):
     assert torch.equal(sliced, whole)
 
 
+def test_long_context_runs_batch_slices_inside_one_call():
+    """The library runs the long path's G/P and P.Z kernels per batch slice whose
+    P workspace holds up to 256 MB: at 8192 tokens (128 MB of P per row) a
+    batch of 3 runs as two slices, and matches running the rows one at a time."""
+    g = torch.Generator(device='cpu').manual_seed(17)
+    x = torch.randn(3, 8192, 2 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    head, tail = x[..., :64], x[..., 64:]
+    plan = ops.plan(tail, z_tl=head, causal=False, normalize=True)
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.launches == 1 + 2 * 2
+    before = _native.launch_count()
+    whole = avey_b(tail, z_tl=head)
+    torch.cuda.synchronize()
+    assert _native.launch_count() == before + plan.launches
+    for r in range(3):
+        assert torch.equal(whole[r:r + 1], avey_b(tail[r:r + 1], z_tl=head[r:r + 1]))
+
+
 def test_noncontiguous_and_strided_views():
     z = torch.rand(2, 37, 35, device=DEV).transpose(1, 2)
     ref = oracle.avey_b(to_numpy(z))
@@ -357,6 +402,23 @@ def test_autograd_inputs_run_the_native_backward():
     z.grad = None
     avey_b(z, backend='cuda').sum().backward()
     assert z.grad is not None
+
+
+def test_noncontiguous_inputs_and_the_triton_backend_rules():
+    # The reference's CUDA integration test (tests/test_triton.py:217-228): a
+    # transposed view matches the PyTorch path, autograd under 'auto' works,
+    # and backend='triton' refuses inputs that require grad; fp64 too.
+    z = torch.rand(2, 37, 35, device=DEV).transpose(1, 2)
+    torch.testing.assert_close(avey_b(z), avey_b(z, backend='torch'), atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(avey_b(z, backend='triton'), avey_b(z, backend='torch'), atol=1e-5,
+                               rtol=1e-5)
+    z.requires_grad_()
+    avey_b(z).sum().backward()
+    assert z.grad is not None
+    with pytest.raises(ValueError):
+        avey_b(z, backend='triton')
+    with pytest.raises(ValueError):
+        avey_b(torch.rand(1, 8, 8, device=DEV, dtype=torch.float64), backend='triton')
 
 
 @pytest.mark.parametrize('n', [512, 900], ids=['fused', 'long'])
