@@ -21,6 +21,7 @@
 #include "simt2_kernel.cuh"
 #include "tc_kernel.cuh"
 #include "tc_long.cuh"
+#include "tc_tf32.cuh"
 
 namespace {
 
@@ -46,7 +47,7 @@ int ok() {
 
 enum Reason {
   kReasonNone = 0,
-  kReasonDtype = 1,      // tcgen05 kernel needs bf16 or f16
+  kReasonDtype = 1,      // tcgen05 kernels take bf16, f16 and fp32 (3xTF32)
   kReasonContext = 2,    // more than 8192 tokens per row (or more than 512 without a workspace)
   kReasonAlignment = 3,  // base / strides not 16-byte aligned (TMA, vector I/O)
   kReasonForced = 4,     // caller asked for the CUDA-core kernel
@@ -137,15 +138,18 @@ cudaError_t smem_opt_in(int bytes) {
 // `allow_long` is false for the no-allocation entry point.
 int tc_reason(const AveyFwdParams* p, bool allow_long = true) {
   if (p->kernel == AVEY_KERNEL_SIMT) return kReasonForced;
-  if (p->dtype != AVEY_BF16 && p->dtype != AVEY_F16) return kReasonDtype;
+  if (p->dtype != AVEY_BF16 && p->dtype != AVEY_F16 && p->dtype != AVEY_F32) return kReasonDtype;
   if (p->context > (allow_long ? avey::kLongMaxContext : avey::kTcMaxKeys)) return kReasonContext;
   if (p->features > avey::kTcMaxFeatures) return kReasonFeatures;
+  // Elements per 16 bytes: rows, batch strides and the feature count must be
+  // whole 16-byte units (TMA strides, vector loads of the gate).
+  const int64_t u = 16 / elem_size(p->dtype);
   const bool a = aligned16(p->z_tr) && aligned16(p->out) && (!p->z_tl || aligned16(p->z_tl)) &&
-                 (p->z_tr_row_stride % 8 == 0) && (p->out_row_stride % 8 == 0) &&
-                 (p->z_tr_batch_stride % 8 == 0 || p->batch == 1) &&
-                 (p->out_batch_stride % 8 == 0 || p->batch == 1) && (p->features % 8 == 0) &&
-                 (!p->z_tl || ((p->z_tl_row_stride % 8 == 0) &&
-                               (p->z_tl_batch_stride % 8 == 0 || p->batch == 1)));
+                 (p->z_tr_row_stride % u == 0) && (p->out_row_stride % u == 0) &&
+                 (p->z_tr_batch_stride % u == 0 || p->batch == 1) &&
+                 (p->out_batch_stride % u == 0 || p->batch == 1) && (p->features % u == 0) &&
+                 (!p->z_tl || ((p->z_tl_row_stride % u == 0) &&
+                               (p->z_tl_batch_stride % u == 0 || p->batch == 1)));
   if (!a) return kReasonAlignment;
   return kReasonNone;
 }
@@ -175,6 +179,11 @@ TcLayout tc_layout(const AveyFwdParams* p) {
 }
 
 bool is_long(const AveyFwdParams* p) { return p->context > avey::kTcMaxKeys; }
+
+// Inputs that run a kernel pair with a P workspace (G/P, then P.Z): 16-bit
+// rows above 512 tokens, and every fp32 input (3xTF32 kernels).
+bool is_pair(const AveyFwdParams* p) { return is_long(p) || p->dtype == AVEY_F32; }
+bool is_tf32(const AveyFwdParams* p) { return p->dtype == AVEY_F32; }
 
 // Long-context path: grid shapes, shared memory and the workspace layout
 // [row sums of squares | partial row sums of P | P (bf16/f16, rows padded to
@@ -212,14 +221,21 @@ LongLayout long_layout(const AveyFwdParams* p) {
   const int64_t cp = (C + 63) / 64 * 64;
   l.geom.p_rs = cp;
   l.geom.p_bs = C * cp;
-  const uint64_t p_row_bytes = static_cast<uint64_t>(C * cp) * 2u;
+  const uint64_t p_es = is_tf32(p) ? 4u : 2u;  // P is fp32 on the 3xTF32 path
+  const uint64_t p_row_bytes = static_cast<uint64_t>(C * cp) * p_es;
   l.slice_rows = static_cast<int>(std::max<uint64_t>(
       1, std::min<uint64_t>(static_cast<uint64_t>(B), kLongSliceBytes / p_row_bytes)));
   l.off_den = align256(static_cast<uint64_t>(B * C) * sizeof(float));
   l.off_p = l.off_den + align256(static_cast<uint64_t>(B * l.geom.n_groups * C) * sizeof(float));
   l.total = l.off_p + static_cast<uint64_t>(l.slice_rows) * p_row_bytes;
-  l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes + avey::kLgCtrlBytes;
-  l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes + avey::kPvCtrlBytes;
+  if (is_tf32(p)) {
+    l.geom.n_fgroups = static_cast<int>((D + avey::kTfPvCols - 1) / avey::kTfPvCols);
+    l.smem_gp = 1024 + avey::kTfStages * avey::kTfGramStage + avey::kTfCtrlBytes;
+    l.smem_pv = 1024 + avey::kTfStages * avey::kTfPvStage + avey::kTfCtrlBytes;
+  } else {
+    l.smem_gp = 1024 + avey::kLgStages * avey::kLgStageBytes + avey::kLgCtrlBytes;
+    l.smem_pv = 1024 + avey::kPvStages * avey::kPvStageBytes + avey::kPvCtrlBytes;
+  }
   return l;
 }
 
@@ -323,8 +339,9 @@ int encode_cached(int dtype, const void* base, const cuuint64_t (&dims)[3], cons
   const CUtensorMapSwizzle swz =
       box_cols * es == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapDataType dt =
-      dtype == AVEY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = dtype == AVEY_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : dtype == AVEY_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
   cuuint64_t st[2] = {strides[0], strides[1]};
   const CUresult r = fn(map, dt, 3, const_cast<void*>(base), d, st, box, estr,
@@ -437,6 +454,72 @@ int launch_long(const AveyFwdParams* p, cudaStream_t stream) {
     g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   return ok();
+}
+
+// fp32 inputs: per batch slice, tf_gram_p (G in 3xTF32 with the row norms
+// from its own split, P as fp32 into the workspace) then tf_pv (O = P Z in
+// 3xTF32 and the epilogue). No pre-pass: the split sums the squares.
+template <int ACT>
+int launch_tf32(const AveyFwdParams* p, cudaStream_t stream) {
+  cudaError_t attr_err = smem_opt_in<avey::tf_gram_p>(kMaxDynSmem);
+  if (attr_err == cudaSuccess) attr_err = smem_opt_in<avey::tf_pv<ACT>>(kMaxDynSmem);
+  if (attr_err != cudaSuccess)
+    return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  LongLayout l = long_layout(p);
+  if (!p->workspace || p->workspace_bytes < l.total ||
+      (reinterpret_cast<uintptr_t>(p->workspace) & 255u))
+    return fail(AVEY_ERR_ARGUMENT,
+                "the fp32 tcgen05 path needs a 256-byte aligned workspace of %llu bytes",
+                (unsigned long long)l.total);
+  uint8_t* ws = static_cast<uint8_t*>(p->workspace);
+  float* den_base = reinterpret_cast<float*>(ws + l.off_den);
+  void* pbuf = ws + l.off_p;
+  const uint64_t C = static_cast<uint64_t>(p->context);
+  const uint64_t prow = static_cast<uint64_t>(l.geom.p_rs) * 4u, pbat = static_cast<uint64_t>(l.geom.p_bs) * 4u;
+  for (int64_t b0 = 0; b0 < p->batch; b0 += l.slice_rows) {
+    AveyFwdParams q = *p;
+    q.batch = std::min<int64_t>(l.slice_rows, p->batch - b0);
+    q.z_tr = static_cast<const float*>(p->z_tr) + b0 * p->z_tr_batch_stride;
+    if (p->z_tl) q.z_tl = static_cast<const float*>(p->z_tl) + b0 * p->z_tl_batch_stride;
+    q.out = static_cast<float*>(p->out) + b0 * p->out_batch_stride;
+    if (p->valid) q.valid = p->valid + b0 * p->valid_batch_stride;
+    if (p->lengths) q.lengths = p->lengths + b0;
+    const uint64_t nb = static_cast<uint64_t>(q.batch);
+    CUtensorMap map_k, map_pst, map_p, map_z, map_o;
+    int rc = encode_map(&q, q.z_tr, q.z_tr_batch_stride, q.z_tr_row_stride, avey::kTfChunk, 128, &map_k);
+    if (rc == AVEY_OK) rc = encode_map_dims(AVEY_F32, pbuf, C, C, nb, prow, pbat, 32, 32, &map_pst);
+    if (rc == AVEY_OK) rc = encode_map_dims(AVEY_F32, pbuf, C, C, nb, prow, pbat, avey::kTfPvKeys, 128, &map_p);
+    if (rc == AVEY_OK)
+      rc = encode_map(&q, q.z_tr, q.z_tr_batch_stride, q.z_tr_row_stride, 32, avey::kTfPvKeys, &map_z);
+    if (rc == AVEY_OK) rc = encode_map(&q, q.out, q.out_batch_stride, q.out_row_stride, 32, 32, &map_o);
+    if (rc != AVEY_OK) return rc;
+    const avey::FwdArgs args = make_args(&q);
+    avey::LongGeom geom = l.geom;
+    geom.den_part = den_base + b0 * geom.n_groups * static_cast<int64_t>(C);
+    avey::tf_gram_p<<<dim3(static_cast<unsigned>(l.gp_items), static_cast<unsigned>(q.batch)),
+                      avey::kTfThreads, static_cast<size_t>(l.smem_gp), stream>>>(args, map_k, map_pst, geom);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tf_gram_p launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    avey::tf_pv<ACT><<<dim3(static_cast<unsigned>(geom.n_qtiles * geom.n_fgroups),
+                            static_cast<unsigned>(q.batch)),
+                       avey::kTfThreads, static_cast<size_t>(l.smem_pv), stream>>>(
+        args, map_p, map_z, map_o, geom);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tf_pv launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  }
+  return ok();
+}
+
+int launch_tf32_act(const AveyFwdParams* p, cudaStream_t stream) {
+  switch (p->activation) {
+    case AVEY_ACT_RELU: return launch_tf32<AVEY_ACT_RELU>(p, stream);
+    case AVEY_ACT_RELU2: return launch_tf32<AVEY_ACT_RELU2>(p, stream);
+    case AVEY_ACT_SILU: return launch_tf32<AVEY_ACT_SILU>(p, stream);
+    case AVEY_ACT_GELU: return launch_tf32<AVEY_ACT_GELU>(p, stream);
+    default: return launch_tf32<AVEY_ACT_IDENTITY>(p, stream);
+  }
 }
 
 template <typename T, int ACT>
@@ -559,13 +642,14 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
   std::memset(plan, 0, sizeof(*plan));
   plan->reason = reason;
   plan->launches = 1;
-  if (reason == kReasonNone && is_long(p)) {
+  if (reason == kReasonNone && is_pair(p)) {
     const LongLayout l = long_layout(p);
     plan->kernel = AVEY_KERNEL_TCGEN05;
-    // The pre-pass, then a G/P + P.Z launch pair per batch slice.
-    plan->launches = 1 + 2 * static_cast<int32_t>((p->batch + l.slice_rows - 1) / l.slice_rows);
+    // (16-bit: the pre-pass, then) a G/P + P.Z launch pair per batch slice.
+    plan->launches = (is_tf32(p) ? 0 : 1) +
+                     2 * static_cast<int32_t>((p->batch + l.slice_rows - 1) / l.slice_rows);
     plan->grid = static_cast<int32_t>(std::min<int64_t>(p->batch, l.slice_rows) * l.gp_items);
-    plan->block = avey::kLgThreads;
+    plan->block = is_tf32(p) ? avey::kTfThreads : avey::kLgThreads;
     plan->smem_bytes = std::max(l.smem_gp, l.smem_pv);
   } else if (reason == kReasonNone) {
     const TcLayout l = tc_layout(p);
@@ -596,7 +680,7 @@ int avey_fwd_workspace_size(const AveyFwdParams* p, uint64_t* bytes) {
   if (!bytes) return fail(AVEY_ERR_ARGUMENT, "bytes is NULL");
   if (plan.kernel != AVEY_KERNEL_TCGEN05)
     *bytes = 0u;
-  else if (is_long(p))
+  else if (is_pair(p))
     *bytes = long_layout(p).total;
   else
     *bytes = static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context) * sizeof(float);
@@ -611,6 +695,7 @@ int avey_fwd_v1(const AveyFwdParams* p, void* stream_ptr) {
   if (rc != AVEY_OK) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (plan.kernel == AVEY_KERNEL_TCGEN05) {
+    if (is_tf32(p)) return launch_tf32_act(p, stream);
     return p->dtype == AVEY_BF16 ? launch_tc_act<__nv_bfloat16>(p, stream)
                                  : launch_tc_act<__half>(p, stream);
   }
@@ -656,17 +741,19 @@ int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
   int rc = avey_fwd_plan(p, &plan);
   if (rc != AVEY_OK) return rc;
   AveyFwdParams q = *p;
-  // Contexts above 512 would take the long-context tensor-core path, whose P
-  // workspace this entry point does not have: they run the CUDA-core kernel.
-  if (is_long(p)) {
+  // Contexts above 512 and fp32 inputs would take a tensor-core kernel pair
+  // whose P workspace this entry point does not have: they run the CUDA-core
+  // kernel.
+  if (is_pair(p)) {
     if (p->kernel == AVEY_KERNEL_TCGEN05)
       return fail(AVEY_ERR_UNSUPPORTED,
-                  "the no-allocation entry point runs contexts above 512 on CUDA cores only");
+                  "the no-allocation entry point runs contexts above 512 and fp32 inputs on CUDA "
+                  "cores only");
     q.kernel = AVEY_KERNEL_SIMT;
   }
   // Only the fused tensor-core path reads scratch (one float per row); the
   // CUDA-core kernels need none and have no row limit here.
-  if (plan.kernel != AVEY_KERNEL_TCGEN05 || is_long(p)) return avey_fwd_v1(&q, stream);
+  if (plan.kernel != AVEY_KERNEL_TCGEN05 || is_pair(p)) return avey_fwd_v1(&q, stream);
   const uint64_t rows = static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context);
   if (rows > AVEY_NOALLOC_MAX_ROWS)
     return fail(AVEY_ERR_ARGUMENT,

@@ -233,6 +233,26 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, 
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem] with tf32 operands (32-bit containers whose
+// low 13 mantissa bits are zero) and fp32 accumulation.
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// x rounded to tf32 (nearest, ties away from zero): an fp32 bit pattern whose
+// low 13 mantissa bits are zero.
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
 // Arrive once on `bar` when every tcgen05 op issued so far by this thread is done.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile(
@@ -318,6 +338,18 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t m, ui
   return (1u << 4)             // D format: f32
          | (ab_fmt << 7)       // A format
          | (ab_fmt << 10)      // B format
+         | (a_mn << 15)        // A major
+         | (b_mn << 16)        // B major
+         | ((n >> 3) << 17)    // N / 8
+         | ((m >> 4) << 24);   // M / 16
+}
+
+// Instruction descriptor for kind::tf32 (A and B tf32) with fp32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_tf32(uint32_t m, uint32_t n, uint32_t a_mn,
+                                                  uint32_t b_mn) {
+  return (1u << 4)             // D format: f32
+         | (2u << 7)           // A format: tf32
+         | (2u << 10)          // B format: tf32
          | (a_mn << 15)        // A major
          | (b_mn << 16)        // B major
          | ((n >> 3) << 17)    // N / 8

@@ -70,10 +70,11 @@ struct LgCtrl {
 static_assert(sizeof(LgCtrl) <= kLgCtrlBytes, "control block too large");
 
 struct PvCtrl {
-  uint64_t full[kPvStages], empty[kPvStages];
+  uint64_t full[kPvStages], empty[kPvStages], fixed[kPvStages];
   uint64_t o_full;
   uint32_t tmem_base;
   int last_valid;
+  int fix;  // some key row the MMA reads outside the allowed set is not finite
   alignas(16) float bias[kPvGroupCols];
 };
 static_assert(sizeof(PvCtrl) <= kPvCtrlBytes, "control block too large");
@@ -378,9 +379,11 @@ __global__ void __launch_bounds__(kPvThreads, 2)
     for (int s = 0; s < kPvStages; ++s) {
       mbar_init(smem_u32(&ctrl->full[s]), 1);
       mbar_init(smem_u32(&ctrl->empty[s]), 1);
+      mbar_init(smem_u32(&ctrl->fixed[s]), 4);  // warps 4-7, in fix mode
     }
     mbar_init(smem_u32(&ctrl->o_full), 1);
     ctrl->last_valid = -1;
+    ctrl->fix = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -397,17 +400,32 @@ __global__ void __launch_bounds__(kPvThreads, 2)
   if (args.has_bias)
     for (int f = tid; f < width; f += kPvThreads)
       ctrl->bias[f] = to_f32<T>(static_cast<const T*>(args.bias)[f_lo + f]);
-  tc_fence_before();
   __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = ctrl->tmem_base;
-
   const int kv_end = ctrl->last_valid + 1;
   const int nkeys = args.causal ? min(kv_end, q_lo + 128) : kv_end;
   const bool skip = q_lo >= kv_end;
   const int nkc = skip ? 0 : (nkeys + kPvChunkKeys - 1) / kPvChunkKeys;
   const int nfb = (width + 63) / 64;
   const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  // The MMA reads whole 64-key chunks. With a padding mask some of their key
+  // rows are outside the allowed set: P is exactly zero there, but 0 * Inf or
+  // 0 * NaN in a padded row of z_tr would still reach O. If any such row is
+  // not finite (its sum of squares, from norm_prepass, which completed before
+  // the G/P launch did), warps 4-7 zero those rows of every stage before the
+  // MMA reads it.
+  if (!skip && args.has_valid) {
+    const float* ssq = args.sumsq + static_cast<int64_t>(b) * C;
+    const int kend = min(C, nkc * kPvChunkKeys);
+    int bad = 0;
+    for (int j = tid; j < kend; j += kPvThreads)
+      if (!(j < nkeys && pos_valid(args, b, j)) && !isfinite(ssq[j])) bad = 1;
+    if (bad) ctrl->fix = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctrl->tmem_base;
+  const bool fix = ctrl->fix != 0;
 
   if (warp == 0) {
     if (!skip && lane == 0) {
@@ -438,7 +456,7 @@ __global__ void __launch_bounds__(kPvThreads, 2)
       int st = 0;
       uint32_t ph = 0;
       for (int kc = 0; kc < nkc; ++kc) {
-        mbar_wait(smem_u32(&ctrl->full[st]), ph);
+        mbar_wait(smem_u32(fix ? &ctrl->fixed[st] : &ctrl->full[st]), ph);
         tc_fence_after();
         const uint32_t adv = static_cast<uint32_t>(st * kPvStageBytes) >> 4;
 #pragma unroll
@@ -452,6 +470,30 @@ __global__ void __launch_bounds__(kPvThreads, 2)
         }
       }
       tc_commit(smem_u32(&ctrl->o_full));
+    }
+  } else if (warp >= 4 && fix && !skip) {
+    // Fix mode: zero the Z rows of keys outside the allowed set in each stage.
+    const int t = tid - 128;
+    int st = 0;
+    uint32_t ph = 0;
+    for (int kc = 0; kc < nkc; ++kc) {
+      mbar_wait(smem_u32(&ctrl->full[st]), ph);
+      const uint32_t zb = ring + st * kPvStageBytes + kPvABytes;
+      for (int r = t; r < nfb * kPvChunkKeys; r += 128) {
+        const int kr = r % kPvChunkKeys, key = kc * kPvChunkKeys + kr;
+        if (key < C && !(key < nkeys && pos_valid(args, b, key))) {
+          const uint32_t ra = zb + (r / kPvChunkKeys) * kPvBBoxBytes + kr * 128;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) st_shared_v4(ra + q * 16, 0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctrl->fixed[st]));
+      if (++st == kPvStages) {
+        st = 0;
+        ph ^= 1u;
+      }
     }
   }
   __syncwarp();  // lanes 1-31 of the producer and MMA warps rejoin lane 0

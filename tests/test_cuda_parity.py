@@ -285,9 +285,11 @@ def test_activation_and_mode_matrix_at_scale(shape, dtype, op, act):
         assert (y[r:r + 1][~ok] == 0).all()
 
 
+@pytest.mark.parametrize('kernel', [_native.KERNEL_SIMT, _native.KERNEL_TCGEN05], ids=['simt', 'tf32x3'])
 @pytest.mark.parametrize('op', ['avey', 'avey_b'])
-def test_fp32_long_context_cuda_core_path(op):
-    """fp32 rows above 512 tokens: the CUDA-core kernel's 512-key super-blocks."""
+def test_fp32_long_context(op, kernel):
+    """fp32 rows above 512 tokens: the CUDA-core kernel's 512-key super-blocks
+    and the 3xTF32 tensor-core pair, both at the fp32 bound."""
     g = torch.Generator(device='cpu').manual_seed(21)
     b, n, d = 2, 1100, 72
     x = torch.randn(b, n, 2 * d, generator=g).to(DEV)
@@ -296,12 +298,14 @@ def test_fp32_long_context_cuda_core_path(op):
     head, tail = x[..., :d], x[..., d:]
     valid = (torch.rand(b, n, generator=g) > 0.1).to(DEV)
     plan = ops.plan(tail, z_tl=head, causal=op == 'avey', normalize=op == 'avey_b')
-    assert plan.kernel == _native.KERNEL_SIMT and plan.block == 256
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.block == 256
+    v = torch.randn(n, n, generator=g).to(DEV) * 0.05
     if op == 'avey':
-        v = torch.randn(n, n, generator=g).to(DEV) * 0.05
-        out = avey(tail, v, z_tl=head, valid=valid, activation='silu')
+        out = ops.contextualize(tail, v, head, None, valid, 1e-6, 1e-12, True, False,
+                                _native.ACTIVATION_IDS['silu'], kernel)
     else:
-        out = avey_b(tail, z_tl=head, valid=valid, eps=0.25, activation='gelu')
+        out = ops.contextualize(tail, None, head, None, valid, 0.25, 1e-12, False, True,
+                                _native.ACTIVATION_IDS['gelu'], kernel)
     torch.cuda.synchronize()
     y = to_numpy(out)
     for r in range(b):
@@ -393,11 +397,13 @@ def test_fp64_inputs_run_natively():
 
 def test_autograd_inputs_run_the_native_backward():
     z = torch.rand(2, 35, 40, device=DEV, requires_grad=True)
+    plan = ops.plan(z.detach(), causal=False, normalize=True)
     before = _native.launch_count()
     avey_b(z).sum().backward()
     torch.cuda.synchronize()
-    # forward (1) + prep, scores, epilogue, dscores, final (5)
-    assert _native.launch_count() == before + 6
+    # forward (fp32: the 3xTF32 pair) + prep, scores, epilogue, dscores, final (5)
+    assert plan.launches == 2
+    assert _native.launch_count() == before + plan.launches + 5
     assert z.grad is not None and torch.isfinite(z.grad).all()
     z.grad = None
     avey_b(z, backend='cuda').sum().backward()
@@ -481,3 +487,87 @@ def test_prefix_lengths_match_the_byte_mask(dtype, n, op):
     assert torch.equal(outs[0], outs[1])
     y = to_numpy(outs[1])
     assert (y[2] == 0).all() and np.isfinite(y).all()
+
+
+@pytest.mark.parametrize('shape,op', [((2, 256, 128), 'avey'), ((64, 512, 768), 'avey'),
+                                      ((8, 512, 384), 'avey_b')], ids=['c1', 'c2-shape', 'c3-shape'])
+def test_fp32_runs_on_tensor_cores_at_the_fp32_bound(shape, op):
+    # fp32 takes the 3xTF32 tcgen05 pair (BASELINE config 1 and the config-2
+    # and config-3 shapes in fp32): norm-wise 1e-4 against the fp64 oracle on
+    # every row checked, and the elementwise bound of the reference's own fp32
+    # kernel tests (atol = rtol = 1e-5) on config 1.
+    g = torch.Generator(device='cpu').manual_seed(7)
+    b, n, d = shape
+    x = torch.randn(b, n, 2 * d, generator=g)
+    head, tail = x[..., :d].to(DEV), x[..., d:].to(DEV)
+    valid = None
+    if op == 'avey':
+        w = (torch.randn(n, n, generator=g) * 0.02).to(DEV)
+        bias = (torch.randn(d, generator=g) * 0.01).to(DEV) if b > 2 else None
+        plan = ops.plan(tail, w, head, bias)
+        out = avey(tail, w, z_tl=head, bias=bias)
+    else:
+        lengths = torch.randint(n // 4, n + 1, (b,), generator=g)
+        valid = (torch.arange(n)[None, :] < lengths[:, None]).to(DEV)
+        plan = ops.plan(tail, None, head, None, valid, causal=False, normalize=True)
+        tail = tail.abs()  # keep the signed row sums away from -eps
+        out = avey_b(tail, z_tl=head, valid=valid, eps=1e-6)
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.launches == 2
+    torch.cuda.synchronize()
+    y = to_numpy(out)
+    assert np.isfinite(y).all()
+    rows = range(b) if b <= 8 else range(0, b, 8)
+    for r in rows:
+        zt, zl = to_numpy(tail[r:r + 1]), to_numpy(head[r:r + 1])
+        if op == 'avey':
+            ref = oracle.avey(zt, to_numpy(w), z_tl=zl, bias=None if bias is None else to_numpy(bias))
+        else:
+            ref = oracle.avey_b(zt, z_tl=zl, valid=to_numpy(valid[r:r + 1].float()) > 0, eps=1e-6)
+        err = norm_rel_err(y[r:r + 1], ref)
+        assert err <= TOL['float32'], (r, err)
+        if b == 2:
+            np.testing.assert_allclose(y[r:r + 1], ref, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize('dtype,n', [(torch.bfloat16, 300), (torch.bfloat16, 700), (torch.float16, 700),
+                                     (torch.float32, 300), (torch.float32, 700)],
+                         ids=['bf16-fused', 'bf16-long', 'f16-long', 'fp32-300', 'fp32-700'])
+@pytest.mark.parametrize('mask', ['prefix', 'holes'])
+@pytest.mark.parametrize('fill', ['nan', 'inf'])
+def test_non_finite_padding_never_reaches_the_output(dtype, n, mask, fill):
+    # Padded rows of z_tr and of the gate hold NaN or Inf (the reference masks
+    # them before any arithmetic, ops.py:64-66): every tensor-core kernel must
+    # keep them out of the output, also where a padded key shares a 64-key
+    # chunk with valid ones (prefix lengths that are not multiples of 64, and
+    # holes inside the row).
+    g = torch.Generator(device='cpu').manual_seed(n + (mask == 'holes'))
+    b, d = 3, 64
+    x = torch.randn(b, n, 2 * d, generator=g)
+    if mask == 'prefix':
+        lengths = torch.tensor([n - 37, n // 2 + 3, n])
+        valid = torch.arange(n)[None, :] < lengths[:, None]
+    else:
+        valid = torch.rand(b, n, generator=g) > 0.2
+    x[~valid] = float(fill)
+    x = x.to(dtype).to(DEV)
+    valid = valid.to(DEV)
+    head, tail = x[..., :d], x[..., d:]
+    w = (torch.randn(n, n, generator=g) * 0.05).to(dtype).to(DEV)
+    assert ops.plan(tail, w, head, None, valid).kernel == _native.KERNEL_TCGEN05
+    # Avey-B on non-negative tails keeps the signed row sums away from -eps.
+    outs = {'avey': avey(tail, w, z_tl=head, valid=valid),
+            'avey_b': avey_b(tail.abs(), z_tl=head, valid=valid, eps=0.5)}
+    torch.cuda.synchronize()
+    ok = to_numpy(valid.float()) > 0
+    tol = TOL['float32'] if dtype == torch.float32 else TOL['bfloat16']
+    for op, out in outs.items():
+        y = to_numpy(out)
+        assert np.isfinite(y).all(), op
+        assert (y[~ok] == 0).all(), op
+        for r in range(b):
+            zt, zl = to_numpy(tail[r:r + 1]), to_numpy(head[r:r + 1])
+            if op == 'avey':
+                ref = oracle.avey(zt, to_numpy(w), z_tl=zl, valid=ok[r:r + 1])
+            else:
+                ref = oracle.avey_b(np.abs(zt), z_tl=zl, valid=ok[r:r + 1], eps=0.5)
+            assert norm_rel_err(y[r:r + 1], ref) <= tol, (op, r, norm_rel_err(y[r:r + 1], ref))

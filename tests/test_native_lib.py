@@ -95,15 +95,33 @@ def test_plan_accepts_head_tail_views_without_copy():
 
 
 @pytest.mark.parametrize('shape,dtype,reason', [
-    ((2, 35, 133), torch.float32, 1),    # fp32 -> CUDA-core kernel
+    ((2, 35, 133), torch.float32, 3),    # 133 fp32 features: rows not 16-byte aligned
     ((2, 35, 37), torch.bfloat16, 3),    # 37 features: rows not 16-byte aligned
     ((1, 8200, 64), torch.bfloat16, 2),  # more than 8192 tokens
-    ((2, 35, 40), torch.float64, 1),
+    ((1, 8200, 64), torch.float32, 2),
+    ((2, 35, 40), torch.float64, 1),     # fp64 -> CUDA-core kernel
 ])
 def test_plan_falls_back_to_cuda_core_kernel(shape, dtype, reason):
     z = torch.randn(*shape).to(dtype)
     plan = ops.plan(z)
     assert plan.kernel == _native.KERNEL_SIMT and plan.reason == reason
+
+
+@pytest.mark.parametrize('shape,items', [((2, 256, 128), 2), ((64, 512, 768), 6), ((1, 1100, 72), 25)])
+def test_plan_runs_fp32_on_the_3xtf32_kernel_pair(shape, items):
+    # fp32: tf_gram_p per (query tile, key group of 256) and tf_pv, no pre-pass
+    # (the split of each staged tile sums the squares); the workspace holds P
+    # as fp32.
+    z = torch.randn(*shape)
+    b, n, d = shape
+    plan = ops.plan(z, torch.randn(n, n), z_tl=z)
+    assert plan.kernel == _native.KERNEL_TCGEN05 and plan.reason == 0
+    assert plan.launches == 2 and plan.block == 256 and plan.grid == b * items
+    assert 190_000 < plan.smem_bytes <= 232_448
+    params = ops.build_params(z, torch.randn(n, n), z, None, None, torch.empty_like(z), eps=1e-6,
+                              norm_eps=1e-12, causal=True, normalize=False, activation_id=0)
+    cp = -(-n // 64) * 64
+    assert _native.workspace_size(params) >= b * n * cp * 4
 
 
 def test_plan_takes_the_long_context_tcgen05_path_above_512_tokens():
@@ -150,8 +168,15 @@ def test_workspace_size_is_four_bytes_per_row_on_the_tcgen05_path():
     p = ops.build_params(z, None, None, None, None, out, eps=1e-6, norm_eps=1e-12, causal=False,
                          normalize=True, activation_id=0)
     assert _native.workspace_size(p) == 3 * 384 * 4
+    # fp32 runs the 3xTF32 kernel pair: partial row sums and P (fp32, rows
+    # padded to 64 keys) follow the per-row floats.
     z32 = z.float()
     p = ops.build_params(z32, None, None, None, None, z32.clone(), eps=1e-6, norm_eps=1e-12,
+                         causal=False, normalize=True, activation_id=0)
+    assert _native.workspace_size(p) >= 3 * 384 * 384 * 4 + 3 * 384 * 4
+    # Inputs the CUDA-core kernels take need none.
+    z37 = torch.randn(3, 384, 37)
+    p = ops.build_params(z37, None, None, None, None, z37.clone(), eps=1e-6, norm_eps=1e-12,
                          causal=False, normalize=True, activation_id=0)
     assert _native.workspace_size(p) == 0
 

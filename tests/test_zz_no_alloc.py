@@ -77,6 +77,18 @@ def test_noalloc_entry_point_on_the_cuda_core_path():
     assert norm_rel_err(to_numpy(got), to_numpy(want)) <= TOL['float32']
 
 
+@pytest.mark.gpu
+def test_noalloc_entry_point_runs_fp32_on_cuda_cores():
+    # avey_fwd_v1 runs aligned fp32 on the 3xTF32 kernel pair, whose P
+    # workspace the no-allocation entry point does not have: it takes the
+    # CUDA-core kernel, within the fp32 bound of the pair's result.
+    z = torch.rand(2, 96, 64, device='cuda')
+    assert ops.plan(z, causal=False, normalize=True).kernel == _native.KERNEL_TCGEN05
+    want = _call(z, None, z, None, None, causal=False, normalize=True, act=0, noalloc=False)
+    got = _call(z, None, z, None, None, causal=False, normalize=True, act=0, noalloc=True)
+    assert norm_rel_err(to_numpy(got), to_numpy(want)) <= TOL['float32']
+
+
 def test_noalloc_entry_point_rejects_inputs_beyond_its_limit():
     # 2049 x 512 rows on the fused tensor-core path (the one that reads the
     # scratch) is past the limit; rejected before anything launches.
