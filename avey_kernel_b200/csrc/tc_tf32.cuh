@@ -73,11 +73,14 @@ static_assert(sizeof(TfPvCtrl) <= kTfCtrlBytes, "control block too large");
 // One staged 128-byte row (32 fp32 values; the swizzle only permutes its
 // 16-byte pieces) split in place: heads where the values were, tails `lo_off`
 // bytes further on; `zero` writes zeros to both instead. Returns the sum of
-// squares of the row's values.
+// squares of the row's values. The pieces are visited in the row's swizzled
+// order (piece q at q ^ (row % 8)), so the 32 rows a warp splits at once
+// spread over all banks.
 __device__ __forceinline__ float tf32_split_row(uint32_t addr, uint32_t lo_off, bool zero) {
+  const uint32_t sw = (addr >> 7) & 7u;
   uint4 v[8];
 #pragma unroll
-  for (int q = 0; q < 8; ++q) v[q] = ld_shared_v4(addr + q * 16);
+  for (int q = 0; q < 8; ++q) v[q] = ld_shared_v4(addr + ((q ^ sw) << 4));
   float s = 0.f;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
@@ -91,8 +94,8 @@ __device__ __forceinline__ float tf32_split_row(uint32_t addr, uint32_t lo_off, 
       l[e] = tf32_rna(x[e] - __uint_as_float(h[e]));
       if (zero) h[e] = l[e] = 0u;
     }
-    st_shared_v4(addr + q * 16, h[0], h[1], h[2], h[3]);
-    st_shared_v4(addr + lo_off + q * 16, l[0], l[1], l[2], l[3]);
+    st_shared_v4(addr + ((q ^ sw) << 4), h[0], h[1], h[2], h[3]);
+    st_shared_v4(addr + lo_off + ((q ^ sw) << 4), l[0], l[1], l[2], l[3]);
   }
   return s;
 }
