@@ -25,10 +25,10 @@ STATUS_NAMES = {
 EXPORTS = ('avey_fwd_v1', 'avey_fwd_plan', 'avey_fwd_workspace_size', 'avey_fwd_noalloc_v1',
            'avey_bwd_step_v1', 'avey_bwd_workspace_size',
            'avey_last_error', 'avey_device_status', 'avey_launch_count', 'avey_abi_version',
-           'avey_test_hooks_v1')
+           'avey_test_hooks_v1', 'avey_gemm_v1', 'avey_fwd_presummed_v1')
 BWD_PREP, BWD_SCORES, BWD_EPILOGUE, BWD_DSCORES, BWD_FINAL = range(5)
 NOALLOC_MAX_ROWS = 1 << 20
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class AveyFwdParams(ctypes.Structure):
@@ -116,6 +116,37 @@ class AveyBwdParams(ctypes.Structure):
     ]
 
 
+class AveyGemmParams(ctypes.Structure):
+    _fields_ = [
+        ('struct_size', ctypes.c_uint32),
+        ('dtype', ctypes.c_int32),
+        ('out_dtype', ctypes.c_int32),
+        ('mode', ctypes.c_int32),
+        ('batch', ctypes.c_int64),
+        ('m', ctypes.c_int64),
+        ('n', ctypes.c_int64),
+        ('k', ctypes.c_int64),
+        ('a', ctypes.c_void_p),
+        ('a_batch_stride', ctypes.c_int64),
+        ('a_ld', ctypes.c_int64),
+        ('a_major', ctypes.c_int32),
+        ('b', ctypes.c_void_p),
+        ('b_batch_stride', ctypes.c_int64),
+        ('b_ld', ctypes.c_int64),
+        ('b_major', ctypes.c_int32),
+        ('c', ctypes.c_void_p),
+        ('c_batch_stride', ctypes.c_int64),
+        ('c_ld', ctypes.c_int64),
+        ('bias', ctypes.c_void_p),
+        ('gate', ctypes.c_void_p),
+        ('gate_batch_stride', ctypes.c_int64),
+        ('gate_ld', ctypes.c_int64),
+        ('activation', ctypes.c_int32),
+        ('sumsq_col0', ctypes.c_int32),
+        ('sumsq', ctypes.c_void_p),
+    ]
+
+
 class AveyPlan(ctypes.Structure):
     _fields_ = [
         ('kernel', ctypes.c_int32),
@@ -183,6 +214,11 @@ def lib() -> ctypes.CDLL:
         dll.avey_abi_version.restype = ctypes.c_int
         dll.avey_test_hooks_v1.argtypes = [ctypes.c_longlong, ctypes.c_int]
         dll.avey_test_hooks_v1.restype = ctypes.c_int
+        dll.avey_gemm_v1.argtypes = [ctypes.POINTER(AveyGemmParams), ctypes.c_void_p]
+        dll.avey_gemm_v1.restype = ctypes.c_int
+        dll.avey_fwd_presummed_v1.argtypes = [ctypes.POINTER(AveyFwdParams), ctypes.c_void_p,
+                                              ctypes.c_int, ctypes.c_void_p]
+        dll.avey_fwd_presummed_v1.restype = ctypes.c_int
         if dll.avey_abi_version() != ABI_VERSION:
             raise RuntimeError(f'{path}: ABI version {dll.avey_abi_version()} != {ABI_VERSION}')
         _lib = dll
@@ -202,6 +238,17 @@ def forward(params: AveyFwdParams, stream: int) -> None:
 def forward_noalloc(params: AveyFwdParams, stream: int) -> None:
     """avey_fwd_noalloc_v1: like forward() but with the library's own scratch."""
     _check(lib().avey_fwd_noalloc_v1(ctypes.byref(params), ctypes.c_void_p(stream)))
+
+
+def gemm(params: AveyGemmParams, stream: int) -> None:
+    """avey_gemm_v1: enqueue one batched tcgen05 matrix product on `stream`."""
+    _check(lib().avey_gemm_v1(ctypes.byref(params), ctypes.c_void_p(stream)))
+
+
+def forward_presummed(params: AveyFwdParams, sumsq: int, planes: int, stream: int) -> None:
+    """avey_fwd_presummed_v1: forward with the row sums of squares supplied."""
+    _check(lib().avey_fwd_presummed_v1(ctypes.byref(params), ctypes.c_void_p(sumsq), int(planes),
+                                       ctypes.c_void_p(stream)))
 
 
 def plan(params: AveyFwdParams) -> AveyPlan:

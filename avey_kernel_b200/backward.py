@@ -3,9 +3,11 @@
 The reference differentiates only through its PyTorch path
 (avey_kernels/ops.py:94-106 route inputs that require grad to _reference,
 ops.py:61-91). Here ``avey_b200::contextualize`` (the native forward) gets a
-native backward: five library GEMMs (``torch.bmm``, i.e. cuBLAS) with the
-fused elementwise / reduction steps of ``csrc/bwd_kernels.cuh`` between them,
-called through the C ABI (``avey_bwd_step_v1``):
+native backward: five batched GEMMs (this library's tcgen05 kernel,
+``avey_gemm_v1``, for bf16 inputs; ``torch.bmm`` for the fp32 / fp64 GEMMs
+of the other input types and for unaligned shapes) with the fused
+elementwise / reduction steps of ``csrc/bwd_kernels.cuh`` between them, called
+through the C ABI (``avey_bwd_step_v1``):
 
   PREP      zm (z_tr, padded rows 0), norms      g   = zm zm^T
   SCORES    s = g r_i r_j (.) v (.) mask, den    num = s zm
@@ -18,7 +20,10 @@ input type, and the norms are applied in fp32 inside the steps. GEMM operands
 are bf16 for bf16 inputs (fp32 accumulation and fp32 results) and fp32 / fp64
 otherwise: the fp16 range would not hold the products of arbitrary upstream
 gradients. fp32 GEMMs follow torch's matmul precision setting (full fp32
-unless the caller allows TF32).
+unless the caller allows TF32). Under the causal mask s is lower triangular:
+g and ds0 are computed only in their 128 x 256 tiles that reach the diagonal
+(the steps read nothing above it), and the K loops of num = s zm and
+dzd = s^T dnum stop at / start from each row tile's diagonal.
 """
 
 from __future__ import annotations
@@ -28,6 +33,7 @@ from typing import List, Optional
 import torch
 
 from . import _native
+from . import gemm as _gemm
 
 _GEMM_DTYPE = {torch.bfloat16: torch.bfloat16, torch.float16: torch.float32,
                torch.float32: torch.float32, torch.float64: torch.float64}
@@ -43,7 +49,14 @@ def _unit_last(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     return t if t is None or t.stride(-1) == 1 else t.contiguous()
 
 
-def _bmm(a: torch.Tensor, b: torch.Tensor, acc: torch.dtype) -> torch.Tensor:
+def _bmm(a: torch.Tensor, b: torch.Tensor, acc: torch.dtype, mode: int = _gemm.DENSE) -> torch.Tensor:
+    """a @ b with results of type `acc`: this library's tcgen05 GEMM for 16-bit
+    operands with fp32 results whose bases and strides are 16-byte aligned,
+    skipping what the causal `mode` allows; the library GEMM (torch.bmm)
+    otherwise (fp32 / fp64 operands, unaligned shapes). Under LOWER_OUT only
+    the entries [i][j] with j <= i of the result are defined."""
+    if acc == torch.float32 and a.shape[-1] > 0 and b.shape[-1] % 4 == 0 and _gemm.supported(a, b):
+        return _gemm.bmm(a, b, mode=mode)
     return torch.bmm(a, b) if a.dtype == acc else torch.bmm(a, b, out_dtype=acc)
 
 
@@ -108,11 +121,12 @@ def contextualize_backward_impl(z_tr, v, z_tl, bias, valid, grad_out, eps, norm_
             p.zm = zm.data_ptr()
         p.norms = norms.data_ptr()
         _native.bwd_step(p, _native.BWD_PREP, stream)
-        g = _bmm(zm, zm.transpose(1, 2), acc)
+        tri = bool(causal)
+        g = _bmm(zm, zm.transpose(1, 2), acc, _gemm.LOWER_OUT if tri else _gemm.DENSE)
         s, den = empty(B, C, C, dtype=gdt), empty(B, C, dtype=acc)
         p.g, p.s, p.den = g.data_ptr(), s.data_ptr(), den.data_ptr()
         _native.bwd_step(p, _native.BWD_SCORES, stream)
-        num = _bmm(s, zm, acc)
+        num = _bmm(s, zm, acc, _gemm.K_LOWER if tri else _gemm.DENSE)
         dnum, dden = empty(B, C, d, dtype=gdt), empty(B, C, dtype=acc)
         workspace = empty(_native.bwd_workspace_size(p), dtype=torch.uint8)
         if packed_out is not None:
@@ -128,14 +142,14 @@ def contextualize_backward_impl(z_tr, v, z_tl, bias, valid, grad_out, eps, norm_
         del num
         gz = gv = None
         if need_z or need_v:
-            ds0 = _bmm(dnum, zm.transpose(1, 2), acc)
+            ds0 = _bmm(dnum, zm.transpose(1, 2), acc, _gemm.LOWER_OUT if tri else _gemm.DENSE)
             dgsym = empty(B, C, C, dtype=gdt)
             gv = empty(C, C, dtype=dt) if need_v else None
             p.ds0, p.dgsym, p.grad_v = ds0.data_ptr(), dgsym.data_ptr(), _ptr(gv)
             _native.bwd_step(p, _native.BWD_DSCORES, stream)
             del ds0, g
             if need_z:
-                dzd = _bmm(s.transpose(1, 2), dnum, acc)
+                dzd = _bmm(s.transpose(1, 2), dnum, acc, _gemm.K_UPPER if tri else _gemm.DENSE)
                 dzh = _bmm(dgsym, zm, acc)
                 gz = packed_out[..., d:] if packed_out is not None else empty(B, C, d, dtype=dt)
                 p.dzd, p.dzh, p.grad_z_tr = dzd.data_ptr(), dzh.data_ptr(), gz.data_ptr()

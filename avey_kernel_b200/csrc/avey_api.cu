@@ -22,6 +22,7 @@
 #include "tc_kernel.cuh"
 #include "tc_long.cuh"
 #include "tc_tf32.cuh"
+#include "tc_gemm.cuh"
 
 namespace {
 
@@ -379,8 +380,34 @@ int encode_map_dims(int dtype, const void* base, uint64_t inner, uint64_t rows, 
   return encode_cached(dtype, base, dims, strides, box_cols, box_rows, map);
 }
 
+// Row sums of squares of z_tr, written into the workspace before the main
+// kernels: the pre-pass over z_tr, or (avey_fwd_presummed_v1) the sum of the
+// caller's partial planes. Both let the next launch start at once
+// (programmatic dependent launch).
+struct PreSum {
+  const float* planes = nullptr;
+  int n = 0;
+};
+
+template <typename T>
+int launch_row_sums(const AveyFwdParams* p, const avey::FwdArgs& args, const PreSum& ps,
+                    cudaStream_t stream) {
+  const int rows = static_cast<int>(p->batch * p->context);
+  if (ps.planes) {
+    const int blocks = std::min(148 * 4, (rows + avey::kPrepassThreads - 1) / avey::kPrepassThreads);
+    avey::sumsq_planes<<<blocks, avey::kPrepassThreads, 0, stream>>>(ps.planes, ps.n, rows, args.sumsq);
+  } else {
+    const int pre_blocks = std::min(148 * 8, (rows + 7) / 8);
+    avey::norm_prepass<T><<<pre_blocks, avey::kPrepassThreads, 0, stream>>>(args);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "row-sum launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return AVEY_OK;
+}
+
 template <typename T, int ACT>
-int launch_long(const AveyFwdParams* p, cudaStream_t stream) {
+int launch_long(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps) {
   cudaError_t attr_err = smem_opt_in<avey::tc_gram_p<T>>(kMaxDynSmem);
   if (attr_err == cudaSuccess) attr_err = smem_opt_in<avey::tc_pv<T, ACT>>(kMaxDynSmem);
   if (attr_err != cudaSuccess)
@@ -398,12 +425,9 @@ int launch_long(const AveyFwdParams* p, cudaStream_t stream) {
   const uint64_t prow = static_cast<uint64_t>(l.geom.p_rs) * 2u, pbat = static_cast<uint64_t>(l.geom.p_bs) * 2u;
   const avey::FwdArgs all = make_args(p);
   // 1. Row sums of squares of every row.
-  const int rows = static_cast<int>(p->batch * p->context);
-  const int pre_blocks = std::min(148 * 8, (rows + 7) / 8);
-  avey::norm_prepass<T><<<pre_blocks, avey::kPrepassThreads, 0, stream>>>(all);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "norm pre-pass launch: %s", cudaGetErrorString(e));
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+  int rc0 = launch_row_sums<T>(p, all, ps, stream);
+  if (rc0 != AVEY_OK) return rc0;
+  cudaError_t e = cudaSuccess;
   // 2./3. Per batch slice: G and P per (query tile, key group) into the P
   // workspace (written with an L2 evict-last hint), then O = P Z and the
   // epilogue; a slice's P is small enough to be read back from L2.
@@ -523,8 +547,8 @@ int launch_tf32_act(const AveyFwdParams* p, cudaStream_t stream) {
 }
 
 template <typename T, int ACT>
-int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
-  if (is_long(p)) return launch_long<T, ACT>(p, stream);
+int launch_tc(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps) {
+  if (is_long(p)) return launch_long<T, ACT>(p, stream, ps);
   const cudaError_t attr_err = smem_opt_in<avey::tc_contextualize<T, ACT>>(kMaxDynSmem);
   if (attr_err != cudaSuccess)
     return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
@@ -553,12 +577,9 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
     return fail(AVEY_ERR_ARGUMENT, "the tcgen05 path needs a 4-byte aligned workspace of %llu bytes",
                 (unsigned long long)need);
   // 1. Row sums of squares (the first launch lets the second start at once).
-  const int rows = static_cast<int>(p->batch * p->context);
-  const int pre_blocks = std::min(148 * 8, (rows + 7) / 8);
-  avey::norm_prepass<T><<<pre_blocks, avey::kPrepassThreads, 0, stream>>>(args);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "norm pre-pass launch: %s", cudaGetErrorString(e));
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+  rc = launch_row_sums<T>(p, args, ps, stream);
+  if (rc != AVEY_OK) return rc;
+  cudaError_t e = cudaSuccess;
   // 2. The fused kernel, as a programmatic dependent of the pre-pass: it waits
   //    for the sums only before its P phase.
   cudaLaunchConfig_t cfg = {};
@@ -578,13 +599,13 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream) {
 }
 
 template <typename T>
-int launch_tc_act(const AveyFwdParams* p, cudaStream_t stream) {
+int launch_tc_act(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps = PreSum{}) {
   switch (p->activation) {
-    case AVEY_ACT_RELU: return launch_tc<T, AVEY_ACT_RELU>(p, stream);
-    case AVEY_ACT_RELU2: return launch_tc<T, AVEY_ACT_RELU2>(p, stream);
-    case AVEY_ACT_SILU: return launch_tc<T, AVEY_ACT_SILU>(p, stream);
-    case AVEY_ACT_GELU: return launch_tc<T, AVEY_ACT_GELU>(p, stream);
-    default: return launch_tc<T, AVEY_ACT_IDENTITY>(p, stream);
+    case AVEY_ACT_RELU: return launch_tc<T, AVEY_ACT_RELU>(p, stream, ps);
+    case AVEY_ACT_RELU2: return launch_tc<T, AVEY_ACT_RELU2>(p, stream, ps);
+    case AVEY_ACT_SILU: return launch_tc<T, AVEY_ACT_SILU>(p, stream, ps);
+    case AVEY_ACT_GELU: return launch_tc<T, AVEY_ACT_GELU>(p, stream, ps);
+    default: return launch_tc<T, AVEY_ACT_IDENTITY>(p, stream, ps);
   }
 }
 
@@ -618,6 +639,142 @@ int launch_simt(const AveyFwdParams* p, cudaStream_t stream) {
   if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "CUDA-core kernel launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return ok();
+}
+
+// ---------------------------------------------------------------------------
+// Batched tcgen05 matrix product (avey_gemm_v1).
+
+int sm_count() {
+  static std::once_flag once[kMaxDevices];
+  static int count[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  std::call_once(once[dev], [dev] {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+    count[dev] = n;
+  });
+  return count[dev];
+}
+
+// Output tiles of one batch entry (the kernel's gemm_cols_of summed over row tiles).
+int64_t gemm_tiles_per_batch(const avey::GemmGeom& g) {
+  int64_t n = 0;
+  for (int mt = 0; mt < g.n_mt; ++mt)
+    n += g.mode == avey::kGemmLowerOut
+             ? std::min<int64_t>(g.n_nt, (mt * avey::kGmBM + avey::kGmBM - 1) / avey::kGmBN + 1)
+             : g.n_nt;
+  return n;
+}
+
+int validate_gemm(const AveyGemmParams* p) {
+  if (!p) return fail(AVEY_ERR_ARGUMENT, "params is NULL");
+  if (p->struct_size != sizeof(AveyGemmParams))
+    return fail(AVEY_ERR_ARGUMENT, "struct_size %u != sizeof(AveyGemmParams) %zu", p->struct_size,
+                sizeof(AveyGemmParams));
+  if (p->dtype != AVEY_BF16 && p->dtype != AVEY_F16)
+    return fail(AVEY_ERR_ARGUMENT, "avey_gemm_v1 takes bf16 or f16 operands (dtype %d)", p->dtype);
+  if (p->out_dtype != AVEY_F32 && p->out_dtype != p->dtype)
+    return fail(AVEY_ERR_ARGUMENT, "out_dtype must be AVEY_F32 or the operand dtype");
+  if (p->mode < AVEY_GEMM_DENSE || p->mode > AVEY_GEMM_K_UPPER)
+    return fail(AVEY_ERR_ARGUMENT, "unknown mode %d", p->mode);
+  if (p->batch < 1 || p->m < 1 || p->n < 1 || p->k < 1 || p->batch > 65535 || p->m > (1 << 24) ||
+      p->n > (1 << 24) || p->k > (1 << 24))
+    return fail(AVEY_ERR_ARGUMENT, "batch, m, n, k must be in [1, 2^24] (batch <= 65535)");
+  if (!p->a || !p->b || !p->c) return fail(AVEY_ERR_ARGUMENT, "a, b and c are required");
+  if ((p->a_major != AVEY_MAJOR_K && p->a_major != AVEY_MAJOR_MN) ||
+      (p->b_major != AVEY_MAJOR_K && p->b_major != AVEY_MAJOR_MN))
+    return fail(AVEY_ERR_ARGUMENT, "a_major / b_major must be AVEY_MAJOR_K or AVEY_MAJOR_MN");
+  const int64_t a_inner = p->a_major == AVEY_MAJOR_K ? p->k : p->m;
+  const int64_t b_inner = p->b_major == AVEY_MAJOR_K ? p->k : p->n;
+  if (p->a_ld < a_inner || p->b_ld < b_inner || p->c_ld < p->n)
+    return fail(AVEY_ERR_ARGUMENT, "leading dimensions must be at least the contiguous extent");
+  if (p->a_batch_stride < 0 || p->b_batch_stride < 0 || p->c_batch_stride < 0)
+    return fail(AVEY_ERR_ARGUMENT, "negative batch strides are not supported");
+  const int es = 2, oes = p->out_dtype == AVEY_F32 ? 4 : 2;
+  auto whole16 = [](int64_t elems, int size) { return (elems * size) % 16 == 0; };
+  if (!aligned16(p->a) || !aligned16(p->b) || !aligned16(p->c) || !whole16(p->a_ld, es) ||
+      !whole16(p->b_ld, es) || !whole16(p->c_ld, oes) || !whole16(p->a_batch_stride, es) ||
+      !whole16(p->b_batch_stride, es) || (p->batch > 1 && !whole16(p->c_batch_stride, oes)))
+    return fail(AVEY_ERR_ARGUMENT,
+                "avey_gemm_v1 needs 16-byte aligned bases and strides that are whole 16-byte units");
+  if (p->out_dtype == AVEY_F32 && (p->bias || p->gate || p->sumsq || p->activation != AVEY_ACT_IDENTITY))
+    return fail(AVEY_ERR_ARGUMENT, "bias, gate, activation and sumsq need a 16-bit output");
+  if (p->activation < 0 || p->activation > 4)
+    return fail(AVEY_ERR_ARGUMENT, "unknown activation %d", p->activation);
+  if (p->gate && (p->gate_ld < p->n || p->gate_batch_stride < 0))
+    return fail(AVEY_ERR_ARGUMENT, "gate strides must cover a [batch][m][n] array");
+  if (p->sumsq && (p->sumsq_col0 < 0 || p->sumsq_col0 % 128 != 0 || p->sumsq_col0 >= p->n))
+    return fail(AVEY_ERR_ARGUMENT, "sumsq_col0 must be a multiple of 128 below n");
+  return AVEY_OK;
+}
+
+template <typename T, bool OUT16, int ACT>
+int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
+  constexpr auto K = avey::tc_gemm<T, OUT16, ACT>;
+  const cudaError_t attr_err = smem_opt_in<K>(avey::kGmSmem);
+  if (attr_err != cudaSuccess)
+    return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  avey::GemmGeom g{};
+  g.batch = static_cast<int>(p->batch);
+  g.m = static_cast<int>(p->m);
+  g.n = static_cast<int>(p->n);
+  g.k = static_cast<int>(p->k);
+  g.n_mt = static_cast<int>((p->m + avey::kGmBM - 1) / avey::kGmBM);
+  g.n_nt = static_cast<int>((p->n + avey::kGmBN - 1) / avey::kGmBN);
+  g.mode = p->mode;
+  g.a_mn = p->a_major == AVEY_MAJOR_MN;
+  g.b_mn = p->b_major == AVEY_MAJOR_MN;
+  g.a_batched = p->a_batch_stride != 0 && p->batch > 1;
+  g.b_batched = p->b_batch_stride != 0 && p->batch > 1;
+  const int64_t tiles = gemm_tiles_per_batch(g) * p->batch;
+  if (tiles > (1ll << 30)) return fail(AVEY_ERR_ARGUMENT, "too many output tiles");
+  g.total_tiles = static_cast<int>(tiles);
+  g.has_bias = p->bias != nullptr;
+  g.has_gate = p->gate != nullptr;
+  g.bias = p->bias;
+  g.gate = p->gate;
+  g.gate_bs = p->gate_batch_stride;
+  g.gate_rs = p->gate_ld;
+  g.sumsq = p->sumsq;
+  g.sumsq_col0 = p->sumsq_col0;
+  // Operand maps: {contiguous extent, other extent, batch}; boxes of 64
+  // contiguous elements (128 bytes, 128-byte swizzle) by 128 rows (A, K-major),
+  // 256 rows (B, K-major) or 64 k rows (MN-major operands).
+  const uint64_t ab = g.a_batched ? static_cast<uint64_t>(p->batch) : 1u;
+  const uint64_t bb = g.b_batched ? static_cast<uint64_t>(p->batch) : 1u;
+  CUtensorMap map_a, map_b, map_c;
+  int rc = g.a_mn
+               ? encode_map_dims(p->dtype, p->a, p->m, p->k, ab, p->a_ld * 2, p->a_batch_stride * 2, 64, 64, &map_a)
+               : encode_map_dims(p->dtype, p->a, p->k, p->m, ab, p->a_ld * 2, p->a_batch_stride * 2, 64,
+                                 avey::kGmBM, &map_a);
+  if (rc != AVEY_OK) return rc;
+  rc = g.b_mn ? encode_map_dims(p->dtype, p->b, p->n, p->k, bb, p->b_ld * 2, p->b_batch_stride * 2, 64, 64, &map_b)
+              : encode_map_dims(p->dtype, p->b, p->k, p->n, bb, p->b_ld * 2, p->b_batch_stride * 2, 64,
+                                avey::kGmBN, &map_b);
+  if (rc != AVEY_OK) return rc;
+  const int oes = OUT16 ? 2 : 4;
+  rc = encode_map_dims(p->out_dtype, p->c, p->n, p->m, p->batch, p->c_ld * oes, p->c_batch_stride * oes, 32,
+                       32, &map_c);
+  if (rc != AVEY_OK) return rc;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
+  K<<<grid, avey::kGmThreads, avey::kGmSmem, stream>>>(map_a, map_b, map_c, g);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_gemm launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ok();
+}
+
+template <typename T>
+int launch_gemm_out(const AveyGemmParams* p, cudaStream_t stream) {
+  if (p->out_dtype == AVEY_F32) return launch_gemm<T, false, AVEY_ACT_IDENTITY>(p, stream);
+  switch (p->activation) {
+    case AVEY_ACT_RELU: return launch_gemm<T, true, AVEY_ACT_RELU>(p, stream);
+    case AVEY_ACT_RELU2: return launch_gemm<T, true, AVEY_ACT_RELU2>(p, stream);
+    case AVEY_ACT_SILU: return launch_gemm<T, true, AVEY_ACT_SILU>(p, stream);
+    case AVEY_ACT_GELU: return launch_gemm<T, true, AVEY_ACT_GELU>(p, stream);
+    default: return launch_gemm<T, true, AVEY_ACT_IDENTITY>(p, stream);
+  }
 }
 
 }  // namespace
@@ -774,6 +931,31 @@ int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
   q.workspace = g_noalloc_ptr[dev];
   q.workspace_bytes = static_cast<uint64_t>(AVEY_NOALLOC_MAX_ROWS) * sizeof(float);
   return avey_fwd_v1(&q, stream);
+}
+
+int avey_gemm_v1(const AveyGemmParams* p, void* stream) {
+  int rc = validate_gemm(p);
+  if (rc != AVEY_OK) return rc;
+  rc = device_arch_ok(nullptr);
+  if (rc != AVEY_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return p->dtype == AVEY_BF16 ? launch_gemm_out<__nv_bfloat16>(p, s) : launch_gemm_out<__half>(p, s);
+}
+
+int avey_fwd_presummed_v1(const AveyFwdParams* p, const float* sumsq, int planes, void* stream_ptr) {
+  AveyPlan plan;
+  int rc = avey_fwd_plan(p, &plan);
+  if (rc != AVEY_OK) return rc;
+  if (!sumsq || planes < 1 || planes > 64)
+    return fail(AVEY_ERR_ARGUMENT, "sumsq must hold 1 to 64 planes of row sums of squares");
+  // Paths without the row-sum pre-pass (CUDA cores, 3xTF32) ignore the sums.
+  if (plan.kernel != AVEY_KERNEL_TCGEN05 || is_tf32(p)) return avey_fwd_v1(p, stream_ptr);
+  rc = device_arch_ok(nullptr);
+  if (rc != AVEY_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const PreSum ps{sumsq, planes};
+  return p->dtype == AVEY_BF16 ? launch_tc_act<__nv_bfloat16>(p, stream, ps)
+                               : launch_tc_act<__half>(p, stream, ps);
 }
 
 const char* avey_last_error(void) { return g_last_error.c_str(); }

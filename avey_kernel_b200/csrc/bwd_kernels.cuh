@@ -788,7 +788,9 @@ __device__ __forceinline__ void ds_compute(const BwdArgs& a, const DsIn& x, int 
     rk[e] = in ? 1.f / fmaxf(ns[e], ne) : 0.f;
     const bool ok = in && (!a.causal || j + e <= i) && ns[e] >= 0.f;  // padding has norm -1
     const float dsm = ok ? xs[e] + x.dd : 0.f;
-    acc[e] = fmaf(dsm, gs[e] * rq * rk[e], acc[e]);
+    // Selected, not multiplied by zero: under the causal mask the tiles of Gr
+    // and ds0 above the diagonal may be left unwritten by their GEMMs.
+    if (ok) acc[e] = fmaf(dsm, gs[e] * rq * rk[e], acc[e]);
     dg[e] = dsm * v[e];
   }
 }

@@ -81,4 +81,20 @@ __global__ void __launch_bounds__(kPrepassThreads) norm_prepass(const FwdArgs ar
   }
 }
 
+// The pre-summed form (avey_fwd_presummed_v1): the producer of z_tr (the
+// enricher's GEMM epilogue) already wrote the row sums of squares as partial
+// planes of `rows` floats; they are added in plane order into the workspace
+// (4 bytes per plane and row instead of a pass over z_tr). Launched where
+// norm_prepass would be, with the same programmatic dependent launch.
+__global__ void __launch_bounds__(kPrepassThreads)
+    sumsq_planes(const float* __restrict__ planes, int nplanes, int64_t rows, float* __restrict__ out) {
+  griddep_launch_dependents();
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kPrepassThreads + threadIdx.x; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * kPrepassThreads) {
+    float s = 0.f;
+    for (int p = 0; p < nplanes; ++p) s += __ldg(planes + p * rows + r);
+    out[r] = s;
+  }
+}
+
 }  // namespace avey

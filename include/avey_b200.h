@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define AVEY_ABI_VERSION 4
+#define AVEY_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define AVEY_API __attribute__((visibility("default")))
@@ -267,6 +267,100 @@ typedef struct AveyBwdParams {
 /* Enqueue one backward step on `stream`. Returns AVEY_OK or a negative
  * AveyStatus; the pointers a step reads or writes must be set. */
 AVEY_API int avey_bwd_step_v1(const AveyBwdParams* params, int step, void* stream);
+
+/*
+ * Batched matrix product on the tcgen05 tensor cores (no counterpart in the
+ * reference, which computes its products with torch.matmul / tl.dot): for
+ * every batch entry b,
+ *
+ *   C[b] = A[b] B[b]                              out_dtype AVEY_F32, or
+ *   C[b] = act(A[b] B[b] + bias) (.) gate[b]      out_dtype == dtype (16-bit)
+ *
+ * with A [m x k] and B [k x n] of `dtype` (AVEY_BF16 or AVEY_F16) and fp32
+ * accumulation. It runs the contractions of the backward steps above
+ * (avey_kernel_b200/backward.py), the enricher projection that feeds
+ * avey_fwd_v1 (with the row sums of squares of its tail columns, see
+ * avey_fwd_presummed_v1) and the static layers.
+ *
+ * Layouts (strides in elements, each operand's contiguous dimension has
+ * stride 1):
+ *   A: a_major AVEY_MAJOR_K:  A[b][i][k] at a + b*a_batch_stride + i*a_ld + k
+ *      a_major AVEY_MAJOR_MN: A[b][i][k] at a + b*a_batch_stride + k*a_ld + i
+ *   B: b_major AVEY_MAJOR_K:  B[b][k][j] at b + b*b_batch_stride + j*b_ld + k
+ *      b_major AVEY_MAJOR_MN: B[b][k][j] at b + b*b_batch_stride + k*b_ld + j
+ *   C: C[b][i][j] at c + b*c_batch_stride + i*c_ld + j
+ * A batch stride of 0 shares the operand across the batch. Base addresses
+ * must be 16-byte aligned and every ld / batch stride a whole number of 16
+ * bytes (TMA); k, m and n are otherwise free (edges are zero-filled).
+ *
+ * mode skips work that the causal structure makes unnecessary:
+ *   AVEY_GEMM_DENSE      every C[b][i][j];
+ *   AVEY_GEMM_LOWER_OUT  only C[b][i][j] with j <= i is wanted: 128 x 256
+ *                        output tiles wholly above the diagonal are not
+ *                        computed and not written (their memory keeps
+ *                        whatever it held);
+ *   AVEY_GEMM_K_LOWER    A[b][i][k] == 0 for k > i (lower-triangular A): the
+ *                        K loop of each 128-row tile stops after its last row;
+ *   AVEY_GEMM_K_UPPER    A[b][i][k] == 0 for k < i: the K loop of each
+ *                        128-row tile starts at its first row.
+ * The K-range modes give the dense result bit for bit (the skipped terms are
+ * exact zeros).
+ *
+ * 16-bit output only: bias [n] (or NULL), activation (AveyActivation), gate
+ * (same shape as C, or NULL), and sumsq: NULL, or n_planes = ceil((n -
+ * sumsq_col0) / 128) planes of batch*m floats, plane p holding for every row
+ * the sum of squares of the stored (rounded) outputs of columns
+ * [sumsq_col0 + 128p, sumsq_col0 + 128p + 128) (sumsq_col0 a multiple of 128;
+ * sums in a fixed order, bitwise reproducible).
+ */
+typedef enum AveyMajor {
+  AVEY_MAJOR_K = 0,
+  AVEY_MAJOR_MN = 1,
+} AveyMajor;
+
+typedef enum AveyGemmMode {
+  AVEY_GEMM_DENSE = 0,
+  AVEY_GEMM_LOWER_OUT = 1,
+  AVEY_GEMM_K_LOWER = 2,
+  AVEY_GEMM_K_UPPER = 3,
+} AveyGemmMode;
+
+typedef struct AveyGemmParams {
+  uint32_t struct_size; /* sizeof(AveyGemmParams) */
+  int32_t dtype;        /* operands: AVEY_BF16 or AVEY_F16 */
+  int32_t out_dtype;    /* AVEY_F32, or dtype */
+  int32_t mode;         /* AveyGemmMode */
+  int64_t batch, m, n, k;
+  const void* a;
+  int64_t a_batch_stride, a_ld;
+  int32_t a_major; /* AveyMajor */
+  const void* b;
+  int64_t b_batch_stride, b_ld;
+  int32_t b_major; /* AveyMajor */
+  void* c;
+  int64_t c_batch_stride, c_ld;
+  const void* bias; /* [n] of dtype, or NULL (16-bit output only) */
+  const void* gate; /* [batch][m][n] of dtype, or NULL (16-bit output only) */
+  int64_t gate_batch_stride, gate_ld;
+  int32_t activation; /* AveyActivation (16-bit output only) */
+  int32_t sumsq_col0; /* first column of the row sums of squares */
+  float* sumsq;       /* planes of row sums of squares, or NULL */
+} AveyGemmParams;
+
+AVEY_API int avey_gemm_v1(const AveyGemmParams* params, void* stream);
+
+/*
+ * avey_fwd_v1 with the row sums of squares of z_tr supplied by the caller
+ * (no counterpart in the reference, whose normalisation pre-pass,
+ * ops.py:107-108, is always a separate pass over z_tr): `sumsq` holds
+ * `planes` planes of batch*context floats, summed in plane order, as written
+ * by the enricher's avey_gemm_v1 epilogue (its tail columns). The norm
+ * pre-pass of the tcgen05 path is skipped; other paths ignore the sums.
+ * params->workspace is still required (the pre-summed planes are read, never
+ * written).
+ */
+AVEY_API int avey_fwd_presummed_v1(const AveyFwdParams* params, const float* sumsq, int planes,
+                                   void* stream);
 
 /* Bytes of `workspace` the backward steps need for these parameters. */
 AVEY_API int avey_bwd_workspace_size(const AveyBwdParams* params, uint64_t* bytes);

@@ -22,7 +22,7 @@ def header_functions():
 
 def test_library_loads_and_reports_abi_version():
     dll = _native.lib()
-    assert dll.avey_abi_version() == _native.ABI_VERSION == 4
+    assert dll.avey_abi_version() == _native.ABI_VERSION == 5
 
 
 def test_every_header_function_is_exported():

@@ -21,10 +21,10 @@ from avey_kernel_b200 import _native, ops
 from helpers import TOL, norm_rel_err, to_numpy
 
 
-def _call(z_tr, v, z_tl, bias, valid, *, causal, normalize, act, noalloc):
+def _call(z_tr, v, z_tl, bias, valid, *, causal, normalize, act, noalloc, kernel=0):
     out = torch.empty(z_tr.shape, dtype=z_tr.dtype, device=z_tr.device)
     params = ops.build_params(z_tr, v, z_tl, bias, valid, out, eps=1e-6, norm_eps=1e-12,
-                              causal=causal, normalize=normalize, activation_id=act)
+                              causal=causal, normalize=normalize, activation_id=act, kernel=kernel)
     stream = torch.cuda.current_stream().cuda_stream
     if noalloc:
         _native.forward_noalloc(params, stream)  # params.workspace stays NULL
@@ -119,10 +119,14 @@ def test_noalloc_entry_point_runs_long_contexts_on_cuda_cores():
 @pytest.mark.gpu
 def test_noalloc_entry_point_runs_cuda_core_inputs_past_the_row_limit():
     # The CUDA-core kernels read no scratch, so the row limit does not apply:
-    # fp32 input with more rows than the array holds.
+    # fp32 input with more rows than the array holds. avey_fwd_v1 would run
+    # fp32 on the 3xTF32 tensor-core pair (with a P workspace); this entry
+    # point runs it on CUDA cores, so the bitwise comparison forces that
+    # kernel on the workspace entry point too.
     z = torch.rand(_native.NOALLOC_MAX_ROWS // 64 + 1, 64, 8, device='cuda')
     got = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=True)
-    want = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=False)
+    want = _call(z, None, None, None, None, causal=False, normalize=True, act=0, noalloc=False,
+                 kernel=_native.KERNEL_SIMT)
     assert torch.equal(got, want)
 
 
