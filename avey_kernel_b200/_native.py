@@ -144,6 +144,7 @@ class AveyGemmParams(ctypes.Structure):
         ('activation', ctypes.c_int32),
         ('sumsq_col0', ctypes.c_int32),
         ('sumsq', ctypes.c_void_p),
+        ('kernel', ctypes.c_int32),
     ]
 
 

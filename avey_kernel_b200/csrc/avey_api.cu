@@ -662,7 +662,7 @@ int64_t gemm_tiles_per_batch(const avey::GemmGeom& g) {
   int64_t n = 0;
   for (int mt = 0; mt < g.n_mt; ++mt)
     n += g.mode == avey::kGemmLowerOut
-             ? std::min<int64_t>(g.n_nt, (mt * avey::kGmBM + avey::kGmBM - 1) / avey::kGmBN + 1)
+             ? std::min<int64_t>(g.n_nt, (static_cast<int64_t>(mt) * g.bm + g.bm - 1) / avey::kGmBN + 1)
              : g.n_nt;
   return n;
 }
@@ -706,13 +706,21 @@ int validate_gemm(const AveyGemmParams* p) {
     return fail(AVEY_ERR_ARGUMENT, "gate strides must cover a [batch][m][n] array");
   if (p->sumsq && (p->sumsq_col0 < 0 || p->sumsq_col0 % 128 != 0 || p->sumsq_col0 >= p->n))
     return fail(AVEY_ERR_ARGUMENT, "sumsq_col0 must be a multiple of 128 below n");
+  if (p->kernel < AVEY_GEMM_KERNEL_AUTO || p->kernel > AVEY_GEMM_KERNEL_PAIR)
+    return fail(AVEY_ERR_ARGUMENT, "unknown GEMM kernel %d", p->kernel);
   return AVEY_OK;
 }
 
 template <typename T, bool OUT16, int ACT>
 int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
-  constexpr auto K = avey::tc_gemm<T, OUT16, ACT>;
-  const cudaError_t attr_err = smem_opt_in<K>(avey::kGmSmem);
+  // AUTO: pairs for K-major B (measured faster: g = zm zm^T 27.8 against
+  // 28.9 us, the enricher shape 81.8 against 85.0 us); with an MN-major B the
+  // pair measured slower (num = s zm 43.6 against 36.9 us), so one CTA per tile.
+  const bool pair = p->kernel == AVEY_GEMM_KERNEL_PAIR ||
+                    (p->kernel == AVEY_GEMM_KERNEL_AUTO && p->m > 128 && p->b_major == AVEY_MAJOR_K);
+  constexpr auto K1 = avey::tc_gemm<T, OUT16, ACT>;
+  constexpr auto K2 = avey::tc_gemm_pair<T, OUT16, ACT>;
+  const cudaError_t attr_err = pair ? smem_opt_in<K2>(avey::kG2Smem) : smem_opt_in<K1>(avey::kGmSmem);
   if (attr_err != cudaSuccess)
     return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
   avey::GemmGeom g{};
@@ -720,7 +728,8 @@ int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
   g.m = static_cast<int>(p->m);
   g.n = static_cast<int>(p->n);
   g.k = static_cast<int>(p->k);
-  g.n_mt = static_cast<int>((p->m + avey::kGmBM - 1) / avey::kGmBM);
+  g.bm = pair ? 256 : avey::kGmBM;
+  g.n_mt = static_cast<int>((p->m + g.bm - 1) / g.bm);
   g.n_nt = static_cast<int>((p->n + avey::kGmBN - 1) / avey::kGmBN);
   g.mode = p->mode;
   g.a_mn = p->a_major == AVEY_MAJOR_MN;
@@ -749,17 +758,37 @@ int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
                : encode_map_dims(p->dtype, p->a, p->k, p->m, ab, p->a_ld * 2, p->a_batch_stride * 2, 64,
                                  avey::kGmBM, &map_a);
   if (rc != AVEY_OK) return rc;
+  // K-major B: each CTA of a pair loads 128 of the tile's 256 columns.
   rc = g.b_mn ? encode_map_dims(p->dtype, p->b, p->n, p->k, bb, p->b_ld * 2, p->b_batch_stride * 2, 64, 64, &map_b)
               : encode_map_dims(p->dtype, p->b, p->k, p->n, bb, p->b_ld * 2, p->b_batch_stride * 2, 64,
-                                avey::kGmBN, &map_b);
+                                pair ? 128 : avey::kGmBN, &map_b);
   if (rc != AVEY_OK) return rc;
   const int oes = OUT16 ? 2 : 4;
   rc = encode_map_dims(p->out_dtype, p->c, p->n, p->m, p->batch, p->c_ld * oes, p->c_batch_stride * oes, 32,
                        32, &map_c);
   if (rc != AVEY_OK) return rc;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
-  K<<<grid, avey::kGmThreads, avey::kGmSmem, stream>>>(map_a, map_b, map_c, g);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  if (!pair) {
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
+    K1<<<grid, avey::kGmThreads, avey::kGmSmem, stream>>>(map_a, map_b, map_c, g);
+    e = cudaGetLastError();
+  } else {
+    // Persistent CTA pairs: (2, 1, 1) clusters, one pair per two SMs.
+    const int pairs = static_cast<int>(std::min<int64_t>(tiles, sm_count() / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    cfg.blockDim = dim3(avey::kGmThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(avey::kG2Smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, K2, map_a, map_b, map_c, g);
+  }
   if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_gemm launch: %s", cudaGetErrorString(e));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return ok();

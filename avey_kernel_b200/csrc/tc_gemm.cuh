@@ -48,6 +48,7 @@ enum GemmMode { kGemmDense = 0, kGemmLowerOut = 1, kGemmKLower = 2, kGemmKUpper 
 
 struct GemmGeom {
   int batch, m, n, k;
+  int bm;               // rows per output tile: 128 (one CTA) or 256 (a CTA pair)
   int n_mt, n_nt;       // row and column tiles per batch entry
   int mode;             // GemmMode
   int a_mn, b_mn;       // operand is MN-major (else K-major)
@@ -77,7 +78,7 @@ struct GemmTile {
 // Output tiles per row tile: all of them, or under kGemmLowerOut those with a
 // column at or below the tile's last row.
 __device__ __forceinline__ int gemm_cols_of(const GemmGeom& g, int mt) {
-  return g.mode == kGemmLowerOut ? min(g.n_nt, (mt * kGmBM + kGmBM - 1) / kGmBN + 1) : g.n_nt;
+  return g.mode == kGemmLowerOut ? min(g.n_nt, (mt * g.bm + g.bm - 1) / kGmBN + 1) : g.n_nt;
 }
 
 // Tile t of the launch: row tiles in order (the longest K ranges first under
@@ -99,8 +100,8 @@ __device__ __forceinline__ GemmTile gemm_tile(const GemmGeom& g, int t) {
     rem -= per;
   }
   int klo = 0, khi = g.k;
-  if (g.mode == kGemmKLower) khi = min(g.k, (c.mt + 1) * kGmBM);
-  if (g.mode == kGemmKUpper) klo = min(g.k, c.mt * kGmBM);
+  if (g.mode == kGemmKLower) khi = min(g.k, (c.mt + 1) * g.bm);
+  if (g.mode == kGemmKUpper) klo = min(g.k, c.mt * g.bm);
   c.k0 = klo / kGmBK;
   c.nk = khi > klo ? (khi - c.k0 * kGmBK + kGmBK - 1) / kGmBK : 0;
   return c;
@@ -112,6 +113,104 @@ __device__ __forceinline__ void st_stage_f32(uint32_t stage, int lane, const uin
   for (int q = 0; q < 8; ++q)
     st_shared_v4(stage + lane * 128 + ((q ^ (lane & 7)) << 4), o[4 * q], o[4 * q + 1], o[4 * q + 2],
                  o[4 * q + 3]);
+}
+
+// Drain this warp's 32 rows (first row `row0`) x 128 columns (half `h` of the
+// 256-column tile) of one accumulator (`tb`: TMEM address of column 0 of the
+// buffer in this warp's lane quarter) into C, then release the accumulator by
+// one arrival on `acc_empty` (a shared::cluster address: this CTA's barrier or
+// the pair leader's). fp32 output: 32 x 32 tiles through the staging tile and
+// TMA stores; 16-bit output: bias, activation, gate, row sums of squares.
+template <typename T, bool OUT16, int ACT, bool PAIR>
+__device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTile& c, int row0,
+                                                uint32_t tb0, int h, int lane, uint32_t stage,
+                                                const CUtensorMap* map_c, uint64_t stream,
+                                                uint32_t acc_empty) {
+  const int m = row0 + lane;
+  const int n_half = c.nt * kGmBN + h * 128;
+  const uint32_t tb = tb0 + static_cast<uint32_t>(h * 128);
+  const bool rows_in = row0 < g.m;
+  float ss = 0.f;  // row sum of squares over this half's columns (16-bit output)
+  const T* grow = nullptr;
+  if (OUT16 && g.has_gate && m < g.m)
+    grow = static_cast<const T*>(g.gate) + static_cast<int64_t>(c.b) * g.gate_bs +
+           static_cast<int64_t>(m) * g.gate_rs;
+#pragma unroll 1
+  for (int ch = 0; ch < 4; ++ch) {
+    const int n0 = n_half + ch * 32;
+    if (n0 >= g.n) break;  // uniform across the warp
+    uint32_t o[32];
+    if (c.nk > 0) {
+      tmem_ld32(tb + ch * 32, o);
+      tmem_wait_ld(o);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 32; ++q) o[q] = 0u;
+    }
+    if constexpr (!OUT16) {
+      if (lane == 0) bulk_wait_read_all();  // the previous store has read the tile
+      __syncwarp();
+      st_stage_f32(stage, lane, o);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && rows_in) {
+        tma_store_3d(map_c, stage, n0, row0, c.b, stream);
+        bulk_commit_group();
+      }
+    } else {
+      float bv[32];
+      if (g.has_bias) {
+        const T* bp = static_cast<const T*>(g.bias) + n0;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) bv[q] = n0 + q < g.n ? to_f32<T>(bp[q]) : 0.f;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) bv[q] = 0.f;
+      }
+      uint32_t gw[16];
+      if (grow)
+        load_raw32<T>(grow + n0, g.n - n0,
+                      (g.gate_rs & 7) == 0 && (g.gate_bs & 7) == 0 &&
+                          (reinterpret_cast<uintptr_t>(g.gate) & 15u) == 0,
+                      gw, stream);
+      const bool want_ss = g.sumsq && n0 >= g.sumsq_col0;
+      uint32_t pk[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        float y0 = act_fn<ACT>(__uint_as_float(o[2 * q]) + bv[2 * q]);
+        float y1 = act_fn<ACT>(__uint_as_float(o[2 * q + 1]) + bv[2 * q + 1]);
+        if (grow) {
+          y0 *= raw_at<T>(gw, 2 * q);
+          y1 *= raw_at<T>(gw, 2 * q + 1);
+        }
+        pk[q] = pack2<T>(y0, y1);
+        if (want_ss) {
+          // Squares of the stored (rounded) values, columns past n excluded.
+          const uint16_t lo = static_cast<uint16_t>(pk[q] & 0xFFFFu), hi = static_cast<uint16_t>(pk[q] >> 16);
+          const float r0 = to_f32<T>(*reinterpret_cast<const T*>(&lo));
+          const float r1 = to_f32<T>(*reinterpret_cast<const T*>(&hi));
+          if (n0 + 2 * q < g.n) ss = fmaf(r0, r0, ss);
+          if (n0 + 2 * q + 1 < g.n) ss = fmaf(r1, r1, ss);
+        }
+      }
+      if (lane == 0) bulk_wait_read_1();  // two tiles per warp: the store two chunks back is done
+      __syncwarp();
+      if (rows_in) warp_tile_store(stage + (ch & 1) * 2048, pk, map_c, n0, row0, c.b, stream, lane);
+    }
+  }
+  // The accumulator has been read: the MMA may refill it.
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) {
+    if (PAIR)
+      mbar_arrive_cluster(acc_empty);
+    else
+      mbar_arrive(acc_empty);
+  }
+  if (OUT16 && g.sumsq && n_half >= g.sumsq_col0 && n_half < g.n && m < g.m) {
+    const int plane = (n_half - g.sumsq_col0) / 128;
+    g.sumsq[static_cast<int64_t>(plane) * g.batch * g.m + static_cast<int64_t>(c.b) * g.m + m] = ss;
+  }
 }
 
 template <typename T, bool OUT16, int ACT>
@@ -248,86 +347,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       const int buf = it & 1;
       if (!mbar_wait(smem_u32(&ctrl->acc_full[buf]), (it >> 1) & 1)) break;
       tc_fence_after();
-      const int row0 = c.mt * kGmBM + wq * 32;
-      const int m = row0 + lane;
-      const int n_half = c.nt * kGmBN + h * 128;
-      const uint32_t tb = tmem + lane_off + static_cast<uint32_t>(buf * kGmBN + h * 128);
-      const bool rows_in = row0 < g.m;
-      float ss = 0.f;  // row sum of squares over this half's columns (16-bit output)
-      const T* grow = nullptr;
-      if (OUT16 && g.has_gate && m < g.m)
-        grow = static_cast<const T*>(g.gate) + static_cast<int64_t>(c.b) * g.gate_bs +
-               static_cast<int64_t>(m) * g.gate_rs;
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        const int n0 = n_half + ch * 32;
-        if (n0 >= g.n) break;  // uniform across the warp
-        uint32_t o[32];
-        if (c.nk > 0) {
-          tmem_ld32(tb + ch * 32, o);
-          tmem_wait_ld(o);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 32; ++q) o[q] = 0u;
-        }
-        if constexpr (!OUT16) {
-          if (lane == 0) bulk_wait_read_all();  // the previous store has read the tile
-          __syncwarp();
-          st_stage_f32(stage, lane, o);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && rows_in) {
-            tma_store_3d(&map_c, stage, n0, row0, c.b, stream);
-            bulk_commit_group();
-          }
-        } else {
-          float bv[32];
-          if (g.has_bias) {
-            const T* bp = static_cast<const T*>(g.bias) + n0;
-#pragma unroll
-            for (int q = 0; q < 32; ++q) bv[q] = n0 + q < g.n ? to_f32<T>(bp[q]) : 0.f;
-          } else {
-#pragma unroll
-            for (int q = 0; q < 32; ++q) bv[q] = 0.f;
-          }
-          uint32_t gw[16];
-          if (grow) load_raw32<T>(grow + n0, g.n - n0, (g.gate_rs & 7) == 0 && (g.gate_bs & 7) == 0 &&
-                                                           (reinterpret_cast<uintptr_t>(g.gate) & 15u) == 0,
-                                  gw, stream);
-          const bool want_ss = g.sumsq && n0 >= g.sumsq_col0;
-          uint32_t pk[16];
-#pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            float y0 = act_fn<ACT>(__uint_as_float(o[2 * q]) + bv[2 * q]);
-            float y1 = act_fn<ACT>(__uint_as_float(o[2 * q + 1]) + bv[2 * q + 1]);
-            if (grow) {
-              y0 *= raw_at<T>(gw, 2 * q);
-              y1 *= raw_at<T>(gw, 2 * q + 1);
-            }
-            pk[q] = pack2<T>(y0, y1);
-            if (want_ss) {
-              // Squares of the stored (rounded) values, columns past n excluded.
-              const uint16_t lo = static_cast<uint16_t>(pk[q] & 0xFFFFu), hi = static_cast<uint16_t>(pk[q] >> 16);
-              const float r0 = to_f32<T>(*reinterpret_cast<const T*>(&lo));
-              const float r1 = to_f32<T>(*reinterpret_cast<const T*>(&hi));
-              if (n0 + 2 * q < g.n) ss = fmaf(r0, r0, ss);
-              if (n0 + 2 * q + 1 < g.n) ss = fmaf(r1, r1, ss);
-            }
-          }
-          if (lane == 0) bulk_wait_read_1();  // two tiles per warp: the store two chunks back is done
-          __syncwarp();
-          if (rows_in)
-            warp_tile_store(stage + (ch & 1) * 2048, pk, &map_c, n0, row0, c.b, stream, lane);
-        }
-      }
-      // The accumulator has been read: the MMA may refill it.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctrl->acc_empty[buf]));
-      if (OUT16 && g.sumsq && n_half >= g.sumsq_col0 && n_half < g.n && m < g.m) {
-        const int plane = (n_half - g.sumsq_col0) / 128;
-        g.sumsq[static_cast<int64_t>(plane) * g.batch * g.m + static_cast<int64_t>(c.b) * g.m + m] = ss;
-      }
+      gemm_drain_tile<T, OUT16, ACT, false>(g, c, c.mt * g.bm + wq * 32, tmem + lane_off + static_cast<uint32_t>(buf * kGmBN),
+                                     h, lane, stage, &map_c, stream,
+                                     smem_u32(&ctrl->acc_empty[buf]));
     }
     if (lane == 0) bulk_wait_read_all();
   }
@@ -338,6 +360,205 @@ __global__ void __launch_bounds__(kGmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================
+// The same product on CTA pairs (cta_group::2): a (2, 1, 1) cluster computes
+// 256 x 256 output tiles, the even CTA (rank 0) holding rows 0-127 and the
+// odd one rows 128-255. Each CTA loads its own 128 rows of the A tile and its
+// half of the B tile's 256 columns (16 KB + 16 KB per 64-wide K block), so a
+// CTA moves half the B bytes of the single-CTA kernel per MMA cycle; rank 0
+// issues the M = 256 MMAs for both. Six 32 KB stages per CTA.
+//
+// Barriers: full[s] of rank 0 counts both CTAs' TMA bytes (their loads name
+// it through its shared::cluster address); empty[s] and acc_full[b] of both
+// CTAs are signalled by rank 0's commits (one commit per CTA, no multicast);
+// acc_empty[b] of rank 0 counts the epilogue warps of both CTAs. Every wait
+// is bounded, and both CTAs always reach the final cluster barrier.
+// ============================================================================
+constexpr int kG2Stages = 6;
+constexpr int kG2HalfBytes = 128 * kGmBK * 2;          // 16 KB: 128 rows (A) or N-columns (B)
+constexpr int kG2StageBytes = 2 * kG2HalfBytes;         // 32 KB per CTA
+constexpr int kG2Smem = 1024 + kG2Stages * kG2StageBytes + 8 * kGmStageTile + kGmCtrlBytes;
+
+struct Gemm2Ctrl {
+  uint64_t full[kG2Stages], empty[kG2Stages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+};
+static_assert(sizeof(Gemm2Ctrl) <= kGmCtrlBytes, "control block too large");
+
+template <typename T, bool OUT16, int ACT>
+__global__ void __launch_bounds__(kGmThreads, 1)
+    tc_gemm_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 const __grid_constant__ CUtensorMap map_c, const GemmGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw);
+  const uint32_t stages = base;
+  const uint32_t staging = base + kG2Stages * kG2StageBytes;
+  Gemm2Ctrl* ctrl = reinterpret_cast<Gemm2Ctrl*>(base_ptr + kG2Stages * kG2StageBytes + 8 * kGmStageTile);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  if (tid == 0) {
+    for (int s = 0; s < kG2Stages; ++s) {
+      mbar_init(smem_u32(&ctrl->full[s]), 1);
+      mbar_init(smem_u32(&ctrl->empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&ctrl->acc_full[i]), 1);
+      mbar_init(smem_u32(&ctrl->acc_empty[i]), 16);  // 8 epilogue warps in each CTA
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    tma_prefetch_desc(&map_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&ctrl->tmem_base), 512);
+    tmem_relinquish_pair();
+  }
+  // Both CTAs' barriers are initialised and the TMEM is allocated before
+  // either CTA signals the other.
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = ctrl->tmem_base;
+  const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+
+  if (warp == 0) {
+    // ============================================================ TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t keep = l2_policy_evict_last();
+      int st = 0, fills = 0;
+      uint32_t ph = 0;
+      bool alive = true;
+      for (int t = pair; t < g.total_tiles && alive; t += npairs) {
+        const GemmTile c = gemm_tile(g, t);
+        const int ab = g.a_batched ? c.b : 0, bb = g.b_batched ? c.b : 0;
+        const int arow = c.mt * 256 + static_cast<int>(rank) * 128;  // this CTA's A rows
+        const int bcol = c.nt * kGmBN + static_cast<int>(rank) * 128;  // this CTA's B columns
+        for (int kk = 0; kk < c.nk; ++kk) {
+          if (fills >= kG2Stages && !mbar_wait(smem_u32(&ctrl->empty[st]), ph ^ 1u)) {
+            alive = false;
+            break;
+          }
+          const uint32_t full = mapa_shared(smem_u32(&ctrl->full[st]), 0);
+          const uint32_t sa = stages + st * kG2StageBytes, sb = sa + kG2HalfBytes;
+          const int kx = (c.k0 + kk) * kGmBK;
+          if (leader) mbar_arrive_expect_tx(smem_u32(&ctrl->full[st]), 2 * kG2StageBytes);
+          if (!g.a_mn) {
+            tma_load_3d_pair(sa, &map_a, full, kx, arow, ab, keep);
+          } else {
+            tma_load_3d_pair(sa, &map_a, full, arow, kx, ab, keep);
+            tma_load_3d_pair(sa + kGmMnBox, &map_a, full, arow + 64, kx, ab, keep);
+          }
+          if (!g.b_mn) {
+            tma_load_3d_pair(sb, &map_b, full, kx, bcol, bb, keep);
+          } else {
+            tma_load_3d_pair(sb, &map_b, full, bcol, kx, bb, keep);
+            tma_load_3d_pair(sb + kGmMnBox, &map_b, full, bcol + 64, kx, bb, keep);
+          }
+          ++fills;
+          if (++st == kG2Stages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Wait until every stage this CTA filled has been released by the
+      // leader's commits, so none of them is still in flight when it exits.
+      for (int i = 0; i < kG2Stages && i < fills && alive; ++i) {
+        // Stage (st - 1 - i) mod S was filled last in its own phase.
+        const int s = (st - 1 - i + kG2Stages) % kG2Stages;
+        const int uses = (fills - 1 - i) / kG2Stages;  // index of that stage's last fill
+        if (!mbar_wait(smem_u32(&ctrl->empty[s]), uses & 1)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer (rank 0 only)
+    if (lane == 0 && leader) {
+      const uint32_t idesc = idesc_f16(fmt, 256, kGmBN, static_cast<uint32_t>(g.a_mn),
+                                       static_cast<uint32_t>(g.b_mn));
+      const uint64_t da0 = g.a_mn ? smem_desc_sw128(stages, kGmMnBox, 1024) : smem_desc_sw128(stages, 16, 1024);
+      const uint64_t db0 = g.b_mn ? smem_desc_sw128(stages + kG2HalfBytes, kGmMnBox, 1024)
+                                  : smem_desc_sw128(stages + kG2HalfBytes, 16, 1024);
+      const uint32_t ka = g.a_mn ? (2048u >> 4) : 2u, kb = g.b_mn ? (2048u >> 4) : 2u;
+      int st = 0, it = 0;
+      uint32_t ph = 0;
+      bool alive = true;
+      for (int t = pair; t < g.total_tiles && alive; t += npairs, ++it) {
+        const GemmTile c = gemm_tile(g, t);
+        const int buf = it & 1;
+        if (it >= 2) {
+          if (!mbar_wait(smem_u32(&ctrl->acc_empty[buf]), ((it >> 1) - 1) & 1)) break;
+          tc_fence_after();
+        }
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * kGmBN);
+        for (int kk = 0; kk < c.nk; ++kk) {
+          if (!mbar_wait(smem_u32(&ctrl->full[st]), ph)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t adv = static_cast<uint32_t>(st * kG2StageBytes) >> 4;
+#pragma unroll
+          for (int k = 0; k < kGmBK / 16; ++k)
+            tc_mma_f16_pair(d_tmem, da0 + adv + ka * k, db0 + adv + kb * k, idesc,
+                            (kk != 0 || k != 0) ? 1u : 0u);
+          tc_commit_pair(smem_u32(&ctrl->empty[st]));
+          tc_commit_pair(mapa_shared(smem_u32(&ctrl->empty[st]), 1));
+          if (++st == kG2Stages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!alive) break;
+        if (c.nk == 0) {  // empty K range: the tile is zero
+          mbar_arrive(smem_u32(&ctrl->acc_full[buf]));
+          mbar_arrive_cluster(mapa_shared(smem_u32(&ctrl->acc_full[buf]), 1));
+        } else {
+          tc_commit_pair(smem_u32(&ctrl->acc_full[buf]));
+          tc_commit_pair(mapa_shared(smem_u32(&ctrl->acc_full[buf]), 1));
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ============================================================ epilogue (both CTAs)
+    const int h = (warp - 4) >> 2;
+    const int wq = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t stage = staging + static_cast<uint32_t>((warp - 4) * kGmStageTile);
+    const uint64_t stream = l2_policy_evict_normal();
+    int it = 0;
+    for (int t = pair; t < g.total_tiles; t += npairs, ++it) {
+      const GemmTile c = gemm_tile(g, t);
+      const int buf = it & 1;
+      if (!mbar_wait(smem_u32(&ctrl->acc_full[buf]), (it >> 1) & 1)) break;
+      tc_fence_after();
+      gemm_drain_tile<T, OUT16, ACT, true>(g, c, c.mt * 256 + static_cast<int>(rank) * 128 + wq * 32,
+                                           tmem + lane_off + static_cast<uint32_t>(buf * kGmBN), h, lane,
+                                           stage, &map_c, stream,
+                                           mapa_shared(smem_u32(&ctrl->acc_empty[buf]), 0));
+    }
+    if (lane == 0) bulk_wait_read_all();
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // no signal targets either CTA after this point
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 

@@ -26,6 +26,7 @@ from . import _native
 
 DENSE, LOWER_OUT, K_LOWER, K_UPPER = 0, 1, 2, 3
 MAJOR_K, MAJOR_MN = 0, 1
+KERNEL_AUTO, KERNEL_SINGLE, KERNEL_PAIR = 0, 1, 2
 
 _DT = {torch.bfloat16: _native.AVEY_BF16, torch.float16: _native.AVEY_F16,
        torch.float32: _native.AVEY_F32}
@@ -68,7 +69,7 @@ def supported(a: torch.Tensor, b: torch.Tensor) -> bool:
     return _aligned(a, la[1], a.stride(0)) and _aligned(b, lb[1], b.stride(0))
 
 
-def _params(a, b, c, mode):
+def _params(a, b, c, mode, kernel=KERNEL_AUTO):
     la, lb = _layout_a(a), _layout_b(b)
     p = _native.AveyGemmParams()
     p.struct_size = ctypes.sizeof(_native.AveyGemmParams)
@@ -79,12 +80,15 @@ def _params(a, b, c, mode):
     p.a, p.a_batch_stride, p.a_ld, p.a_major = a.data_ptr(), a.stride(0) if a.shape[0] > 1 else 0, la[1], la[0]
     p.b, p.b_batch_stride, p.b_ld, p.b_major = b.data_ptr(), b.stride(0) if b.shape[0] > 1 else 0, lb[1], lb[0]
     p.c, p.c_batch_stride, p.c_ld = c.data_ptr(), c.stride(0), c.stride(1) if c.shape[1] > 1 else c.shape[2]
+    p.kernel = int(kernel)
     return p
 
 
 def bmm(a: torch.Tensor, b: torch.Tensor, mode: int = DENSE, out: Optional[torch.Tensor] = None,
-        out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """``a @ b`` in fp32 (or ``out_dtype`` = the operand type) on tcgen05.
+        out_dtype: torch.dtype = torch.float32, kernel: int = KERNEL_AUTO) -> torch.Tensor:
+    """``a @ b`` in fp32 (or ``out_dtype`` = the operand type) on tcgen05
+    (``kernel``: single-CTA tiles, CTA pairs, or AUTO = pairs when m > 128
+    and b is K-major).
 
     Raises ``ValueError`` for operands the kernel cannot take (see
     ``supported``); there is no fallback here."""
@@ -93,7 +97,7 @@ def bmm(a: torch.Tensor, b: torch.Tensor, mode: int = DENSE, out: Optional[torch
                          'contiguous dimension each and 16-byte aligned bases and strides')
     if out is None:
         out = torch.empty(a.shape[0], a.shape[1], b.shape[2], dtype=out_dtype, device=a.device)
-    p = _params(a, b, out, mode)
+    p = _params(a, b, out, mode, kernel)
     stream = torch.cuda.current_stream(a.device).cuda_stream
     with torch.cuda.device(a.device):
         _native.gemm(p, stream)

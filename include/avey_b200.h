@@ -345,7 +345,16 @@ typedef struct AveyGemmParams {
   int32_t activation; /* AveyActivation (16-bit output only) */
   int32_t sumsq_col0; /* first column of the row sums of squares */
   float* sumsq;       /* planes of row sums of squares, or NULL */
+  int32_t kernel;     /* AVEY_GEMM_KERNEL_*: AUTO picks PAIR when m > 128 and
+                         B is K-major (measured faster there only) */
 } AveyGemmParams;
+
+/* GEMM kernels: one CTA per 128 x 256 output tile, or a pair of CTAs on
+ * neighbouring SMs per 256 x 256 tile sharing each MMA (tcgen05 cta_group::2),
+ * which halves the B bytes each SM loads per MMA cycle. Same results. */
+#define AVEY_GEMM_KERNEL_AUTO 0
+#define AVEY_GEMM_KERNEL_SINGLE 1
+#define AVEY_GEMM_KERNEL_PAIR 2
 
 AVEY_API int avey_gemm_v1(const AveyGemmParams* params, void* stream);
 

@@ -49,22 +49,41 @@ def check(c, a, b, lower_only=False):
     assert float(err.max()) <= 0.0, float(err.max())
 
 
+KERNELS = [gemm.KERNEL_SINGLE, gemm.KERNEL_PAIR]
+
+
+@pytest.mark.parametrize('kernel', KERNELS)
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize('a_major', ['row', 'col'])
 @pytest.mark.parametrize('b_major', ['row', 'col'])
 @pytest.mark.parametrize('shape', [(3, 200, 296, 72), (2, 512, 768, 512), (1, 128, 256, 64),
-                                   (2, 40, 24, 136)])
-def test_dense_matches_fp64(dtype, a_major, b_major, shape):
+                                   (2, 40, 24, 136), (2, 384, 640, 192)])
+def test_dense_matches_fp64(kernel, dtype, a_major, b_major, shape):
     g = torch.Generator().manual_seed(zlib.crc32(repr((a_major, b_major, shape)).encode()))
     bt, m, n, k = shape
     a = operand((bt, m, k), dtype, a_major, g, 'a')
     b = operand((bt, k, n), dtype, b_major, g, 'b')
     assert gemm.supported(a, b)
     before = _native.launch_count()
-    c = gemm.bmm(a, b)
+    c = gemm.bmm(a, b, kernel=kernel)
     torch.cuda.synchronize()
     assert _native.launch_count() == before + 1
     check(c, a, b)
+
+
+@pytest.mark.parametrize('shape', [(64, 512, 768, 512), (4, 1000, 1536, 768)])
+def test_pair_and_single_kernels_agree(shape):
+    """The CTA-pair kernel (256 x 256 tiles) and the single-CTA kernel give the
+    same products up to fp32 summation order, on backward- and enricher-sized
+    shapes (many tiles per CTA: the accumulator double buffering wraps)."""
+    g = torch.Generator().manual_seed(shape[1])
+    bt, m, n, k = shape
+    a = torch.randn(bt, m, k, generator=g).to(torch.bfloat16).to(DEV)
+    b = torch.randn(bt, n, k, generator=g).to(torch.bfloat16).to(DEV).transpose(1, 2)
+    c1 = gemm.bmm(a, b, kernel=gemm.KERNEL_SINGLE)
+    c2 = gemm.bmm(a, b, kernel=gemm.KERNEL_PAIR)
+    check(c2, a, b)
+    torch.testing.assert_close(c1, c2, rtol=1e-5, atol=1e-4)
 
 
 def test_shared_operand_across_batch():
@@ -75,8 +94,9 @@ def test_shared_operand_across_batch():
     check(gemm.bmm(x, w), x, w)
 
 
+@pytest.mark.parametrize('kernel', KERNELS)
 @pytest.mark.parametrize('ctx,feat', [(512, 768), (384, 256), (200, 136)])
-def test_causal_modes(ctx, feat):
+def test_causal_modes(kernel, ctx, feat):
     """The backward's five products under the causal mask: g / ds0 keep only
     j <= i, num = s z and dzd = s^T dnum skip the zero half of s exactly."""
     g = torch.Generator().manual_seed(ctx)
@@ -86,13 +106,13 @@ def test_causal_modes(ctx, feat):
     s = torch.randn(bt, ctx, ctx, generator=g).to(torch.bfloat16).to(DEV).tril()
     # Garbage in the skipped tiles must stay there: prefill the output with NaN.
     out = torch.full((bt, ctx, ctx), float('nan'), device=DEV)
-    gm = gemm.bmm(z, z.transpose(1, 2), mode=gemm.LOWER_OUT, out=out)
+    gm = gemm.bmm(z, z.transpose(1, 2), mode=gemm.LOWER_OUT, out=out, kernel=kernel)
     check(gm, z, z.transpose(1, 2), lower_only=True)
-    num = gemm.bmm(s, z, mode=gemm.K_LOWER)
-    assert torch.equal(num, gemm.bmm(s, z))
+    num = gemm.bmm(s, z, mode=gemm.K_LOWER, kernel=kernel)
+    assert torch.equal(num, gemm.bmm(s, z, kernel=kernel))
     check(num, s, z)
-    dzd = gemm.bmm(s.transpose(1, 2), dn, mode=gemm.K_UPPER)
-    assert torch.equal(dzd, gemm.bmm(s.transpose(1, 2), dn))
+    dzd = gemm.bmm(s.transpose(1, 2), dn, mode=gemm.K_UPPER, kernel=kernel)
+    assert torch.equal(dzd, gemm.bmm(s.transpose(1, 2), dn, kernel=kernel))
     check(dzd, s.transpose(1, 2), dn)
 
 
@@ -100,9 +120,10 @@ ACTS = {0: lambda x: x, 1: torch.relu, 2: lambda x: torch.relu(x) ** 2, 3: torch
         4: lambda x: torch.nn.functional.gelu(x, approximate='tanh')}
 
 
+@pytest.mark.parametrize('kernel', KERNELS)
 @pytest.mark.parametrize('act', [0, 1, 2, 3, 4])
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
-def test_16bit_epilogue(act, dtype):
+def test_16bit_epilogue(kernel, act, dtype):
     """out = act(x w^T + bias) (.) gate in the operand type, and the row sums of
     squares of the stored outputs of columns >= col0 in 128-column planes."""
     import ctypes
@@ -117,7 +138,7 @@ def test_16bit_epilogue(act, dtype):
     planes = (n - col0 + 127) // 128
     ss = torch.full((planes, bt * m), float('nan'), device=DEV)
     wt = w.t().unsqueeze(0).expand(bt, k, n)
-    p = gemm._params(x, wt, out, gemm.DENSE)
+    p = gemm._params(x, wt, out, gemm.DENSE, kernel)
     p.bias, p.gate = bias.data_ptr(), gate.data_ptr()
     p.gate_batch_stride, p.gate_ld = gate.stride(0), gate.stride(1)
     p.activation, p.sumsq_col0, p.sumsq = act, col0, ss.data_ptr()
