@@ -736,9 +736,11 @@ int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
   g.b_mn = p->b_major == AVEY_MAJOR_MN;
   g.a_batched = p->a_batch_stride != 0 && p->batch > 1;
   g.b_batched = p->b_batch_stride != 0 && p->batch > 1;
-  const int64_t tiles = gemm_tiles_per_batch(g) * p->batch;
+  const int64_t per_batch = gemm_tiles_per_batch(g);
+  const int64_t tiles = per_batch * p->batch;
   if (tiles > (1ll << 30)) return fail(AVEY_ERR_ARGUMENT, "too many output tiles");
   g.total_tiles = static_cast<int>(tiles);
+  g.tiles_per_batch = static_cast<int>(per_batch);
   g.has_bias = p->bias != nullptr;
   g.has_gate = p->gate != nullptr;
   g.bias = p->bias;
@@ -763,9 +765,11 @@ int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
               : encode_map_dims(p->dtype, p->b, p->k, p->n, bb, p->b_ld * 2, p->b_batch_stride * 2, 64,
                                 pair ? 128 : avey::kGmBN, &map_b);
   if (rc != AVEY_OK) return rc;
+  // Output boxes: 32 x 32 16-bit values, or 32 rows x 16 fp32 values (two
+  // per 32-column chunk, double-buffered); both 64-byte rows.
   const int oes = OUT16 ? 2 : 4;
-  rc = encode_map_dims(p->out_dtype, p->c, p->n, p->m, p->batch, p->c_ld * oes, p->c_batch_stride * oes, 32,
-                       32, &map_c);
+  rc = encode_map_dims(p->out_dtype, p->c, p->n, p->m, p->batch, p->c_ld * oes, p->c_batch_stride * oes,
+                       OUT16 ? 32 : 16, 32, &map_c);
   if (rc != AVEY_OK) return rc;
   cudaError_t e = cudaSuccess;
   if (!pair) {

@@ -53,7 +53,7 @@ struct GemmGeom {
   int mode;             // GemmMode
   int a_mn, b_mn;       // operand is MN-major (else K-major)
   int a_batched, b_batched;
-  int total_tiles;
+  int total_tiles, tiles_per_batch;
   int has_bias, has_gate;
   int sumsq_col0;       // 16-bit output: first column of the row sums of squares (multiple of 128)
   const void* bias;     // [n], operand type
@@ -81,23 +81,24 @@ __device__ __forceinline__ int gemm_cols_of(const GemmGeom& g, int mt) {
   return g.mode == kGemmLowerOut ? min(g.n_nt, (mt * g.bm + g.bm - 1) / kGmBN + 1) : g.n_nt;
 }
 
-// Tile t of the launch: row tiles in order (the longest K ranges first under
-// kGemmKLower), then batch entries, then column tiles, so neighbouring CTAs
-// share the A row block.
+// Tile t of the launch: batch entries outermost, so the CTAs working at one
+// time share few operands in L2 (a batch entry's A and B are read from DRAM
+// about once: batch-inner orders measured 1.6x the operand bytes); inside a
+// batch entry, row tiles (the longest K ranges first under kGemmKLower), then
+// column tiles, so neighbouring CTAs share the A row block.
 __device__ __forceinline__ GemmTile gemm_tile(const GemmGeom& g, int t) {
   GemmTile c{0, 0, 0, 0, 0};
-  int rem = t;
+  c.b = t / g.tiles_per_batch;
+  int rem = t - c.b * g.tiles_per_batch;
   for (int o = 0; o < g.n_mt; ++o) {
     const int mt = g.mode == kGemmKLower ? g.n_mt - 1 - o : o;
     const int cnt = gemm_cols_of(g, mt);
-    const int per = cnt * g.batch;
-    if (rem < per) {
+    if (rem < cnt) {
       c.mt = mt;
-      c.b = rem / cnt;
-      c.nt = rem % cnt;
+      c.nt = rem;
       break;
     }
-    rem -= per;
+    rem -= cnt;
   }
   int klo = 0, khi = g.k;
   if (g.mode == kGemmKLower) khi = min(g.k, (c.mt + 1) * g.bm);
@@ -105,14 +106,6 @@ __device__ __forceinline__ GemmTile gemm_tile(const GemmGeom& g, int t) {
   c.k0 = klo / kGmBK;
   c.nk = khi > klo ? (khi - c.k0 * kGmBK + kGmBK - 1) / kGmBK : 0;
   return c;
-}
-
-__device__ __forceinline__ void st_stage_f32(uint32_t stage, int lane, const uint32_t (&o)[32]) {
-  // 32 rows x 128 bytes with the 128-byte swizzle (16-byte chunk q of row r at q ^ (r % 8)).
-#pragma unroll
-  for (int q = 0; q < 8; ++q)
-    st_shared_v4(stage + lane * 128 + ((q ^ (lane & 7)) << 4), o[4 * q], o[4 * q + 1], o[4 * q + 2],
-                 o[4 * q + 3]);
 }
 
 // Drain this warp's 32 rows (first row `row0`) x 128 columns (half `h` of the
@@ -135,37 +128,61 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
   if (OUT16 && g.has_gate && m < g.m)
     grow = static_cast<const T*>(g.gate) + static_cast<int64_t>(c.b) * g.gate_bs +
            static_cast<int64_t>(m) * g.gate_rs;
-#pragma unroll 1
-  for (int ch = 0; ch < 4; ++ch) {
+  const bool bias_vec = (reinterpret_cast<uintptr_t>(g.bias) & 15u) == 0;
+  const int nch = max(0, min(4, (g.n - n_half + 31) / 32));  // chunks of 32 columns in range
+  // The staging tiles alternate chunk by chunk (and half by half for fp32)
+  // within a tile; across tiles the stores of the last tile must have read
+  // them first.
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+  // One 32-column chunk: stores (and sums) from registers `o`.
+  auto emit = [&](int ch, const uint32_t (&o)[32]) {
     const int n0 = n_half + ch * 32;
-    if (n0 >= g.n) break;  // uniform across the warp
-    uint32_t o[32];
-    if (c.nk > 0) {
-      tmem_ld32(tb + ch * 32, o);
-      tmem_wait_ld(o);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 32; ++q) o[q] = 0u;
-    }
     if constexpr (!OUT16) {
-      if (lane == 0) bulk_wait_read_all();  // the previous store has read the tile
-      __syncwarp();
-      st_stage_f32(stage, lane, o);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0 && rows_in) {
-        tma_store_3d(map_c, stage, n0, row0, c.b, stream);
-        bulk_commit_group();
+      // Two 16-column halves through two 2 KB staging tiles (64-byte rows,
+      // 64-byte swizzle): a half waits only for the store two halves back.
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t st_tile = stage + static_cast<uint32_t>(hh * 2048);
+        if (lane == 0) bulk_wait_read_1();
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          st_shared_v4(st_tile + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4), o[16 * hh + 4 * q],
+                       o[16 * hh + 4 * q + 1], o[16 * hh + 4 * q + 2], o[16 * hh + 4 * q + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && rows_in && n0 + 16 * hh < g.n) {
+          tma_store_3d(map_c, st_tile, n0 + 16 * hh, row0, c.b, stream);
+          bulk_commit_group();
+        }
       }
     } else {
-      float bv[32];
+      // The chunk's 32 bias values as packed 16-bit pairs (converted where used).
+      uint32_t bw[16];
       if (g.has_bias) {
         const T* bp = static_cast<const T*>(g.bias) + n0;
+        if (bias_vec && n0 + 32 <= g.n) {
 #pragma unroll
-        for (int q = 0; q < 32; ++q) bv[q] = n0 + q < g.n ? to_f32<T>(bp[q]) : 0.f;
+          for (int q = 0; q < 4; ++q) {
+            const uint4 v = ld_global_nc_v4(bp + 8 * q);
+            bw[4 * q] = v.x;
+            bw[4 * q + 1] = v.y;
+            bw[4 * q + 2] = v.z;
+            bw[4 * q + 3] = v.w;
+          }
+        } else {
+          const uint16_t* bh = reinterpret_cast<const uint16_t*>(bp);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const uint32_t lo = n0 + 2 * q < g.n ? bh[2 * q] : 0u;
+            const uint32_t hi = n0 + 2 * q + 1 < g.n ? bh[2 * q + 1] : 0u;
+            bw[q] = lo | (hi << 16);
+          }
+        }
       } else {
 #pragma unroll
-        for (int q = 0; q < 32; ++q) bv[q] = 0.f;
+        for (int q = 0; q < 16; ++q) bw[q] = 0u;  // +0.0 in both 16-bit formats
       }
       uint32_t gw[16];
       if (grow)
@@ -177,8 +194,8 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
       uint32_t pk[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        float y0 = act_fn<ACT>(__uint_as_float(o[2 * q]) + bv[2 * q]);
-        float y1 = act_fn<ACT>(__uint_as_float(o[2 * q + 1]) + bv[2 * q + 1]);
+        float y0 = act_fn<ACT>(__uint_as_float(o[2 * q]) + raw_at<T>(bw, 2 * q));
+        float y1 = act_fn<ACT>(__uint_as_float(o[2 * q + 1]) + raw_at<T>(bw, 2 * q + 1));
         if (grow) {
           y0 *= raw_at<T>(gw, 2 * q);
           y1 *= raw_at<T>(gw, 2 * q + 1);
@@ -197,6 +214,29 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
       __syncwarp();
       if (rows_in) warp_tile_store(stage + (ch & 1) * 2048, pk, map_c, n0, row0, c.b, stream, lane);
     }
+  };
+  if (c.nk > 0) {
+    // TMEM loads run one chunk ahead of the stores.
+    uint32_t oa[32], ob[32];
+    if (nch > 0) tmem_ld32(tb, oa);
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ch += 2) {
+      tmem_wait_ld(oa);
+      const bool has_b = ch + 1 < nch;
+      if (has_b) tmem_ld32(tb + (ch + 1) * 32, ob);
+      emit(ch, oa);
+      if (has_b) {
+        tmem_wait_ld(ob);
+        if (ch + 2 < nch) tmem_ld32(tb + (ch + 2) * 32, oa);
+        emit(ch + 1, ob);
+      }
+    }
+  } else {
+    uint32_t z[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) z[q] = 0u;
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ++ch) emit(ch, z);
   }
   // The accumulator has been read: the MMA may refill it.
   tc_fence_before();
@@ -373,7 +413,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
 //
 // Barriers: full[s] of rank 0 counts both CTAs' TMA bytes (their loads name
 // it through its shared::cluster address); empty[s] and acc_full[b] of both
-// CTAs are signalled by rank 0's commits (one commit per CTA, no multicast);
+// CTAs are signalled by rank 0's commits (one plain commit per CTA, to a mapa address);
 // acc_empty[b] of rank 0 counts the epilogue warps of both CTAs. Every wait
 // is bounded, and both CTAs always reach the final cluster barrier.
 // ============================================================================

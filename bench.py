@@ -109,11 +109,18 @@ def shard_batch(cfg, world):
 
 
 def make_inputs(cfg, batch, seed, device='cpu'):
-    """Seeded synthetic inputs (fixed draw order: x, W, bias, lengths, boost)."""
+    """Seeded synthetic inputs (fixed draw order: x, W, bias, lengths, boost).
+    Inputs of more than 2^28 elements (config 5's 1024-row batch on one GPU)
+    draw x on the device with a seeded CUDA generator: the same distribution,
+    without minutes of host-side generation."""
     import torch
     g = torch.Generator().manual_seed(seed)
     n, d = cfg['n'], cfg['d']
-    x = torch.randn(batch, n, 2 * d, generator=g)
+    if device != 'cpu' and batch * n * 2 * d > (1 << 28):
+        gd = torch.Generator(device=device).manual_seed(seed)
+        x = torch.randn(batch, n, 2 * d, generator=gd, device=device)
+    else:
+        x = torch.randn(batch, n, 2 * d, generator=g)
     w = torch.randn(n, n, generator=g) * 0.02
     bias = torch.randn(d, generator=g) * 0.01 if cfg['bias'] else None
     if bias is not None and cfg.get('zero_bias'):
@@ -123,7 +130,7 @@ def make_inputs(cfg, batch, seed, device='cpu'):
         lengths = torch.randint(n // 4, n + 1, (batch,), generator=g)
         valid = torch.arange(n)[None, :] < lengths[:, None]
     if cfg['boost']:
-        rows = torch.rand(batch, n, 1, generator=g) < 0.05
+        rows = (torch.rand(batch, n, 1, generator=g) < 0.05).to(x.device)
         x = torch.where(rows, x * 50, x)
     bf = torch.float32 if cfg.get('dtype') == 'f32' else torch.bfloat16
     out = dict(x=x.to(bf), w=w.to(bf) if cfg['op'] == 'avey' else None,
