@@ -255,3 +255,54 @@ def test_mask_as_valid_and_lengths_together_is_rejected():
     p.valid, p.lengths = valid.data_ptr(), lengths.data_ptr()
     with pytest.raises(_native.NativeError, match='not both'):
         _native.plan(p)
+
+
+def _gemm_params(**kw):
+    """A valid AveyGemmParams for [2, 64, 32] x [2, 32, 48] bf16 (host pointers
+    are never dereferenced: validation fails or passes before any launch)."""
+    p = _native.AveyGemmParams()
+    p.struct_size = ctypes.sizeof(_native.AveyGemmParams)
+    p.dtype, p.out_dtype, p.mode = _native.AVEY_BF16, _native.AVEY_F32, 0
+    p.batch, p.m, p.n, p.k = 2, 64, 48, 32
+    p.a, p.a_batch_stride, p.a_ld, p.a_major = 1 << 20, 64 * 32, 32, 0
+    p.b, p.b_batch_stride, p.b_ld, p.b_major = 2 << 20, 48 * 32, 32, 0
+    p.c, p.c_batch_stride, p.c_ld = 3 << 20, 64 * 48, 48
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize('field,value,match', [
+    ('struct_size', 8, 'struct_size'),
+    ('dtype', _native.AVEY_F32, 'bf16 or f16'),
+    ('out_dtype', _native.AVEY_F16, 'out_dtype'),
+    ('mode', 9, 'mode'),
+    ('k', 0, r'\[1, 2\^24\]'),
+    ('a_major', 3, 'a_major'),
+    ('a_ld', 16, 'leading dimensions'),
+    ('b_ld', 36, 'whole 16-byte units'),
+    ('a', (1 << 20) + 8, 'aligned'),
+    ('activation', 2, 'need a 16-bit output'),
+    ('kernel', 5, 'GEMM kernel'),
+])
+def test_gemm_arguments_are_rejected_before_any_launch(field, value, match):
+    p = _gemm_params(**{field: value})
+    before = _native.launch_count()
+    with pytest.raises(_native.NativeError, match=match) as info:
+        _native.gemm(p, 0)
+    assert info.value.status == -1
+    assert _native.launch_count() == before
+
+
+def test_gemm_sums_need_a_128_column_boundary():
+    p = _gemm_params(out_dtype=_native.AVEY_BF16, n=512, c_ld=512, sumsq=4 << 20, sumsq_col0=100)
+    with pytest.raises(_native.NativeError, match='multiple of 128'):
+        _native.gemm(p, 0)
+
+
+def test_presummed_forward_checks_its_planes():
+    p, _keep = _params()
+    with pytest.raises(_native.NativeError, match='planes'):
+        _native.forward_presummed(p, 1 << 20, 0, 0)
+    with pytest.raises(_native.NativeError, match='planes'):
+        _native.forward_presummed(p, 0, 2, 0)
