@@ -713,11 +713,11 @@ int validate_gemm(const AveyGemmParams* p) {
 
 template <typename T, bool OUT16, int ACT>
 int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
-  // AUTO: pairs for K-major B (measured faster: g = zm zm^T 27.8 against
-  // 28.9 us, the enricher shape 81.8 against 85.0 us); with an MN-major B the
-  // pair measured slower (num = s zm 43.6 against 36.9 us), so one CTA per tile.
-  const bool pair = p->kernel == AVEY_GEMM_KERNEL_PAIR ||
-                    (p->kernel == AVEY_GEMM_KERNEL_AUTO && p->m > 128 && p->b_major == AVEY_MAJOR_K);
+  // AUTO: one CTA per tile. With the current epilogue the pair measured slower
+  // on every shape tried (4096^3 bf16: 109.0 against 103.2 us; the enricher
+  // shape 75.2 against 71.6 us; num = s zm 41.4 against 36.8 us), so pairs
+  // run only when asked for.
+  const bool pair = p->kernel == AVEY_GEMM_KERNEL_PAIR;
   constexpr auto K1 = avey::tc_gemm<T, OUT16, ACT>;
   constexpr auto K2 = avey::tc_gemm_pair<T, OUT16, ACT>;
   const cudaError_t attr_err = pair ? smem_opt_in<K2>(avey::kG2Smem) : smem_opt_in<K1>(avey::kGmSmem);

@@ -191,6 +191,7 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
                           (reinterpret_cast<uintptr_t>(g.gate) & 15u) == 0,
                       gw, stream);
       const bool want_ss = g.sumsq && n0 >= g.sumsq_col0;
+      const bool whole = n0 + 32 <= g.n;
       uint32_t pk[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
@@ -206,8 +207,8 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
           const uint16_t lo = static_cast<uint16_t>(pk[q] & 0xFFFFu), hi = static_cast<uint16_t>(pk[q] >> 16);
           const float r0 = to_f32<T>(*reinterpret_cast<const T*>(&lo));
           const float r1 = to_f32<T>(*reinterpret_cast<const T*>(&hi));
-          if (n0 + 2 * q < g.n) ss = fmaf(r0, r0, ss);
-          if (n0 + 2 * q + 1 < g.n) ss = fmaf(r1, r1, ss);
+          if (whole || n0 + 2 * q < g.n) ss = fmaf(r0, r0, ss);
+          if (whole || n0 + 2 * q + 1 < g.n) ss = fmaf(r1, r1, ss);
         }
       }
       if (lane == 0) bulk_wait_read_1();  // two tiles per warp: the store two chunks back is done

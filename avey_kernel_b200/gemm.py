@@ -87,8 +87,7 @@ def _params(a, b, c, mode, kernel=KERNEL_AUTO):
 def bmm(a: torch.Tensor, b: torch.Tensor, mode: int = DENSE, out: Optional[torch.Tensor] = None,
         out_dtype: torch.dtype = torch.float32, kernel: int = KERNEL_AUTO) -> torch.Tensor:
     """``a @ b`` in fp32 (or ``out_dtype`` = the operand type) on tcgen05
-    (``kernel``: single-CTA tiles, CTA pairs, or AUTO = pairs when m > 128
-    and b is K-major).
+    (``kernel``: single-CTA tiles, CTA pairs, or AUTO = single-CTA tiles).
 
     Raises ``ValueError`` for operands the kernel cannot take (see
     ``supported``); there is no fallback here."""

@@ -345,8 +345,8 @@ typedef struct AveyGemmParams {
   int32_t activation; /* AveyActivation (16-bit output only) */
   int32_t sumsq_col0; /* first column of the row sums of squares */
   float* sumsq;       /* planes of row sums of squares, or NULL */
-  int32_t kernel;     /* AVEY_GEMM_KERNEL_*: AUTO picks PAIR when m > 128 and
-                         B is K-major (measured faster there only) */
+  int32_t kernel;     /* AVEY_GEMM_KERNEL_*: AUTO runs SINGLE (measured the
+                         faster of the two on every shape tried) */
 } AveyGemmParams;
 
 /* GEMM kernels: one CTA per 128 x 256 output tile, or a pair of CTAs on
