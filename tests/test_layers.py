@@ -182,3 +182,58 @@ def test_enriched_pipeline_with_autograd():
     assert norm_rel_err(to_numpy(out), to_numpy(ref)) <= TOL['bfloat16']
     assert norm_rel_err(to_numpy(x.grad), to_numpy(xe.grad)) <= 5e-2
     assert norm_rel_err(to_numpy(w.grad), to_numpy(we.grad)) <= 5e-2
+
+
+@pytest.mark.gpu
+def test_enriched_pipeline_long_context_and_fallbacks(clean_status):
+    """The pre-summed contextualizer on the long-context path (640 tokens: the
+    plane sums feed the G/P and P.Z kernels), and a width whose tail is not a
+    whole number of 128-column planes (no sums: the contextualizer runs its own
+    pre-pass)."""
+    g = torch.Generator().manual_seed(11)
+    for c, d, sums_expected in ((640, 256, True), (256, 200, False)):
+        x = torch.randn(2, c, 128, generator=g).to(torch.bfloat16).to(DEV)
+        w = (torch.randn(2 * d, 128, generator=g) * 128 ** -0.5).to(torch.bfloat16).to(DEV)
+        v = (torch.randn(c, c, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+        e, sums = layers.enrich(x, w, activation='silu', tail_sums=True)
+        assert (sums is not None) == sums_expected
+        got = layers.avey_enriched(x, w, v, enrich_activation='silu', activation='relu')
+        head, tail = e[..., :d], e[..., d:]
+        ref = oracle.avey(to_numpy(tail), to_numpy(v), z_tl=to_numpy(head), activation='relu')
+        plain = ops.avey(tail, v, z_tl=head, activation='relu')
+        torch.cuda.synchronize()
+        assert norm_rel_err(to_numpy(got), ref) <= TOL['bfloat16']
+        assert norm_rel_err(to_numpy(got), to_numpy(plain)) <= 2e-3
+
+
+@pytest.mark.gpu
+def test_presummed_entry_point_matches_the_plain_one(clean_status):
+    """avey_fwd_presummed_v1 through the C ABI with sums computed here in two
+    planes, against avey_fwd_v1 (its own pre-pass) on the same tensors: the
+    same kernels up to the summation order of the row norms."""
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(3, 512, 2 * 256, generator=g).to(torch.bfloat16).to(DEV)
+    head, tail = x[..., :256], x[..., 256:]
+    tf = tail.float()
+    planes = torch.stack([(tf[..., :128] ** 2).sum(-1).reshape(-1),
+                          (tf[..., 128:] ** 2).sum(-1).reshape(-1)]).contiguous()
+    outs = []
+    for presummed in (False, True):
+        out = torch.empty(tail.shape, dtype=tail.dtype, device=DEV)
+        p = ops.build_params(tail, None, head, None, None, out, eps=0.5, norm_eps=1e-12,
+                             causal=False, normalize=True, activation_id=4)
+        n = _native.workspace_size(p)
+        ws = torch.empty(n, dtype=torch.uint8, device=DEV)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), n
+        stream = torch.cuda.current_stream().cuda_stream
+        if presummed:
+            _native.forward_presummed(p, planes.data_ptr(), 2, stream)
+        else:
+            _native.forward(p, stream)
+        torch.cuda.synchronize()
+        outs.append(out)
+    # The two differ only in the summation order of the row norms (last bits of
+    # rinv), which can move a bf16 rounding of P by one unit (2^-9 relative).
+    assert norm_rel_err(to_numpy(outs[1]), to_numpy(outs[0])) <= 5e-3
+    ref = oracle.avey_b(to_numpy(tail), z_tl=to_numpy(head), eps=0.5, activation='gelu')
+    assert norm_rel_err(to_numpy(outs[1]), ref) <= TOL['bfloat16']
