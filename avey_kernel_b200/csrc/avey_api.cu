@@ -406,6 +406,18 @@ int launch_row_sums(const AveyFwdParams* p, const avey::FwdArgs& args, const Pre
   return AVEY_OK;
 }
 
+// The contextualizer's per-row scale for the GEMM epilogue (O = P Z of the
+// long-context path; see GemmGeom::ctx_*).
+struct CtxMix {
+  const float* sumsq;
+  const float* den;
+  int groups, causal, normalize, rq_in_p;
+  float eps, norm_eps;
+};
+int validate_gemm(const AveyGemmParams* p);
+template <typename T, bool OUT16, int ACT>
+int launch_gemm(const AveyGemmParams* p, cudaStream_t stream, const CtxMix* ctx);
+
 template <typename T, int ACT>
 int launch_long(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps) {
   cudaError_t attr_err = smem_opt_in<avey::tc_gram_p<T>>(kMaxDynSmem);
@@ -469,13 +481,54 @@ int launch_long(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps) {
     e = cudaLaunchKernelEx(&cfg, avey::tc_gram_p<T>, args, map_k, map_pst, geom);
     if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_gram_p launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    avey::tc_pv<T, ACT><<<dim3(static_cast<unsigned>(geom.n_qtiles * geom.n_fgroups),
-                               static_cast<unsigned>(q.batch)),
-                          avey::kPvThreads, static_cast<size_t>(l.smem_pv), stream>>>(
-        args, map_p, map_z, map_o, geom);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_pv launch: %s", cudaGetErrorString(e));
-    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (!p->valid && !p->lengths) {
+      // No padding mask: O = P Z runs on the persistent tcgen05 GEMM (the K
+      // loop of each 128-row tile stops at its diagonal under the causal
+      // mask, where P is zero beyond it), its epilogue scaling each row as
+      // tc_pv does, then bias, activation and gate.
+      AveyGemmParams gp;
+      std::memset(&gp, 0, sizeof(gp));
+      gp.struct_size = sizeof(gp);
+      gp.dtype = q.dtype;
+      gp.out_dtype = q.dtype;
+      gp.mode = q.causal ? AVEY_GEMM_K_LOWER : AVEY_GEMM_DENSE;
+      gp.batch = q.batch;
+      gp.m = q.context;
+      gp.n = q.features;
+      gp.k = q.context;
+      const bool many = q.batch > 1;
+      gp.a = pbuf;
+      gp.a_batch_stride = many ? geom.p_bs : 0;
+      gp.a_ld = geom.p_rs;
+      gp.a_major = AVEY_MAJOR_K;
+      gp.b = q.z_tr;
+      gp.b_batch_stride = many ? q.z_tr_batch_stride : 0;
+      gp.b_ld = q.z_tr_row_stride;
+      gp.b_major = AVEY_MAJOR_MN;
+      gp.c = q.out;
+      gp.c_batch_stride = many ? q.out_batch_stride : 0;
+      gp.c_ld = q.out_row_stride;
+      gp.bias = q.bias;
+      gp.gate = q.z_tl;
+      gp.gate_batch_stride = q.z_tl ? (many ? q.z_tl_batch_stride : 0) : 0;
+      gp.gate_ld = q.z_tl ? q.z_tl_row_stride : 0;
+      gp.activation = ACT;
+      gp.kernel = AVEY_GEMM_KERNEL_SINGLE;
+      rc = validate_gemm(&gp);
+      if (rc != AVEY_OK) return rc;
+      const CtxMix cm{args.sumsq, geom.den_part, geom.n_groups, q.causal != 0, q.normalize != 0,
+                      avey::kRowScaleInP<T> ? 1 : 0, args.eps_f, args.norm_eps_f};
+      rc = launch_gemm<T, true, ACT>(&gp, stream, &cm);
+      if (rc != AVEY_OK) return rc;
+    } else {
+      avey::tc_pv<T, ACT><<<dim3(static_cast<unsigned>(geom.n_qtiles * geom.n_fgroups),
+                                 static_cast<unsigned>(q.batch)),
+                            avey::kPvThreads, static_cast<size_t>(l.smem_pv), stream>>>(
+          args, map_p, map_z, map_o, geom);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "tc_pv launch: %s", cudaGetErrorString(e));
+      g_launches.fetch_add(1, std::memory_order_relaxed);
+    }
   }
   return ok();
 }
@@ -712,7 +765,7 @@ int validate_gemm(const AveyGemmParams* p) {
 }
 
 template <typename T, bool OUT16, int ACT>
-int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
+int launch_gemm(const AveyGemmParams* p, cudaStream_t stream, const CtxMix* ctx) {
   // AUTO: one CTA per tile. With the current epilogue the pair measured slower
   // on every shape tried (4096^3 bf16: 109.0 against 103.2 us; the enricher
   // shape 75.2 against 71.6 us; num = s zm 41.4 against 36.8 us), so pairs
@@ -749,6 +802,16 @@ int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
   g.gate_rs = p->gate_ld;
   g.sumsq = p->sumsq;
   g.sumsq_col0 = p->sumsq_col0;
+  if (ctx) {
+    g.ctx_sumsq = ctx->sumsq;
+    g.ctx_den = ctx->den;
+    g.ctx_groups = ctx->groups;
+    g.ctx_causal = ctx->causal;
+    g.ctx_normalize = ctx->normalize;
+    g.ctx_rq_in_p = ctx->rq_in_p;
+    g.ctx_eps = ctx->eps;
+    g.ctx_norm_eps = ctx->norm_eps;
+  }
   // Operand maps: {contiguous extent, other extent, batch}; boxes of 64
   // contiguous elements (128 bytes, 128-byte swizzle) by 128 rows (A, K-major),
   // 256 rows (B, K-major) or 64 k rows (MN-major operands).
@@ -800,13 +863,13 @@ int launch_gemm(const AveyGemmParams* p, cudaStream_t stream) {
 
 template <typename T>
 int launch_gemm_out(const AveyGemmParams* p, cudaStream_t stream) {
-  if (p->out_dtype == AVEY_F32) return launch_gemm<T, false, AVEY_ACT_IDENTITY>(p, stream);
+  if (p->out_dtype == AVEY_F32) return launch_gemm<T, false, AVEY_ACT_IDENTITY>(p, stream, nullptr);
   switch (p->activation) {
-    case AVEY_ACT_RELU: return launch_gemm<T, true, AVEY_ACT_RELU>(p, stream);
-    case AVEY_ACT_RELU2: return launch_gemm<T, true, AVEY_ACT_RELU2>(p, stream);
-    case AVEY_ACT_SILU: return launch_gemm<T, true, AVEY_ACT_SILU>(p, stream);
-    case AVEY_ACT_GELU: return launch_gemm<T, true, AVEY_ACT_GELU>(p, stream);
-    default: return launch_gemm<T, true, AVEY_ACT_IDENTITY>(p, stream);
+    case AVEY_ACT_RELU: return launch_gemm<T, true, AVEY_ACT_RELU>(p, stream, nullptr);
+    case AVEY_ACT_RELU2: return launch_gemm<T, true, AVEY_ACT_RELU2>(p, stream, nullptr);
+    case AVEY_ACT_SILU: return launch_gemm<T, true, AVEY_ACT_SILU>(p, stream, nullptr);
+    case AVEY_ACT_GELU: return launch_gemm<T, true, AVEY_ACT_GELU>(p, stream, nullptr);
+    default: return launch_gemm<T, true, AVEY_ACT_IDENTITY>(p, stream, nullptr);
   }
 }
 

@@ -60,6 +60,14 @@ struct GemmGeom {
   const void* gate;     // [batch][m][n], operand type
   int64_t gate_bs, gate_rs;
   float* sumsq;         // planes [(n - col0) / 128][batch * m], or null
+  // Contextualizer mix epilogue (O = P Z of the long-context path, 16-bit
+  // output): each row scaled before the bias as tc_pv scales it, from the
+  // rows' sums of squares (ctx_sumsq [batch * m]) and, for Avey-B, the partial
+  // row sums of P (ctx_den [batch][ctx_groups][m]); null when unused.
+  const float* ctx_sumsq;
+  const float* ctx_den;
+  int ctx_groups, ctx_causal, ctx_normalize, ctx_rq_in_p;
+  float ctx_eps, ctx_norm_eps;
 };
 
 struct GemmCtrl {
@@ -129,6 +137,26 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
     grow = static_cast<const T*>(g.gate) + static_cast<int64_t>(c.b) * g.gate_bs +
            static_cast<int64_t>(m) * g.gate_rs;
   const bool bias_vec = (reinterpret_cast<uintptr_t>(g.bias) & 15u) == 0;
+  // Row scale of the contextualizer mix (1 otherwise): 1 / max(||z_i||,
+  // norm_eps) (unless it is already in P), divided by (row sum of P + eps) for
+  // Avey-B, with the partial sums added in group order (as tc_pv does).
+  float rs = 1.f;
+  if (OUT16 && g.ctx_sumsq && m < g.m) {
+    const int64_t r = static_cast<int64_t>(c.b) * g.m + m;
+    const float rq = 1.f / fmaxf(sqrtf(g.ctx_sumsq[r]), g.ctx_norm_eps);
+    const float os = g.ctx_rq_in_p ? 1.f : rq;
+    if (g.ctx_normalize) {
+      const int q_lo = (m / 128) * 128;
+      const int nkeys = g.ctx_causal ? min(g.m, q_lo + 128) : g.m;
+      const int ng = (nkeys + kLgGroupKeys - 1) / kLgGroupKeys;
+      float den = 0.f;
+      for (int gg = 0; gg < ng; ++gg)
+        den += g.ctx_den[(static_cast<int64_t>(c.b) * g.ctx_groups + gg) * g.m + m];
+      rs = os / (os * den + g.ctx_eps);
+    } else {
+      rs = os;
+    }
+  }
   const int nch = max(0, min(4, (g.n - n_half + 31) / 32));  // chunks of 32 columns in range
   // The staging tiles alternate chunk by chunk (and half by half for fp32)
   // within a tile; across tiles the stores of the last tile must have read
@@ -195,8 +223,8 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
       uint32_t pk[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        float y0 = act_fn<ACT>(__uint_as_float(o[2 * q]) + raw_at<T>(bw, 2 * q));
-        float y1 = act_fn<ACT>(__uint_as_float(o[2 * q + 1]) + raw_at<T>(bw, 2 * q + 1));
+        float y0 = act_fn<ACT>(fmaf(__uint_as_float(o[2 * q]), rs, raw_at<T>(bw, 2 * q)));
+        float y1 = act_fn<ACT>(fmaf(__uint_as_float(o[2 * q + 1]), rs, raw_at<T>(bw, 2 * q + 1)));
         if (grow) {
           y0 *= raw_at<T>(gw, 2 * q);
           y1 *= raw_at<T>(gw, 2 * q + 1);
