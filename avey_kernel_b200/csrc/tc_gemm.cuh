@@ -18,15 +18,19 @@
 //    feeds the contextualizer, with partial row sums of squares of its tail
 //    columns written from the epilogue (the contextualizer then needs no
 //    pre-pass over z_tr);
-//  * the static (position-wise or token-mixing) layers, with the gate.
+//  * the static (position-wise or token-mixing) layers, with the gate;
+//  * O = P Z of the long-context contextualizer (tc_long.cuh's P workspace
+//    times z_tr), with the contextualizer's row scale in the epilogue.
 //
 // Structure: persistent CTAs (one per SM, tiles of 128 x 256 taken round
-// robin), warp 0 issues TMA (4 stages of a 128 x 64 A tile and a 64 x 256 B
-// tile, 128-byte swizzle), warp 1 issues tcgen05.mma (M = 128, N = 256, K = 16)
-// into one of two 256-column TMEM accumulators, and warps 4-11 drain the other
-// accumulator (thread = output row, 32 columns per tcgen05.ld) through
+// robin, batch entry by batch entry), warp 0 issues TMA (4 stages of a
+// 128 x 64 A tile and a 64 x 256 B tile, 128-byte swizzle), warp 1 issues
+// tcgen05.mma (M = 128, N = 256, K = 16) into one of two 256-column TMEM
+// accumulators, and warps 4-11 drain the other accumulator (thread = output
+// row, 32 columns per tcgen05.ld, the next chunk's load in flight) through
 // per-warp staging tiles and TMA tensor stores, so a tile's epilogue overlaps
-// the next tile's main loop. Every wait is bounded (ptx.cuh).
+// the next tile's main loop. A variant runs on CTA pairs (tc_gemm_pair, below).
+// Every wait is bounded (ptx.cuh).
 #pragma once
 
 #include "tc_long.cuh"
@@ -40,7 +44,7 @@ constexpr int kGmABytes = kGmBM * kGmBK * 2;         // 16 KB
 constexpr int kGmBBytes = kGmBN * kGmBK * 2;         // 32 KB
 constexpr int kGmStageBytes = kGmABytes + kGmBBytes;  // 48 KB
 constexpr int kGmMnBox = 64 * kGmBK * 2;              // one {64 (m or n), 64 (k)} box: 8 KB
-constexpr int kGmStageTile = 4096;  // a warp's staging tile: 32 x 32 fp32 (or two 32 x 32 16-bit)
+constexpr int kGmStageTile = 4096;  // a warp's two 2 KB staging tiles (32 x 16 fp32 or 32 x 32 16-bit each)
 constexpr int kGmCtrlBytes = 1024;
 constexpr int kGmSmem = 1024 + kGmStages * kGmStageBytes + 8 * kGmStageTile + kGmCtrlBytes;
 
@@ -117,11 +121,12 @@ __device__ __forceinline__ GemmTile gemm_tile(const GemmGeom& g, int t) {
 }
 
 // Drain this warp's 32 rows (first row `row0`) x 128 columns (half `h` of the
-// 256-column tile) of one accumulator (`tb`: TMEM address of column 0 of the
+// 256-column tile) of one accumulator (`tb0`: TMEM address of column 0 of the
 // buffer in this warp's lane quarter) into C, then release the accumulator by
-// one arrival on `acc_empty` (a shared::cluster address: this CTA's barrier or
-// the pair leader's). fp32 output: 32 x 32 tiles through the staging tile and
-// TMA stores; 16-bit output: bias, activation, gate, row sums of squares.
+// one arrival on `acc_empty` (this CTA's barrier, or with PAIR the pair
+// leader's, as a shared::cluster address). fp32 output: 32 x 16 halves
+// through two staging tiles and TMA stores; 16-bit output: row scale, bias,
+// activation, gate, row sums of squares, 32 x 32 tiles.
 template <typename T, bool OUT16, int ACT, bool PAIR>
 __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTile& c, int row0,
                                                 uint32_t tb0, int h, int lane, uint32_t stage,
@@ -164,6 +169,13 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
   if (lane == 0) bulk_wait_read_all();
   __syncwarp();
   // One 32-column chunk: stores (and sums) from registers `o`.
+  // Gate words of the next chunk to emit (16-bit output with a gate).
+  const bool gate_vec = (g.gate_rs & 7) == 0 && (g.gate_bs & 7) == 0 &&
+                        (reinterpret_cast<uintptr_t>(g.gate) & 15u) == 0;
+  uint32_t gn[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) gn[q] = 0u;
+  if (OUT16 && grow && nch > 0) load_raw32<T>(grow + n_half, g.n - n_half, gate_vec, gn, stream);
   auto emit = [&](int ch, const uint32_t (&o)[32]) {
     const int n0 = n_half + ch * 32;
     if constexpr (!OUT16) {
@@ -212,12 +224,11 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmGeom& g, const GemmTil
 #pragma unroll
         for (int q = 0; q < 16; ++q) bw[q] = 0u;  // +0.0 in both 16-bit formats
       }
+      // This chunk's gate words (loaded one chunk ahead), then the next chunk's.
       uint32_t gw[16];
-      if (grow)
-        load_raw32<T>(grow + n0, g.n - n0,
-                      (g.gate_rs & 7) == 0 && (g.gate_bs & 7) == 0 &&
-                          (reinterpret_cast<uintptr_t>(g.gate) & 15u) == 0,
-                      gw, stream);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) gw[q] = gn[q];
+      if (grow && ch + 1 < nch) load_raw32<T>(grow + n0 + 32, g.n - n0 - 32, gate_vec, gn, stream);
       const bool want_ss = g.sumsq && n0 >= g.sumsq_col0;
       const bool whole = n0 + 32 <= g.n;
       uint32_t pk[16];
