@@ -14,6 +14,8 @@ LIB_PATH = Path(__file__).resolve().parent / 'lib' / 'libavey_b200.so'
 
 AVEY_F32, AVEY_F16, AVEY_BF16, AVEY_F64 = 0, 1, 2, 3
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
+# AveyPlan.reason: why the tcgen05 kernels were not chosen (0: they were).
+REASON_DTYPE, REASON_CONTEXT, REASON_ALIGNMENT, REASON_FORCED, REASON_FEATURES, REASON_SMALL = range(1, 7)
 ACTIVATION_IDS = {'identity': 0, 'relu': 1, 'relu2': 2, 'silu': 3, 'gelu': 4}
 
 STATUS_NAMES = {

@@ -19,6 +19,7 @@
 #include "norm_prepass.cuh"
 #include "simt_kernel.cuh"
 #include "simt2_kernel.cuh"
+#include "small_kernel.cuh"
 #include "tc_kernel.cuh"
 #include "tc_long.cuh"
 #include "tc_tf32.cuh"
@@ -53,6 +54,7 @@ enum Reason {
   kReasonAlignment = 3,  // base / strides not 16-byte aligned (TMA, vector I/O)
   kReasonForced = 4,     // caller asked for the CUDA-core kernel
   kReasonFeatures = 5,   // more than 2048 features (bias is staged in shared memory)
+  kReasonSmall = 6,      // small fp32 problem: the 8-row CUDA-core kernel finishes first
 };
 
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
@@ -137,8 +139,11 @@ cudaError_t smem_opt_in(int bytes) {
 // Contexts up to 512 run the fused kernel; longer ones (up to 8192) the
 // two-kernel path of tc_long.cuh, whose P round trip needs a large workspace;
 // `allow_long` is false for the no-allocation entry point.
+bool small_pick(const AveyFwdParams* p);
+
 int tc_reason(const AveyFwdParams* p, bool allow_long = true) {
   if (p->kernel == AVEY_KERNEL_SIMT) return kReasonForced;
+  if (p->kernel == AVEY_KERNEL_AUTO && small_pick(p)) return kReasonSmall;
   if (p->dtype != AVEY_BF16 && p->dtype != AVEY_F16 && p->dtype != AVEY_F32) return kReasonDtype;
   if (p->context > (allow_long ? avey::kLongMaxContext : avey::kTcMaxKeys)) return kReasonContext;
   if (p->features > avey::kTcMaxFeatures) return kReasonFeatures;
@@ -666,6 +671,61 @@ int launch_tc_act(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps 
 // tensor-core kernels do not; fp64 keeps simt_contextualize.
 bool use_simt2(const AveyFwdParams* p) { return p->dtype != AVEY_F64; }
 
+// fp32 inputs the 8-row kernel (small_kernel.cuh) takes: contexts up to 512,
+// feature counts that are multiples of 32 with rows of at most 1 KB, and z_tr
+// rows it can copy in 16-byte pieces.
+bool small_ok(const AveyFwdParams* p) {
+  if (p->dtype != AVEY_F32) return false;
+  if (p->context > avey::kSmMaxCtx || p->features % 32 != 0 ||
+      p->features * 4 > avey::kSmMaxRowBytes)
+    return false;
+  return aligned16(p->z_tr) && p->z_tr_row_stride % 4 == 0 &&
+         (p->z_tr_batch_stride % 4 == 0 || p->batch == 1);
+}
+
+// Query tiles (batch x ceil(context / 8)) up to which the 8-row kernel, one
+// CTA pair per tile and one CTA per SM, finishes before the 3xTF32 kernel
+// pair. Measured on a B200 (fp32, Avey causal): at 64 tiles 10.8 against
+// 37.4 us (config 1), at 128 tiles 20.7 / 36.4 against 37.4 / 68.3 us, at 256
+// tiles 39.7 / 49.5 against 37.4 / 51.6 us. AUTO picks it up to here (reason
+// kReasonSmall); a forced AVEY_KERNEL_SIMT keeps the two-phase kernel.
+constexpr int64_t kSmallTiles = 192;
+
+bool small_pick(const AveyFwdParams* p) {
+  return small_ok(p) &&
+         p->batch * ((p->context + avey::kSmRows - 1) / avey::kSmRows) <= kSmallTiles;
+}
+
+int launch_small(const AveyFwdParams* p, cudaStream_t stream) {
+  const avey::SmallGeom g = avey::small_geom(static_cast<int>(p->features));
+  // The opt-in is made once per device, so it names the largest layout (the
+  // 128-key blocks of 512-byte rows and the 64-key blocks of 1 KB rows; the
+  // kernel's static shared memory comes on top).
+  const int smem_max = std::max(avey::small_geom(128).smem, avey::small_geom(256).smem);
+  const cudaError_t attr_err = smem_opt_in<avey::small_contextualize>(smem_max);
+  if (attr_err != cudaSuccess)
+    return fail(AVEY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  const avey::FwdArgs args = make_args(p);
+  // A (2, 1, 1) cluster per query tile: the two CTAs split the tile's keys.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * ((p->context + avey::kSmRows - 1) / avey::kSmRows)),
+                     static_cast<unsigned>(p->batch));
+  cfg.blockDim = dim3(avey::kSmThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(g.smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, avey::small_contextualize, args, g);
+  if (e != cudaSuccess) return fail(AVEY_ERR_LAUNCH, "CUDA-core kernel launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ok();
+}
+
 template <typename T, bool LONG>
 int launch_simt2(const AveyFwdParams* p, cudaStream_t stream) {
   const cudaError_t attr_err = smem_opt_in<avey::simt2_contextualize<T, LONG>>(avey::kS2SmemBytes);
@@ -911,6 +971,11 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
     plan->grid = static_cast<int32_t>(p->batch * l.geom.n_qtiles);
     plan->block = avey::kTcThreads;
     plan->smem_bytes = l.smem;
+  } else if (reason == kReasonSmall) {
+    plan->kernel = AVEY_KERNEL_SIMT;
+    plan->grid = static_cast<int32_t>(2 * ((p->context + avey::kSmRows - 1) / avey::kSmRows) * p->batch);
+    plan->block = avey::kSmThreads;
+    plan->smem_bytes = avey::small_geom(static_cast<int>(p->features)).smem;
   } else if (use_simt2(p)) {
     plan->kernel = AVEY_KERNEL_SIMT;
     plan->grid = static_cast<int32_t>(((p->context + avey::kS2Rows - 1) / avey::kS2Rows) * p->batch);
@@ -952,6 +1017,7 @@ int avey_fwd_v1(const AveyFwdParams* p, void* stream_ptr) {
     return p->dtype == AVEY_BF16 ? launch_tc_act<__nv_bfloat16>(p, stream)
                                  : launch_tc_act<__half>(p, stream);
   }
+  if (plan.reason == kReasonSmall) return launch_small(p, stream);
   if (use_simt2(p)) {
     const bool lng = p->context > avey::kS2MaxCtx;
     switch (p->dtype) {
@@ -995,9 +1061,9 @@ int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
   if (rc != AVEY_OK) return rc;
   AveyFwdParams q = *p;
   // Contexts above 512 and fp32 inputs would take a tensor-core kernel pair
-  // whose P workspace this entry point does not have: they run the CUDA-core
-  // kernel.
-  if (is_pair(p)) {
+  // whose P workspace this entry point does not have: they run a CUDA-core
+  // kernel (small fp32 problems the 8-row kernel, as avey_fwd_v1 does).
+  if (is_pair(p) && plan.reason != kReasonSmall) {
     if (p->kernel == AVEY_KERNEL_TCGEN05)
       return fail(AVEY_ERR_UNSUPPORTED,
                   "the no-allocation entry point runs contexts above 512 and fp32 inputs on CUDA "

@@ -20,7 +20,7 @@ LIB_DIR = PKG / 'lib'
 LIB = LIB_DIR / 'libavey_b200.so'
 SOURCES = ['avey_api.cu', 'avey_bwd.cu']
 HEADERS = ['ptx.cuh', 'common.cuh', 'norm_prepass.cuh', 'simt_kernel.cuh', 'simt2_kernel.cuh',
-           'tc_kernel.cuh', 'tc_long.cuh', 'tc_tf32.cuh', 'tc_gemm.cuh', 'bwd_kernels.cuh']
+           'small_kernel.cuh', 'tc_kernel.cuh', 'tc_long.cuh', 'tc_tf32.cuh', 'tc_gemm.cuh', 'bwd_kernels.cuh']
 
 NVCC_FLAGS = [
     '-gencode', 'arch=compute_100a,code=sm_100a',

@@ -123,7 +123,10 @@ typedef struct AveyPlan {
   int32_t grid;          /* CTAs of the main launch */
   int32_t block;         /* threads per CTA of the main launch */
   int32_t smem_bytes;    /* dynamic shared memory per CTA */
-  int32_t reason;        /* 0, or why the tcgen05 kernel was not chosen */
+  int32_t reason;        /* 0, or why the tcgen05 kernel was not chosen: 1 dtype,
+                            2 context, 3 alignment, 4 AVEY_KERNEL_SIMT asked for,
+                            5 features, 6 small fp32 problem (AUTO runs the 8-row
+                            CUDA-core kernel, which finishes first there) */
 } AveyPlan;
 
 /*

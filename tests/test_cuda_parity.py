@@ -51,7 +51,9 @@ def oracle_out(case):
 def kernels_for(case, t):
     plan = ops.plan(t['z_tr'], t['v'], t['z_tl'], t['bias'], t['valid'])
     ks = [_native.KERNEL_AUTO, _native.KERNEL_SIMT]
-    if plan.kernel == _native.KERNEL_TCGEN05:
+    # Small fp32 inputs run the 8-row CUDA-core kernel under AUTO; the 3xTF32
+    # pair still takes them when asked for.
+    if plan.kernel == _native.KERNEL_TCGEN05 or plan.reason == _native.REASON_SMALL:
         ks.append(_native.KERNEL_TCGEN05)
     return ks
 
@@ -492,27 +494,35 @@ def test_prefix_lengths_match_the_byte_mask(dtype, n, op):
 @pytest.mark.parametrize('shape,op', [((2, 256, 128), 'avey'), ((64, 512, 768), 'avey'),
                                       ((8, 512, 384), 'avey_b')], ids=['c1', 'c2-shape', 'c3-shape'])
 def test_fp32_runs_on_tensor_cores_at_the_fp32_bound(shape, op):
-    # fp32 takes the 3xTF32 tcgen05 pair (BASELINE config 1 and the config-2
-    # and config-3 shapes in fp32): norm-wise 1e-4 against the fp64 oracle on
+    # fp32 on the 3xTF32 tcgen05 pair (BASELINE config 1 and the config-2 and
+    # config-3 shapes in fp32): norm-wise 1e-4 against the fp64 oracle on
     # every row checked, and the elementwise bound of the reference's own fp32
-    # kernel tests (atol = rtol = 1e-5) on config 1.
+    # kernel tests (atol = rtol = 1e-5) on config 1. The public API takes the
+    # pair for the larger shapes; config 1 it runs on the 8-row CUDA-core
+    # kernel (tests/test_small_kernel.py), so the pair is asked for here.
     g = torch.Generator(device='cpu').manual_seed(7)
     b, n, d = shape
     x = torch.randn(b, n, 2 * d, generator=g)
     head, tail = x[..., :d].to(DEV), x[..., d:].to(DEV)
     valid = None
+    small = shape == (2, 256, 128)
+    tc = _native.KERNEL_TCGEN05
     if op == 'avey':
         w = (torch.randn(n, n, generator=g) * 0.02).to(DEV)
         bias = (torch.randn(d, generator=g) * 0.01).to(DEV) if b > 2 else None
-        plan = ops.plan(tail, w, head, bias)
-        out = avey(tail, w, z_tl=head, bias=bias)
+        plan = ops.plan(tail, w, head, bias, kernel=tc)
+        auto = ops.plan(tail, w, head, bias)
+        out = (ops.contextualize(tail, w, head, bias, None, 1e-6, 1e-12, True, False, 0, tc)
+               if small else avey(tail, w, z_tl=head, bias=bias))
     else:
         lengths = torch.randint(n // 4, n + 1, (b,), generator=g)
         valid = (torch.arange(n)[None, :] < lengths[:, None]).to(DEV)
-        plan = ops.plan(tail, None, head, None, valid, causal=False, normalize=True)
+        plan = ops.plan(tail, None, head, None, valid, causal=False, normalize=True, kernel=tc)
+        auto = ops.plan(tail, None, head, None, valid, causal=False, normalize=True)
         tail = tail.abs()  # keep the signed row sums away from -eps
         out = avey_b(tail, z_tl=head, valid=valid, eps=1e-6)
     assert plan.kernel == _native.KERNEL_TCGEN05 and plan.launches == 2
+    assert auto.reason == (_native.REASON_SMALL if small else 0)
     torch.cuda.synchronize()
     y = to_numpy(out)
     assert np.isfinite(y).all()
@@ -553,10 +563,18 @@ def test_non_finite_padding_never_reaches_the_output(dtype, n, mask, fill):
     valid = valid.to(DEV)
     head, tail = x[..., :d], x[..., d:]
     w = (torch.randn(n, n, generator=g) * 0.05).to(dtype).to(DEV)
-    assert ops.plan(tail, w, head, None, valid).kernel == _native.KERNEL_TCGEN05
+    plan = ops.plan(tail, w, head, None, valid)
+    assert plan.kernel == _native.KERNEL_TCGEN05 or plan.reason == _native.REASON_SMALL
     # Avey-B on non-negative tails keeps the signed row sums away from -eps.
     outs = {'avey': avey(tail, w, z_tl=head, valid=valid),
             'avey_b': avey_b(tail.abs(), z_tl=head, valid=valid, eps=0.5)}
+    if plan.reason == _native.REASON_SMALL:
+        # fp32 at 300 tokens runs the 8-row CUDA-core kernel; the 3xTF32 pair too.
+        tc = _native.KERNEL_TCGEN05
+        outs['avey-tc'] = ops.contextualize(tail, w, head, None, valid, 1e-6, 1e-12, True, False,
+                                            0, tc)
+        outs['avey_b-tc'] = ops.contextualize(tail.abs(), None, head, None, valid, 0.5, 1e-12,
+                                              False, True, 0, tc)
     torch.cuda.synchronize()
     ok = to_numpy(valid.float()) > 0
     tol = TOL['float32'] if dtype == torch.float32 else TOL['bfloat16']
@@ -566,7 +584,7 @@ def test_non_finite_padding_never_reaches_the_output(dtype, n, mask, fill):
         assert (y[~ok] == 0).all(), op
         for r in range(b):
             zt, zl = to_numpy(tail[r:r + 1]), to_numpy(head[r:r + 1])
-            if op == 'avey':
+            if op.split('-')[0] == 'avey':
                 ref = oracle.avey(zt, to_numpy(w), z_tl=zl, valid=ok[r:r + 1])
             else:
                 ref = oracle.avey_b(np.abs(zt), z_tl=zl, valid=ok[r:r + 1], eps=0.5)

@@ -107,7 +107,7 @@ def test_plan_falls_back_to_cuda_core_kernel(shape, dtype, reason):
     assert plan.kernel == _native.KERNEL_SIMT and plan.reason == reason
 
 
-@pytest.mark.parametrize('shape,items', [((2, 256, 128), 2), ((64, 512, 768), 6), ((1, 1100, 72), 25)])
+@pytest.mark.parametrize('shape,items', [((8, 256, 128), 2), ((64, 512, 768), 6), ((1, 1100, 72), 25)])
 def test_plan_runs_fp32_on_the_3xtf32_kernel_pair(shape, items):
     # fp32: tf_gram_p per (query tile, key group of 256) and tf_pv, no pre-pass
     # (the split of each staged tile sums the squares); the workspace holds P
@@ -122,6 +122,32 @@ def test_plan_runs_fp32_on_the_3xtf32_kernel_pair(shape, items):
                               norm_eps=1e-12, causal=True, normalize=False, activation_id=0)
     cp = -(-n // 64) * 64
     assert _native.workspace_size(params) >= b * n * cp * 4
+
+
+@pytest.mark.parametrize('shape,dtype,small', [
+    ((2, 256, 128), torch.float32, True),     # config 1: 64 CTA pairs of 8 query rows
+    ((3, 512, 128), torch.float32, True),     # 192 query tiles: the limit
+    ((2, 96, 256), torch.float32, True),      # rows of 1 KB (64-key blocks)
+    ((4, 512, 256), torch.float32, False),    # 256 query tiles: 3xTF32 pair
+    ((2, 256, 72), torch.float32, False),     # features not a multiple of 32
+    ((2, 256, 512), torch.float32, False),    # rows above 1 KB
+    ((2, 600, 64), torch.float32, False),     # above 512 tokens
+    ((2, 256, 128), torch.bfloat16, False),   # 16-bit inputs keep the fused tcgen05 kernel
+])
+def test_plan_runs_small_fp32_problems_on_the_8_row_kernel(shape, dtype, small):
+    z = torch.randn(*shape).to(dtype)
+    b, n, _ = shape
+    v = torch.randn(n, n).to(dtype)
+    plan = ops.plan(z, v, z_tl=z)
+    if small:
+        assert plan.kernel == _native.KERNEL_SIMT and plan.reason == _native.REASON_SMALL
+        assert plan.launches == 1 and plan.block == 256 and plan.grid == 2 * b * -(-n // 8)
+        assert plan.smem_bytes <= 232_448
+        # Asked for, the 3xTF32 pair still takes these inputs.
+        forced = ops.plan(z, v, z_tl=z, kernel=_native.KERNEL_TCGEN05)
+        assert forced.kernel == _native.KERNEL_TCGEN05 and forced.launches == 2
+    else:
+        assert plan.kernel == _native.KERNEL_TCGEN05 and plan.reason == 0
 
 
 def test_plan_takes_the_long_context_tcgen05_path_above_512_tokens():
@@ -170,10 +196,14 @@ def test_workspace_size_is_four_bytes_per_row_on_the_tcgen05_path():
     assert _native.workspace_size(p) == 3 * 384 * 4
     # fp32 runs the 3xTF32 kernel pair: partial row sums and P (fp32, rows
     # padded to 64 keys) follow the per-row floats.
-    z32 = z.float()
+    z32 = torch.randn(8, 384, 256)
     p = ops.build_params(z32, None, None, None, None, z32.clone(), eps=1e-6, norm_eps=1e-12,
                          causal=False, normalize=True, activation_id=0)
-    assert _native.workspace_size(p) >= 3 * 384 * 384 * 4 + 3 * 384 * 4
+    assert _native.workspace_size(p) >= 8 * 384 * 384 * 4 + 8 * 384 * 4
+    # Small fp32 problems run the 8-row CUDA-core kernel, which needs none.
+    p = ops.build_params(z.float(), None, None, None, None, z.float(), eps=1e-6, norm_eps=1e-12,
+                         causal=False, normalize=True, activation_id=0)
+    assert _native.workspace_size(p) == 0
     # Inputs the CUDA-core kernels take need none.
     z37 = torch.randn(3, 384, 37)
     p = ops.build_params(z37, None, None, None, None, z37.clone(), eps=1e-6, norm_eps=1e-12,

@@ -82,7 +82,7 @@ def test_noalloc_entry_point_runs_fp32_on_cuda_cores():
     # avey_fwd_v1 runs aligned fp32 on the 3xTF32 kernel pair, whose P
     # workspace the no-allocation entry point does not have: it takes the
     # CUDA-core kernel, within the fp32 bound of the pair's result.
-    z = torch.rand(2, 96, 64, device='cuda')
+    z = torch.rand(2, 96, 72, device='cuda')
     assert ops.plan(z, causal=False, normalize=True).kernel == _native.KERNEL_TCGEN05
     want = _call(z, None, z, None, None, causal=False, normalize=True, act=0, noalloc=False)
     got = _call(z, None, z, None, None, causal=False, normalize=True, act=0, noalloc=True)
@@ -100,6 +100,20 @@ def test_noalloc_entry_point_rejects_inputs_beyond_its_limit():
     with pytest.raises(_native.NativeError, match='no-allocation limit'):
         _native.forward_noalloc(params, 0)
     assert _native.launch_count() == before
+
+
+@pytest.mark.gpu
+def test_noalloc_entry_point_runs_small_fp32_on_the_8_row_kernel():
+    # Small fp32 problems run the 8-row CUDA-core kernel on both entry points
+    # (it needs no workspace): the results agree bit for bit.
+    z = torch.rand(2, 96, 64, device='cuda')
+    plan = ops.plan(z, causal=False, normalize=True)
+    assert plan.kernel == _native.KERNEL_SIMT and plan.reason == _native.REASON_SMALL
+    before = _native.launch_count()
+    got = _call(z, None, z, None, None, causal=False, normalize=True, act=0, noalloc=True)
+    assert _native.launch_count() == before + 1
+    want = _call(z, None, z, None, None, causal=False, normalize=True, act=0, noalloc=False)
+    assert torch.equal(got, want)
 
 
 @pytest.mark.gpu
