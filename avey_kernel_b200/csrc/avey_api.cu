@@ -683,17 +683,21 @@ bool small_ok(const AveyFwdParams* p) {
          (p->z_tr_batch_stride % 4 == 0 || p->batch == 1);
 }
 
-// Query tiles (batch x ceil(context / 8)) up to which the 8-row kernel, one
-// CTA pair per tile and one CTA per SM, finishes before the 3xTF32 kernel
-// pair. Measured on a B200 (fp32, Avey causal): at 64 tiles 10.8 against
-// 37.4 us (config 1), at 128 tiles 20.7 / 36.4 against 37.4 / 68.3 us, at 256
-// tiles 39.7 / 49.5 against 37.4 / 51.6 us. AUTO picks it up to here (reason
-// kReasonSmall); a forced AVEY_KERNEL_SIMT keeps the two-phase kernel.
-constexpr int64_t kSmallTiles = 192;
+// Where the 8-row kernel finishes before the 3xTF32 kernel pair: each query
+// tile of 8 rows runs on a CTA pair, one CTA per SM, so a wave is 74 tiles
+// on the 148 SMs of a B200 and costs about 9 us (11.5 us at 512 tokens);
+// the pair takes about 20 / 25 / 37 / 51 us at 64 / 128 / 256 / 512 tokens
+// (fp32, Avey causal, 128 features, few rows). Measured: 9.8 against 36.8 us
+// at config 1 (64 tiles), 35.1 against 37.2 us at 8 x 256 tokens (256 tiles),
+// 25.7 against 20.6 us at 24 x 64 tokens (192 tiles). So AUTO picks it
+// (reason kReasonSmall) for up to 4 waves of tiles above 128 tokens and up to
+// 2 waves at or below; a forced AVEY_KERNEL_SIMT keeps the two-phase kernel.
+constexpr int64_t kSmallTilesPerWave = 74;
 
 bool small_pick(const AveyFwdParams* p) {
-  return small_ok(p) &&
-         p->batch * ((p->context + avey::kSmRows - 1) / avey::kSmRows) <= kSmallTiles;
+  if (!small_ok(p)) return false;
+  const int64_t tiles = p->batch * ((p->context + avey::kSmRows - 1) / avey::kSmRows);
+  return tiles <= (p->context > 128 ? 4 : 2) * kSmallTilesPerWave;
 }
 
 int launch_small(const AveyFwdParams* p, cudaStream_t stream) {

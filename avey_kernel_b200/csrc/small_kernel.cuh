@@ -8,7 +8,7 @@
 //
 //   key blocks of kb rows (128, or 64 for rows of more than 512 bytes) are
 //   copied to shared memory with cp.async, two blocks in flight; per block
-//   phase 1  S = Z_q Z_k^T for the 8 query rows: 256 / kb threads per key,
+//   phase 1  S = Z_q Z_k^T for the 8 query rows: 512 / kb threads per key,
 //            each over its slice of the features (the key's sum of squares
 //            comes from the same loads); the slices are summed in a fixed
 //            order, then P = S * rinv_q * rinv_k * V under the masks goes to
@@ -34,12 +34,14 @@
 namespace avey {
 
 constexpr int kSmRows = 8;  // query rows per cluster
-constexpr int kSmThreads = 256;
+constexpr int kSmThreads = 512;
 constexpr int kSmWarps = kSmThreads / 32;
 constexpr int kSmMaxCtx = 512;
 constexpr int kSmMaxRowBytes = 1024;                        // features x 4 bytes
 constexpr int kSmRedBytes = kSmWarps * kSmRows * 128 * 4;  // phase-2 partial sums
 constexpr int kSmMaxOut = kSmRows / 2 * kSmMaxRowBytes / 4 / kSmThreads;  // outputs per thread
+constexpr int kSmRptMax = kSmRows * 128 / kSmThreads;  // P rows per thread (128-key blocks)
+static_assert(kSmRptMax >= 1 && kSmMaxOut >= 1, "512 threads: 4 or 8 threads per key");
 
 // Shared-memory layout of one CTA (byte offsets), chosen by the host from the
 // feature count.
@@ -48,7 +50,7 @@ struct SmallGeom {
   int stride;  // bytes per staged row: row bytes + 16 (spreads rows over the banks)
   int zbuf;    // offset of the second key block
   int qbuf;    // the 8 query rows
-  int part;    // phase-1 partial sums [256 / kb][9][kb]
+  int part;    // phase-1 partial sums [threads / kb][9][kb]
   int pbuf;    // P [kb][8][2] (each value twice: the pair operand of phase 2)
   int osum;    // this CTA's partial O [8][features]
   int misc;    // rq, den, dpart, row flags, key mask
@@ -98,6 +100,8 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   return v;
 }
 
+// 16 warps per CTA (4 per scheduler) hide the latency of each phase; the
+// launch bound keeps the registers at 128 per thread.
 __global__ void __launch_bounds__(kSmThreads, 1)
     small_contextualize(const FwdArgs args, const SmallGeom g) {
   extern __shared__ __align__(16) char sm_raw[];
@@ -126,6 +130,55 @@ __global__ void __launch_bounds__(kSmThreads, 1)
   const int nseg = row_bytes / 16;
   const float* zr = static_cast<const float*>(args.z_tr) + static_cast<int64_t>(b) * args.zr_bs;
 
+  // Valid positions: all of them without a padding mask (no barrier before
+  // the first copies); with one, the row's mask is cached in shared memory
+  // (C <= 512 here) with its last valid position.
+  const bool masked = args.has_valid != 0;
+  int kv_end = C;
+  if (masked) {
+    if (tid == 0) last_valid_s = -1;
+    __syncthreads();
+    int last = -1;
+    for (int j = tid; j < C; j += kSmThreads) {
+      const uint8_t ok = mask_ok(args, b, j) ? 1 : 0;
+      kv_s[j] = ok;
+      if (ok) last = j;
+    }
+    if (last >= 0) atomicMax(&last_valid_s, last);
+    __syncthreads();
+    kv_end = last_valid_s + 1;
+  }
+  auto kv = [&](int j) { return !masked || kv_s[j] != 0; };
+  const int key_end = args.causal ? min(kv_end, q0 + kSmRows) : kv_end;
+  // This CTA's keys: the even CTA the first half (rounded up to 32 keys).
+  const int half = min(key_end, (((key_end + 1) >> 1) + 31) & ~31);
+  const int kbeg = rank ? half : 0, kend = rank ? key_end : half;
+  const int nblk = (kend - kbeg + kb - 1) / kb;
+  if (tid < kSmRows) {
+    const int i = q0 + tid;
+    row_ok_s[tid] = (i < C && kv(i)) ? 1 : 0;
+    den[tid] = 0.f;
+  }
+
+  // Copies rows [r0, r0 + n) of z_tr into `dst` (rows of `stride` bytes), a
+  // warp per row and a lane per 16 bytes; rows that are padding or at or past
+  // `end` are zero-filled without a read.
+  auto copy_rows = [&](char* dst, int r0, int n, int end) {
+    const uint32_t base = smem_u32(dst);
+    for (int r = warp; r < n; r += kSmWarps) {
+      const int j = r0 + r;
+      const bool ok = j < end && kv(j);
+      const char* src = reinterpret_cast<const char*>(zr + static_cast<int64_t>(ok ? j : 0) * args.zr_rs);
+      for (int s = lane; s < nseg; s += 32)
+        cp_async16(base + r * stride + 16 * s, src + 16 * s, ok ? 16u : 0u);
+    }
+  };
+  copy_rows(qb, q0, kSmRows, C);
+  if (nblk > 0) copy_rows(zb, kbeg, kb, kend);
+  cp_async_commit();
+  if (nblk > 1) copy_rows(zb + g.zbuf, kbeg + kb, kb, kend);
+  cp_async_commit();
+
   // Gate and bias of this CTA's outputs (rows 4 rank .. 4 rank + 3), fetched
   // now so their latency hides behind the products.
   const int r_lo = 4 * static_cast<int>(rank);
@@ -143,48 +196,6 @@ __global__ void __launch_bounds__(kSmThreads, 1)
     }
   }
 
-  // Key validity of the row (C <= 512 here) and its last valid position.
-  if (tid == 0) last_valid_s = -1;
-  __syncthreads();
-  {
-    int last = -1;
-    for (int j = tid; j < C; j += kSmThreads) {
-      const uint8_t ok = mask_ok(args, b, j) ? 1 : 0;
-      kv_s[j] = ok;
-      if (ok) last = j;
-    }
-    if (last >= 0) atomicMax(&last_valid_s, last);
-  }
-  __syncthreads();
-  const int kv_end = last_valid_s + 1;
-  const int key_end = args.causal ? min(kv_end, q0 + kSmRows) : kv_end;
-  // This CTA's keys: the even CTA the first half (rounded up to 32 keys).
-  const int half = min(key_end, (((key_end + 1) >> 1) + 31) & ~31);
-  const int kbeg = rank ? half : 0, kend = rank ? key_end : half;
-  const int nblk = (kend - kbeg + kb - 1) / kb;
-  if (tid < kSmRows) {
-    const int i = q0 + tid;
-    row_ok_s[tid] = (i < C && kv_s[i]) ? 1 : 0;
-    den[tid] = 0.f;
-  }
-
-  // Copies rows [r0, r0 + n) of z_tr into `dst` (rows of `stride` bytes);
-  // rows that are padding or at or past `end` are zero-filled without a read.
-  auto copy_rows = [&](char* dst, int r0, int n, int end) {
-    const uint32_t base = smem_u32(dst);
-    for (int idx = tid; idx < n * nseg; idx += kSmThreads) {
-      const int r = idx / nseg, s = idx - r * nseg, j = r0 + r;
-      const bool ok = j < end && kv_s[j];
-      const char* src = reinterpret_cast<const char*>(zr + static_cast<int64_t>(ok ? j : 0) * args.zr_rs);
-      cp_async16(base + r * stride + 16 * s, src + 16 * s, ok ? 16u : 0u);
-    }
-  };
-  copy_rows(qb, q0, kSmRows, C);
-  if (nblk > 0) copy_rows(zb, kbeg, kb, kend);
-  cp_async_commit();
-  if (nblk > 1) copy_rows(zb + g.zbuf, kbeg + kb, kb, kend);
-  cp_async_commit();
-
   const float norm_eps = args.norm_eps_f;
   const int kk = tid % kb, h = tid / kb;  // phase 1: key kk, feature slice h
   const int seg_bytes = row_bytes / kpt;
@@ -199,12 +210,14 @@ __global__ void __launch_bounds__(kSmThreads, 1)
     const int k0 = kbeg + n * kb;
     char* zcur = zb + (n & 1) * g.zbuf;
     // V of this thread's P entries, fetched before the wait.
-    float vreg[4] = {1.f, 1.f, 1.f, 1.f};
+    float vreg[kSmRptMax];
+#pragma unroll
+    for (int u = 0; u < kSmRptMax; ++u) vreg[u] = 1.f;
     {
       const int j = k0 + kk;
       if (args.has_v && j < kend)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kSmRptMax; ++u) {
           const int i = q0 + h * rpt + u;
           if (u < rpt && i < C)
             vreg[u] = __ldg(static_cast<const float*>(args.v) + static_cast<int64_t>(i) * args.v_rs + j);
@@ -212,7 +225,7 @@ __global__ void __launch_bounds__(kSmThreads, 1)
     }
     cp_async_wait_1();  // this block's group; the next block's may stay in flight
     __syncthreads();
-    if (n == 0) {  // inverse query norms, a warp per row
+    if (n == 0 && warp < kSmRows) {  // inverse query norms, a warp per row
       float ss = 0.f;
       for (int s = lane; s < nseg; s += 32) {
         const float4 x = *reinterpret_cast<const float4*>(qb + warp * stride + 16 * s);
@@ -258,9 +271,9 @@ __global__ void __launch_bounds__(kSmThreads, 1)
       float ss = 0.f;
       for (int hh = 0; hh < kpt; ++hh) ss += part[(hh * 9 + 8) * kb + kk];
       const float rk = 1.f / fmaxf(sqrtf(ss), norm_eps);
-      const bool key_ok = j < kend && kv_s[j];
+      const bool key_ok = j < kend && kv(j);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kSmRptMax; ++u) {
         if (u >= rpt) break;  // uniform across the warp
         const int r = h * rpt + u, i = q0 + r;
         float s = 0.f;
@@ -357,7 +370,9 @@ __global__ void __launch_bounds__(kSmThreads, 1)
     }
     out[static_cast<int64_t>(i) * args.o_rs + f] = y;
   }
-  cluster_sync();  // the peer has read this CTA's shared memory
+  // The peer has read this CTA's shared memory (no data is published here, so
+  // the arrive needs no release).
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
 }  // namespace avey

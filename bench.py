@@ -58,7 +58,8 @@ CONFIGS = {
     # dtype bf16 unless given)
     'c1': dict(batch=2, n=256, d=128, op='avey', bias=True, zero_bias=True, ragged=False,
                boost=False, scaling='weak', dtype='f32',
-               desc="Avey causal, fp32, B=2 per GPU, N=256, d'=128, bias 0 (3xTF32 tensor cores)"),
+               desc="Avey causal, fp32, B=2 per GPU, N=256, d'=128, bias 0 (8-row CUDA-core "
+                    "kernel on CTA pairs)"),
     'c2f32': dict(batch=64, n=512, d=768, op='avey', bias=True, ragged=False, boost=False,
                   scaling='weak', dtype='f32',
                   desc="config 2's shape in fp32 (3xTF32 tensor cores): Avey causal, B=64 per GPU, "
@@ -460,6 +461,8 @@ def run_ours(args, cfg):
     f32 = cfg.get('dtype') == 'f32'
     if plan.kernel == 2 and f32:  # fp32: the 3xTF32 pair, no pre-pass
         kernel_name = 'tf_gram_p + tf_pv (whole step)'
+    if plan.reason == _native.REASON_SMALL:  # small fp32 problems: the 8-row CUDA-core kernel
+        kernel_name = 'small_contextualize (whole step)'
 
     # Warm-up (untimed), then capture chunks of steps into CUDA graphs.
     for i in range(max(args.warmup, 3)):

@@ -107,7 +107,7 @@ def test_plan_falls_back_to_cuda_core_kernel(shape, dtype, reason):
     assert plan.kernel == _native.KERNEL_SIMT and plan.reason == reason
 
 
-@pytest.mark.parametrize('shape,items', [((8, 256, 128), 2), ((64, 512, 768), 6), ((1, 1100, 72), 25)])
+@pytest.mark.parametrize('shape,items', [((16, 256, 128), 2), ((64, 512, 768), 6), ((1, 1100, 72), 25)])
 def test_plan_runs_fp32_on_the_3xtf32_kernel_pair(shape, items):
     # fp32: tf_gram_p per (query tile, key group of 256) and tf_pv, no pre-pass
     # (the split of each staged tile sums the squares); the workspace holds P
@@ -126,9 +126,12 @@ def test_plan_runs_fp32_on_the_3xtf32_kernel_pair(shape, items):
 
 @pytest.mark.parametrize('shape,dtype,small', [
     ((2, 256, 128), torch.float32, True),     # config 1: 64 CTA pairs of 8 query rows
-    ((3, 512, 128), torch.float32, True),     # 192 query tiles: the limit
+    ((4, 512, 128), torch.float32, True),     # 256 query tiles: within 4 waves of 74
+    ((5, 512, 128), torch.float32, False),    # 320 query tiles: 3xTF32 pair
+    ((18, 64, 128), torch.float32, True),     # 144 tiles of short rows: within 2 waves
+    ((19, 64, 128), torch.float32, False),    # 152 tiles of short rows: 3xTF32 pair
     ((2, 96, 256), torch.float32, True),      # rows of 1 KB (64-key blocks)
-    ((4, 512, 256), torch.float32, False),    # 256 query tiles: 3xTF32 pair
+    ((8, 512, 256), torch.float32, False),    # 512 query tiles: 3xTF32 pair
     ((2, 256, 72), torch.float32, False),     # features not a multiple of 32
     ((2, 256, 512), torch.float32, False),    # rows above 1 KB
     ((2, 600, 64), torch.float32, False),     # above 512 tokens
@@ -141,7 +144,7 @@ def test_plan_runs_small_fp32_problems_on_the_8_row_kernel(shape, dtype, small):
     plan = ops.plan(z, v, z_tl=z)
     if small:
         assert plan.kernel == _native.KERNEL_SIMT and plan.reason == _native.REASON_SMALL
-        assert plan.launches == 1 and plan.block == 256 and plan.grid == 2 * b * -(-n // 8)
+        assert plan.launches == 1 and plan.block == 512 and plan.grid == 2 * b * -(-n // 8)
         assert plan.smem_bytes <= 232_448
         # Asked for, the 3xTF32 pair still takes these inputs.
         forced = ops.plan(z, v, z_tl=z, kernel=_native.KERNEL_TCGEN05)

@@ -2,8 +2,9 @@
 B200, against the oracle.
 
 AUTO runs small fp32 inputs (contexts up to 512, features a multiple of 32
-up to 256, at most 192 query tiles of 8 rows) on this kernel, config 1 among
-them; each tile runs on a CTA pair that splits its keys. Bound: the north-star fp32 bound norm-wise (1e-4), and 1e-5
+up to 256, up to 4 waves of query tiles of 8 rows, 2 at 128 tokens or fewer)
+on this kernel, config 1 among them; each tile runs on a CTA pair that splits
+its keys. Bound: the north-star fp32 bound norm-wise (1e-4), and 1e-5
 elementwise (rtol, with an atol of 1e-5 of the largest output). Covered:
 Avey (causal, learned V, bias, every activation) and Avey-B (bidirectional,
 signed row-sum divide), both key-block sizes (128 keys for rows up to 512
