@@ -392,6 +392,9 @@ int encode_map_dims(int dtype, const void* base, uint64_t inner, uint64_t rows, 
 struct PreSum {
   const float* planes = nullptr;
   int n = 0;
+  // Without planes: the fused kernel sums the rows' squares itself, unless
+  // prepass is set (norm_prepass writes them to the workspace first).
+  bool prepass = false;
 };
 
 template <typename T>
@@ -620,8 +623,7 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps) {
   if (rc != AVEY_OK) return rc;
   rc = encode_map(p, p->out, p->out_batch_stride, p->out_row_stride, 32, 32, &map_o);
   if (rc != AVEY_OK) return rc;
-  const TcLayout l = tc_layout(p);
-  if (l.geom.v_tma) {
+  if (tc_layout(p).geom.v_tma) {
     // V [query, key] as a 2-D map (one "batch"): {64 keys, 128 query rows} boxes.
     rc = encode_map_dims(p->dtype, p->v, static_cast<uint64_t>(p->context),
                          static_cast<uint64_t>(p->context), 1,
@@ -630,13 +632,21 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps) {
     if (rc != AVEY_OK) return rc;
   }
   const avey::FwdArgs args = make_args(p);
+  TcLayout l = tc_layout(p);
+  l.geom.self_sums = (ps.planes || ps.prepass) ? 0 : 1;
   const uint64_t need = static_cast<uint64_t>(p->batch) * p->context * sizeof(float);
-  if (!p->workspace || p->workspace_bytes < need || (reinterpret_cast<uintptr_t>(p->workspace) & 3u))
-    return fail(AVEY_ERR_ARGUMENT, "the tcgen05 path needs a 4-byte aligned workspace of %llu bytes",
+  if (!l.geom.self_sums &&
+      (!p->workspace || p->workspace_bytes < need || (reinterpret_cast<uintptr_t>(p->workspace) & 3u)))
+    return fail(AVEY_ERR_ARGUMENT,
+                "the row sums of squares need a 4-byte aligned workspace of %llu bytes",
                 (unsigned long long)need);
-  // 1. Row sums of squares (the first launch lets the second start at once).
-  rc = launch_row_sums<T>(p, args, ps, stream);
-  if (rc != AVEY_OK) return rc;
+  // 1. Row sums of squares into the workspace, from given planes or by the
+  //    pre-pass (the first launch lets the second start at once); otherwise
+  //    the fused kernel sums the rows itself.
+  if (!l.geom.self_sums) {
+    rc = launch_row_sums<T>(p, args, ps, stream);
+    if (rc != AVEY_OK) return rc;
+  }
   cudaError_t e = cudaSuccess;
   // 2. The fused kernel, as a programmatic dependent of the pre-pass: it waits
   //    for the sums only before its P phase.
@@ -971,7 +981,7 @@ int avey_fwd_plan(const AveyFwdParams* p, AveyPlan* plan) {
   } else if (reason == kReasonNone) {
     const TcLayout l = tc_layout(p);
     plan->kernel = AVEY_KERNEL_TCGEN05;
-    plan->launches = 2;
+    plan->launches = 1;  // the fused kernel sums the rows' squares itself
     plan->grid = static_cast<int32_t>(p->batch * l.geom.n_qtiles);
     plan->block = avey::kTcThreads;
     plan->smem_bytes = l.smem;
@@ -1000,12 +1010,8 @@ int avey_fwd_workspace_size(const AveyFwdParams* p, uint64_t* bytes) {
   const int rc = avey_fwd_plan(p, &plan);
   if (rc != AVEY_OK) return rc;
   if (!bytes) return fail(AVEY_ERR_ARGUMENT, "bytes is NULL");
-  if (plan.kernel != AVEY_KERNEL_TCGEN05)
-    *bytes = 0u;
-  else if (is_pair(p))
-    *bytes = long_layout(p).total;
-  else
-    *bytes = static_cast<uint64_t>(p->batch) * static_cast<uint64_t>(p->context) * sizeof(float);
+  // The fused kernel (up to 512 tokens, 16-bit) sums the rows' squares itself.
+  *bytes = (plan.kernel == AVEY_KERNEL_TCGEN05 && is_pair(p)) ? long_layout(p).total : 0u;
   return ok();
 }
 
@@ -1096,7 +1102,15 @@ int avey_fwd_noalloc_v1(const AveyFwdParams* p, void* stream) {
                 cudaGetErrorString(g_noalloc_err[dev]));
   q.workspace = g_noalloc_ptr[dev];
   q.workspace_bytes = static_cast<uint64_t>(AVEY_NOALLOC_MAX_ROWS) * sizeof(float);
-  return avey_fwd_v1(&q, stream);
+  // The pre-pass variant of the fused kernel: row sums of squares in the
+  // array, read back by the kernel.
+  rc = device_arch_ok(nullptr);
+  if (rc != AVEY_OK) return rc;
+  PreSum pre;
+  pre.prepass = true;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return q.dtype == AVEY_BF16 ? launch_tc_act<__nv_bfloat16>(&q, s, pre)
+                              : launch_tc_act<__half>(&q, s, pre);
 }
 
 int avey_gemm_v1(const AveyGemmParams* p, void* stream) {

@@ -69,6 +69,8 @@ struct TcGeom {
   int n_qtiles;  // query tiles per batch row
   int v_tma;     // V tiles reach shared memory by TMA (aligned V), else per-thread loads
   int test_stall;  // test hook: the TMA and MMA warps issue nothing, so waits run out
+  int self_sums;   // the compute warps sum the key rows' squares from the phase-A stages
+                   // (no row-sum pre-pass; args.sumsq is not read)
 };
 
 // TMEM column of the packed P pair holding key j (two keys per 32-bit column).
@@ -198,6 +200,14 @@ __device__ __forceinline__ void p_chunk(const uint32_t (&g)[32], const float (&r
   }
 }
 
+// The two 16-bit values packed in w (low half first) as fp32.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  T h[2];
+  memcpy(h, &w, 4);
+  return make_float2(to_f32<T>(h[0]), to_f32<T>(h[1]));
+}
+
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -295,7 +305,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kTcMaxStages; ++s) {
       mbar_init(smem_u32(&ctrl->a_full[s]), 1);
-      mbar_init(smem_u32(&ctrl->a_empty[s]), 1);
+      // Released by the MMAs' commit, and with self_sums also by every
+      // compute warp once it has read the stage.
+      mbar_init(smem_u32(&ctrl->a_empty[s]), geom.self_sums ? 9 : 1);
     }
     for (int s = 0; s < kTcMaxSlots; ++s) {
       mbar_init(smem_u32(&ctrl->full[s]), 1);
@@ -552,11 +564,55 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int nbytes = min(64, D - h * 64) * 2;
         for (int l = 0; l < nbytes; l += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(grow + l));
       }
-      // ---------------- phase A (compute warps): sums of squares of the key rows
-      // from norm_prepass, which may still be running (programmatic dependent
-      // launch): wait for it only here.
-      griddep_wait();
-      {
+      // ---------------- phase A (compute warps): sums of squares of the key rows.
+      if (geom.self_sums) {
+        // From the phase-A stages, as the Gram consumes them: thread tid_c sums
+        // key rows tid_c and tid_c + 256 over every 64-feature chunk. A row's
+        // 128 bytes hold its 8 granules of 16 bytes in swizzled order (granule
+        // g at g ^ (row & 7)); visiting granule k ^ (row & 7) at step k keeps
+        // the 8 rows of each access phase on distinct banks.
+        const int tid_c = cw * 32 + lane;
+        float ss[2] = {0.f, 0.f};
+        int st = 0;
+        uint32_t ph = 0;
+        for (int c = 0; c < nchunk; ++c) {
+          const bool ok = mbar_wait(smem_u32(&ctrl->a_full[st]), ph);
+          if (ok) {
+            const uint32_t stage = stage_addr + st * a_stage_bytes;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const int j = tid_c + 256 * q;
+              if (j < nk * 128) {
+                const uint32_t rowa = stage + (j >> 7) * kTcTileBytesA + (j & 127) * 128;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  const uint4 v = ld_shared_v4(rowa + ((k ^ (j & 7)) << 4));
+                  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float2 f = unpack2<T>(w[e]);
+                    ss[q] = fmaf(f.x, f.x, fmaf(f.y, f.y, ss[q]));
+                  }
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctrl->a_empty[st]));
+          if (++st == nst) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int j = tid_c + 256 * q;
+          if (j < nk * 128) ctrl->rinv[j] = j < C ? ss[q] : 0.f;
+        }
+      } else {
+        // From the row-sum pre-pass, which may still be running (programmatic
+        // dependent launch): wait for it only here.
+        griddep_wait();
         const float* ssq = args.sumsq + static_cast<int64_t>(b) * C;
         for (int j = cw * 32 + lane; j < nk * 128; j += 256) ctrl->rinv[j] = j < C ? ssq[j] : 0.f;
       }

@@ -129,7 +129,9 @@ def _contextualize_presummed(z_tr, v, z_tl, bias, valid, sums, *, eps, norm_eps,
     params = ops.build_params(z_tr, v, z_tl, bias, valid, out, eps=eps, norm_eps=norm_eps,
                               causal=causal, normalize=normalize,
                               activation_id=_ACT_IDS[activation])
-    nbytes = _native.workspace_size(params)
+    # Up to 512 tokens the planes are combined into a workspace of one float
+    # per row; above, the long-context path's workspace.
+    nbytes = max(_native.workspace_size(params), 4 * z_tr.shape[0] * z_tr.shape[1])
     with torch.cuda.device(z_tr.device):
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=z_tr.device)
         params.workspace, params.workspace_bytes = ws.data_ptr(), nbytes

@@ -455,7 +455,7 @@ def run_ours(args, cfg):
     verify_err = max_over_ranks(verify_err, device=dev)
     plan = ops.plan(sets[0]['x'][..., d:], sets[0]['w'], sets[0]['x'][..., :d], sets[0]['bias'],
                     sets[0]['valid'], causal=cfg['op'] == 'avey', normalize=cfg['op'] != 'avey')
-    kernel_name = {1: 'simt_contextualize', 2: 'norm_prepass + tc_contextualize (whole step)'}[plan.kernel]
+    kernel_name = {1: 'simt_contextualize', 2: 'tc_contextualize (whole step)'}[plan.kernel]
     if plan.kernel == 2 and plan.launches == 3:  # contexts above 512: two tensor-core kernels
         kernel_name = 'norm_prepass + tc_gram_p + tc_pv (whole step)'
     f32 = cfg.get('dtype') == 'f32'

@@ -117,9 +117,10 @@ typedef struct AveyFwdParams {
 /* What avey_fwd_v1 would launch for these parameters. */
 typedef struct AveyPlan {
   int32_t kernel;        /* AVEY_KERNEL_SIMT or AVEY_KERNEL_TCGEN05 */
-  int32_t launches;      /* kernel launches per call: 2 on the tcgen05 path up to
-                            512 tokens (row-norm pre-pass, fused kernel), 3 above
-                            (pre-pass, G/P kernel, O = P Z kernel), 1 on CUDA cores */
+  int32_t launches;      /* kernel launches per call: 1 on the tcgen05 path up to
+                            512 tokens (the fused kernel), 3 above (row-sum pre-pass,
+                            G/P kernel, O = P Z kernel), 2 for fp32 on the 3xTF32
+                            pair, 1 on CUDA cores */
   int32_t grid;          /* CTAs of the main launch */
   int32_t block;         /* threads per CTA of the main launch */
   int32_t smem_bytes;    /* dynamic shared memory per CTA */
@@ -145,13 +146,15 @@ AVEY_API int avey_fwd_v1(const AveyFwdParams* params, void* stream);
 AVEY_API int avey_fwd_plan(const AveyFwdParams* params, AveyPlan* plan);
 
 /* Device workspace avey_fwd_v1 needs for these parameters, in bytes: 0 for the
- * CUDA-core kernel; on the tcgen05 path 4 per row of z_tr (batch x context)
- * up to 512 tokens, and above 512 tokens, in 256-byte aligned parts, those
- * row sums, 4 bytes per row per group of 256 keys (partial row sums) and P
- * itself (2 bytes per (query, key) pair, rows padded to 64 keys): 134 MB for
- * batch 16 x 2048 tokens. The workspace must be 256-byte aligned. The
- * reference allocates its normalisation buffer itself (ops.py:108); this
- * library leaves allocation to the caller. Launches nothing. */
+ * CUDA-core kernels and for the fused tcgen05 kernel (up to 512 tokens: it
+ * sums the rows' squares from the tiles it stages); above 512 tokens and for
+ * fp32 on the 3xTF32 pair, in 256-byte aligned parts, the row sums of squares
+ * (4 bytes per row of z_tr), 4 bytes per row per group of 256 keys (partial
+ * row sums) and P itself (2 bytes per (query, key) pair, 4 for fp32, rows
+ * padded to 64 keys): 134 MB for batch 16 x 2048 tokens. The workspace must
+ * be 256-byte aligned. The reference allocates its normalisation buffer
+ * itself (ops.py:108); this library leaves allocation to the caller.
+ * Launches nothing. */
 AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* bytes);
 
 /*
@@ -168,8 +171,14 @@ AVEY_API int avey_fwd_workspace_size(const AveyFwdParams* params, uint64_t* byte
  * for them needs a P workspace); forcing AVEY_KERNEL_TCGEN05 for them fails
  * with AVEY_ERR_UNSUPPORTED.
  *
- * Limit: on the fused tensor-core path (bf16 / f16 up to 512 tokens, the only
- * path that reads the scratch) batch * context <= AVEY_NOALLOC_MAX_ROWS
+ * On the fused tensor-core path (bf16 / f16 up to 512 tokens) this entry point
+ * runs the kernel's pre-pass variant: a row-norm pre-pass writes each row's
+ * sum of squares into the array and the fused kernel reads them, where
+ * avey_fwd_v1 has the fused kernel sum the rows itself; the two agree to
+ * the rounding of those sums.
+ *
+ * Limit: on the fused tensor-core path (the only path that reads the
+ * scratch) batch * context <= AVEY_NOALLOC_MAX_ROWS
  * (1,048,576 rows; the array holds one float per row, 4 MiB per GPU); larger
  * inputs are rejected with AVEY_ERR_ARGUMENT. Inputs that run a CUDA-core
  * kernel use no scratch and have no such limit. The first call on each device
@@ -367,9 +376,11 @@ AVEY_API int avey_gemm_v1(const AveyGemmParams* params, void* stream);
  * ops.py:107-108, is always a separate pass over z_tr): `sumsq` holds
  * `planes` planes of batch*context floats, summed in plane order, as written
  * by the enricher's avey_gemm_v1 epilogue (its tail columns). The norm
- * pre-pass of the tcgen05 path is skipped; other paths ignore the sums.
- * params->workspace is still required (the pre-summed planes are read, never
- * written).
+ * fused tcgen05 kernel and the long-context path read these sums instead of
+ * summing z_tr's rows; other paths ignore them. Up to 512 tokens the planes
+ * are combined into params->workspace, which must then hold batch * context
+ * floats (4-byte aligned); above 512 tokens the workspace is the one
+ * avey_fwd_workspace_size reports.
  */
 AVEY_API int avey_fwd_presummed_v1(const AveyFwdParams* params, const float* sumsq, int planes,
                                    void* stream);

@@ -83,7 +83,7 @@ def test_plan_chooses_tcgen05_for_aligned_16bit_inputs():
     z = torch.randn(4, 512, 768).to(torch.bfloat16)
     plan = ops.plan(z, torch.randn(512, 512).to(torch.bfloat16), z_tl=z)
     assert plan.kernel == _native.KERNEL_TCGEN05 and plan.reason == 0
-    assert plan.grid == 4 * 4 and plan.block == 384 and plan.launches == 2
+    assert plan.grid == 4 * 4 and plan.block == 384 and plan.launches == 1
     assert 200_000 < plan.smem_bytes <= 232_448
 
 
@@ -191,12 +191,20 @@ def test_ctypes_struct_matches_header_field_order():
     assert ctypes.sizeof(_native.AveyFwdParams) == 208
 
 
-def test_workspace_size_is_four_bytes_per_row_on_the_tcgen05_path():
+def test_workspace_size_by_path():
+    # The fused tcgen05 kernel (16-bit, up to 512 tokens) sums the rows'
+    # squares itself: no workspace.
     z = torch.randn(3, 384, 256).to(torch.bfloat16)
     out = torch.empty_like(z)
     p = ops.build_params(z, None, None, None, None, out, eps=1e-6, norm_eps=1e-12, causal=False,
                          normalize=True, activation_id=0)
-    assert _native.workspace_size(p) == 3 * 384 * 4
+    assert ops.plan(z, causal=False, normalize=True).kernel == _native.KERNEL_TCGEN05
+    assert _native.workspace_size(p) == 0
+    # Above 512 tokens: row sums, partial row sums and P (bf16, rows padded to 64 keys).
+    zl = torch.randn(2, 600, 64).to(torch.bfloat16)
+    p = ops.build_params(zl, None, None, None, None, zl.clone(), eps=1e-6, norm_eps=1e-12,
+                         causal=False, normalize=True, activation_id=0)
+    assert _native.workspace_size(p) >= 2 * 600 * 640 * 2 + 2 * 600 * 4
     # fp32 runs the 3xTF32 kernel pair: partial row sums and P (fp32, rows
     # padded to 64 keys) follow the per-row floats.
     z32 = torch.randn(8, 384, 256)

@@ -5,9 +5,12 @@ hands raw pointers over, or code running while a stream is captured into a
 CUDA graph, where allocation is not allowed). For them the library keeps its
 scratch -- one float per row of z_tr -- in an array of its own, up to
 AVEY_NOALLOC_MAX_ROWS rows. These tests call that entry point through the C
-ABI and check it against avey_fwd_v1 (which takes the scratch from the
-caller), on two calls in a row: the second call finds the first call's sums
-still in the shared array and must not depend on them.
+ABI and check it against avey_fwd_v1 on calls in a row: a later call finds an
+earlier call's sums still in the shared array and must not depend on them.
+On the fused tensor-core path this entry point runs the kernel's pre-pass
+variant (row sums in the array) where avey_fwd_v1 sums the rows inside the
+kernel, so the two agree within the bf16 tolerance, and a repeated call of
+this entry point agrees with itself bit for bit.
 
 This file is collected last on purpose, so a run that stops at the first
 failure has already run every other test.
@@ -48,6 +51,7 @@ def test_noalloc_entry_point_matches_the_workspace_entry_point_on_two_calls():
         # so the array still holds the first call's sums past these rows
         dict(b=3, n=384, d=256, causal=False, normalize=True, act=4, weight=False, mask=True),
     ]
+    first = None
     for c in cases:
         x = torch.randn(c['b'], c['n'], 2 * c['d'], generator=g).to(torch.bfloat16).cuda()
         head, tail = x[..., :c['d']], x[..., c['d']:]
@@ -64,8 +68,12 @@ def test_noalloc_entry_point_matches_the_workspace_entry_point_on_two_calls():
         got = _call(tail, v, head, None, valid, noalloc=True, **kw)
         assert np.isfinite(to_numpy(got)).all()
         assert norm_rel_err(to_numpy(got), to_numpy(want)) <= TOL['bfloat16']
-        # Same kernels, same arithmetic: the results agree bit for bit.
-        assert torch.equal(got, want)
+        if first is None:
+            first = (tail, v, head, valid, kw, got)
+    # The first case again, after the second left its sums in the array: the
+    # same bits as its first call.
+    tail, v, head, valid, kw, got = first
+    assert torch.equal(_call(tail, v, head, None, valid, noalloc=True, **kw), got)
     assert _native.device_status(clear=True) == 0
 
 
@@ -148,14 +156,15 @@ def test_noalloc_entry_point_runs_cuda_core_inputs_past_the_row_limit():
 def test_noalloc_entry_point_replays_from_a_cuda_graph():
     # Graph capture is one of the situations with no allocator: warm up once
     # (the first call on a device looks up the scratch address), capture one
-    # call into a CUDA graph, replay it, and compare with the workspace entry
-    # point bit for bit.
+    # call into a CUDA graph, replay it, and compare with an eager call of the
+    # same entry point bit for bit, and with avey_fwd_v1 within the tolerance.
     g = torch.Generator().manual_seed(5)
     x = torch.randn(4, 512, 2 * 256, generator=g).to(torch.bfloat16).cuda()
     head, tail = x[..., :256], x[..., 256:]
     v = (torch.randn(512, 512, generator=g) * 0.02).to(torch.bfloat16).cuda()
-    want = _call(tail, v, head, None, None, causal=True, normalize=False, act=3, noalloc=False)
-    _call(tail, v, head, None, None, causal=True, normalize=False, act=3, noalloc=True)  # warm-up
+    plain = _call(tail, v, head, None, None, causal=True, normalize=False, act=3, noalloc=False)
+    want = _call(tail, v, head, None, None, causal=True, normalize=False, act=3, noalloc=True)
+    assert norm_rel_err(to_numpy(want), to_numpy(plain)) <= TOL['bfloat16']
     out = torch.full(tail.shape, float('nan'), dtype=tail.dtype, device='cuda')
     params = ops.build_params(tail, v, head, None, None, out, eps=1e-6, norm_eps=1e-12,
                               causal=True, normalize=False, activation_id=3)
