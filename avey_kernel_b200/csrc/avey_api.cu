@@ -648,8 +648,9 @@ int launch_tc(const AveyFwdParams* p, cudaStream_t stream, const PreSum& ps) {
     if (rc != AVEY_OK) return rc;
   }
   cudaError_t e = cudaSuccess;
-  // 2. The fused kernel, as a programmatic dependent of the pre-pass: it waits
-  //    for the sums only before its P phase.
+  // 2. The fused kernel as a programmatic dependent of the previous launch:
+  //    after the pre-pass it waits for the sums only before its P phase;
+  //    otherwise it waits once its set-up is done, before reading any input.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p->batch * l.geom.n_qtiles));
   cfg.blockDim = dim3(avey::kTcThreads);

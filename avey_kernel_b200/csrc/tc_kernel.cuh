@@ -336,6 +336,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tmem_relinquish();
   }
   __syncthreads();
+  // Without a pre-pass the launch may overlap the previous kernel of the
+  // stream (programmatic dependent launch): the set-up above runs early, and
+  // nothing is read from global memory before that kernel has finished.
+  if (geom.self_sums) griddep_wait();
   // Key validity of this batch row and the last valid position.
   {
     int last = -1;
