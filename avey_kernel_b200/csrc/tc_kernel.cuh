@@ -9,10 +9,12 @@
 //     space of the phase-C ring (unused until phase C). The MMA warp
 //     accumulates the raw Gram block G = Z_q Z_k^T (fp32) in TMEM, two key
 //     tiles per MMA (N = 256), up to 512 keys = all 512 TMEM columns. The L2
-//     normalisation is applied to G in phase B from per-row sums of squares
-//     (4 bytes per row, written by norm_prepass into the workspace, which runs
-//     concurrently through programmatic dependent launch); no normalised copy
-//     of z_tr exists anywhere.
+//     normalisation is applied to G in phase B from per-row sums of squares,
+//     which the compute warps take from the same phase-A stages while the
+//     Gram runs (each stage is released by the MMAs and by them); in the
+//     pre-pass variant (given row sums, or norm_prepass running concurrently
+//     through programmatic dependent launch) they read them from the
+//     workspace instead. No normalised copy of z_tr exists anywhere.
 //  B. P phase. The compute warps read G from TMEM (thread = query row), form
 //     P = G * rinv_i * rinv_j * V[i, j] under the causal / padding masks
 //     (select, so NaN padding cannot leak), accumulate the signed row sum for
