@@ -457,7 +457,9 @@ def run_ours(args, cfg):
                     sets[0]['valid'], causal=cfg['op'] == 'avey', normalize=cfg['op'] != 'avey')
     kernel_name = {1: 'simt_contextualize', 2: 'tc_contextualize (whole step)'}[plan.kernel]
     if plan.kernel == 2 and plan.launches == 3:  # contexts above 512: two tensor-core kernels
-        kernel_name = 'norm_prepass + tc_gram_p + tc_pv (whole step)'
+        # O = P Z on the batched GEMM without a padding mask, on tc_pv with one.
+        mix = 'tc_pv' if sets[0]['valid'] is not None else 'tc_gemm (O = P Z)'
+        kernel_name = f'norm_prepass + tc_gram_p + {mix} (whole step)'
     f32 = cfg.get('dtype') == 'f32'
     if plan.kernel == 2 and f32:  # fp32: the 3xTF32 pair, no pre-pass
         kernel_name = 'tf_gram_p + tf_pv (whole step)'

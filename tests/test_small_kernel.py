@@ -127,3 +127,34 @@ def test_matches_the_3xtf32_pair_and_the_two_phase_kernel(b, n, d):
     torch.cuda.synchronize()
     for y in ys[1:]:
         assert norm_rel_err(to_numpy(ys[0]), to_numpy(y)) <= TOL['float32']
+
+
+@pytest.mark.parametrize('op', ['avey', 'avey_b'])
+def test_rows_that_are_all_padding(op):
+    """A batch row of length 0 beside full and short ones: its CTA pairs have no
+    key block (they still take part in the pair's combine) and its output is
+    zero; the other rows match the oracle."""
+    b, n, d = 3, 136, 64
+    x, v, bias, _ = _inputs(b, n, d, seed=91, signed_tail=op == 'avey')
+    head, tail = x[..., :d], x[..., d:]
+    lengths = torch.tensor([0, n, 37])
+    valid = (torch.arange(n)[None, :] < lengths[:, None]).to(DEV)
+    tail[~valid] = float('nan')
+    causal, normalize = op == 'avey', op == 'avey_b'
+    _small_plan(tail, v if causal else None, head, bias, valid, causal, normalize)
+    y = ops.contextualize(tail, v if causal else None, head, bias, valid, 1e-6, 1e-12, causal,
+                          normalize, _native.ACTIVATION_IDS['silu'])
+    torch.cuda.synchronize()
+    ok = to_numpy(valid.float()) > 0
+    zt = np.nan_to_num(to_numpy(tail))
+    if causal:
+        ref = oracle.avey(zt, to_numpy(v), z_tl=to_numpy(head), bias=to_numpy(bias), valid=ok,
+                          activation='silu')
+    else:
+        ref = oracle.avey_b(zt, z_tl=to_numpy(head), bias=to_numpy(bias), valid=ok,
+                            activation='silu')
+    out = to_numpy(y)
+    assert np.isfinite(out).all()
+    assert (out[0] == 0).all() and (out[~ok] == 0).all()
+    for r in (1, 2):
+        _check(y[r:r + 1], ref[r:r + 1])
