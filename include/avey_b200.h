@@ -51,8 +51,12 @@ typedef enum AveyActivation {
   AVEY_ACT_GELU = 4, /* tanh approximation */
 } AveyActivation;
 
-/* Kernel selection. AUTO picks the tcgen05 kernel whenever the shape, dtype
- * and alignment allow it, else the general CUDA-core kernel. */
+/* Kernel selection. AUTO picks the tcgen05 kernels whenever the shape, dtype
+ * and alignment allow it, except for small fp32 problems (contexts up to
+ * 512, features a multiple of 32 up to 256, a few waves of 8-row query
+ * tiles), which finish sooner on an 8-row CUDA-core kernel (AveyPlan.reason
+ * 6); else the general CUDA-core kernel. AVEY_KERNEL_SIMT forces the general
+ * CUDA-core kernel, AVEY_KERNEL_TCGEN05 the tcgen05 kernels. */
 typedef enum AveyKernel {
   AVEY_KERNEL_AUTO = 0,
   AVEY_KERNEL_SIMT = 1,   /* general CUDA-core kernel: any dtype/stride/shape */
